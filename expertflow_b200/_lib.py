@@ -1,0 +1,116 @@
+"""ctypes binding of libefmoe.so (the C ABI in include/efmoe.h).
+
+The library is loaded from the package directory.  There is no fallback: if
+it is missing, every op raises ``EfmoeUnavailable``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libefmoe.so")
+
+EF_OK = 0
+STATUS = {
+    -1: "EF_ERR_INVALID",
+    -2: "EF_ERR_UNSUPPORTED",
+    -3: "EF_ERR_CUDA",
+    -4: "EF_ERR_WORKSPACE",
+    -5: "EF_ERR_TIMEOUT",
+    -6: "EF_ERR_SLOT_MISS",
+    -7: "EF_ERR_RANGE",
+    -8: "EF_ERR_NOT_READY",
+}
+EF_DT_BF16, EF_DT_F16, EF_DT_F32 = 0, 1, 2
+EF_ROUTER_SOFTMAX, EF_ROUTER_SIGMOID_GROUP = 0, 1
+EF_PATH_AUTO, EF_PATH_GEMV, EF_PATH_GEMM = 0, 1, 2
+
+
+class EfmoeUnavailable(RuntimeError):
+    pass
+
+
+class EfmoeError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+class QWeight(ctypes.Structure):
+    _fields_ = [("w", ctypes.c_void_p), ("scales", ctypes.c_void_p), ("biases", ctypes.c_void_p)]
+
+
+class MoECfg(ctypes.Structure):
+    _fields_ = [
+        ("hidden", ctypes.c_int),
+        ("inter", ctypes.c_int),
+        ("n_experts", ctypes.c_int),
+        ("top_k", ctypes.c_int),
+        ("bits", ctypes.c_int),
+        ("group_size", ctypes.c_int),
+        ("router_mode", ctypes.c_int),
+        ("norm_topk", ctypes.c_int),
+        ("n_group", ctypes.c_int),
+        ("topk_group", ctypes.c_int),
+        ("routed_scaling", ctypes.c_float),
+        ("n_shared", ctypes.c_int),
+        ("shared_inter", ctypes.c_int),
+        ("act_dtype", ctypes.c_int),
+        ("gate_dtype", ctypes.c_int),
+        ("path", ctypes.c_int),
+    ]
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_SZ = ctypes.c_size_t
+_QW = QWeight
+_QWP = ctypes.POINTER(QWeight)
+_CFGP = ctypes.POINTER(MoECfg)
+
+# name -> (restype, argtypes); every function declared in include/efmoe.h
+SIGNATURES = {
+    "ef_version": (ctypes.c_char_p, []),
+    "ef_status_string": (ctypes.c_char_p, [_I]),
+    "ef_last_error_message": (ctypes.c_char_p, []),
+    "ef_get_device_error": (_I, [_P, ctypes.POINTER(_I)]),
+    "ef_moe_workspace_size": (_SZ, [_CFGP, _I]),
+    "ef_moe_forward": (_I, [_CFGP, _P, _I, _P, _P, _QW, _QW, _QW, _QWP, _QWP, _QWP, _P, _P, _P, _P, _SZ, _P]),
+    "ef_router_workspace_size": (_SZ, [_CFGP, _I]),
+    "ef_router_topk": (_I, [_CFGP, _P, _I, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "ef_experts_workspace_size": (_SZ, [_CFGP, _I]),
+    "ef_moe_experts_forward": (_I, [_CFGP, _P, _I, _P, _QW, _QW, _QW, _QWP, _QWP, _QWP, _P, _P, _SZ, _P]),
+    "ef_quantized_matmul_workspace_size": (_SZ, [_I, _I, _I]),
+    "ef_quantized_matmul": (_I, [_P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _P, _P, _SZ, _P]),
+    "ef_dequantize": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _P]),
+    "ef_gather_qmm_workspace_size": (_SZ, [_I, _I, _I, _I, _I]),
+    "ef_gather_qmm": (_I, [_P, _I, _I, _P, _I, _QW, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
+}
+
+_lib = None
+
+
+def lib():
+    """Load libefmoe.so (raises EfmoeUnavailable when it is not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise EfmoeUnavailable(f"{LIB_PATH} is not built (run python -m expertflow_b200.build)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != EF_OK:
+        msg = lib().ef_last_error_message()
+        raise EfmoeError(status, msg.decode() if msg else "")
+
+
+def version() -> str:
+    return lib().ef_version().decode()

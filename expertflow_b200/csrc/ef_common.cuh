@@ -1,0 +1,119 @@
+// ef_common.cuh -- device helpers shared by the sm_100a kernels of libefmoe.
+//
+// Every wait on an mbarrier is bounded: after EF_WAIT_LIMIT polls the waiting
+// thread records an error code in the device error word and returns false, so a
+// lost copy ends the kernel with a status instead of a hang.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "efmoe_internal.h"
+
+#define EF_DEV __device__ __forceinline__
+
+#ifndef EF_WAIT_LIMIT
+#define EF_WAIT_LIMIT (1u << 26)
+#endif
+
+// Device error word (one per process; read and cleared by ef_get_device_error).
+__device__ int g_ef_dev_error = 0;
+
+EF_DEV void ef_set_error(int code) { atomicCAS(&g_ef_dev_error, 0, code); }
+EF_DEV bool ef_error_seen() { return *(volatile int*)&g_ef_dev_error != 0; }
+
+EF_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+// ---------------------------------------------------------------- mbarrier
+EF_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+EF_DEV void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+EF_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+EF_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+EF_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+EF_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; returns false (and records `code`) if the phase never completed
+// or another thread already reported an error.
+EF_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  for (uint32_t i = 0; i < EF_WAIT_LIMIT; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023u) == 1023u && ef_error_seen()) return false;
+  }
+  ef_set_error(code);
+  return false;
+}
+
+// ---------------------------------------------------------------- TMA / bulk copies
+// 2-D tiled tensor load, completion counted on `bar` (bytes).
+EF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int32_t c0, int32_t c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+// 1-D bulk copy global -> shared; dst/src 16-byte aligned, bytes % 16 == 0.
+EF_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+EF_DEV void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------- named barriers
+EF_DEV void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------- bit tricks
+EF_DEV uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {  // (a & b) | c
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+EF_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// mma.sync m16n8k16, fp16 inputs, fp32 accumulate.
+EF_DEV void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+EF_DEV float h16_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+EF_DEV float bf16_to_f32(uint16_t h) { return __uint_as_float(static_cast<uint32_t>(h) << 16); }
+EF_DEV float act_to_f32(uint16_t v, int is_bf16) { return is_bf16 ? bf16_to_f32(v) : h16_to_f32(v); }
+
+// Saturating fp32 -> fp16 (returns bits).
+EF_DEV uint16_t f32_to_h16_sat(float v) {
+  v = fminf(fmaxf(v, -65504.0f), 65504.0f);
+  return __half_as_ushort(__float2half_rn(v));
+}
+
+// Position of column c (within its 8-column block) in the pair-ordered
+// activation layout [c0 c4 c1 c5 c2 c6 c3 c7].
+EF_DEV int pair_pos(int c) { return ((c & 3) << 1) | ((c >> 2) & 1); }

@@ -1,0 +1,7 @@
+// efmoe.cu -- single translation unit of libefmoe.so (the device error word and
+// the kernels are shared without relocatable device code).
+#include "ef_permute.cu"
+#include "ef_router.cu"
+#include "ef_dequant.cu"
+#include "ef_qmv.cu"
+#include "ef_api.cu"

@@ -1,0 +1,64 @@
+// efmoe_internal.h -- structures shared by the host API and the kernels.
+#pragma once
+#include <cuda.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+namespace ef {
+
+// ---- quantised grouped GEMV (decode path) ----
+constexpr int kRowTile = 64;        // weight rows per work item (4 warps x 16 rows)
+constexpr int kTokChunk = 32;       // rows (tokens) per segment: up to 4 n-tiles of 8
+constexpr int kStages = 4;          // TMA pipeline depth
+constexpr int kComputeWarps = 4;
+constexpr int kQmvThreads = (kComputeWarps + 1) * 32;
+constexpr int kActPad = 16;         // bytes of padding per staged activation row
+
+// error codes written to the device error word
+constexpr int kDevErrTimeoutFull = 1001;
+constexpr int kDevErrTimeoutEmpty = 1002;
+constexpr int kDevErrTimeoutScales = 1003;
+constexpr int kDevErrRange = 2001;
+constexpr int kDevErrTimeoutTc = 1004;
+
+// Output of the permutation (all device pointers into the workspace).
+struct PermBufs {
+  int* counts;      // [n_bins]            rows per expert (bin n_experts = shared expert)
+  int* offsets;     // [n_bins + 1]        first sorted row of each expert
+  int* row_src;     // [n_rows]            source row (token) of each sorted row
+  int* inv;         // [n_entries]         sorted row of each routed entry (t*k + j)
+  int* seg_expert;  // [max_segs]
+  int* seg_row0;    // [max_segs]
+  int* seg_nrows;   // [max_segs]
+  int* n_seg;       // [1]
+};
+
+struct QmvParams {
+  CUtensorMap tm_w0;    // routed codes: gate (mode 0) or down (mode 1), 2-D [E*R, K*bits/32]
+  CUtensorMap tm_w1;    // routed codes: up (mode 0)
+  CUtensorMap tm_sw0;   // shared expert codes
+  CUtensorMap tm_sw1;
+  const uint16_t* s0;   // routed scales/biases [E*R, K/64]
+  const uint16_t* b0;
+  const uint16_t* s1;
+  const uint16_t* b1;
+  const uint16_t* ss0;  // shared expert scales/biases [R, K/64]
+  const uint16_t* sb0;
+  const uint16_t* ss1;
+  const uint16_t* sb1;
+  const uint16_t* act;      // pair-ordered fp16 activation rows [*, K]
+  const float* act_sum;     // [*, K/64] group sums of act
+  const int* row_src;       // mode 0: act row of sorted row j; mode 1: nullptr (identity)
+  const int* seg_expert;
+  const int* seg_row0;
+  const int* seg_nrows;
+  const int* n_seg;
+  int K;                    // input dim
+  int R;                    // output rows per expert
+  int n_experts;            // expert id == n_experts selects the shared expert
+  uint16_t* h_out;          // mode 0: fp16 pair-ordered [n_rows, R]
+  float* hsum_out;          // mode 0: [n_rows, R/64]
+  float* y_out;             // mode 1: fp32 [n_rows, R]
+};
+
+}  // namespace ef

@@ -1,0 +1,149 @@
+/*
+ * efmoe.h -- C ABI of libefmoe.so, the B200 (sm_100a) implementation of the
+ * ExpertFlow MoE-layer hot path.
+ *
+ * Conventions
+ *   - Every tensor argument is a DEVICE pointer owned by the caller; sizes are
+ *     plain ints.  No call allocates device memory: scratch space is the
+ *     caller's `workspace` (size from ef_moe_workspace_size).
+ *   - Every compute call is asynchronous on `stream` (a cudaStream_t, passed as
+ *     void*; NULL = legacy default stream) and returns EF_OK or a negative
+ *     EF_ERR_* code.  Argument checks happen on the host before any launch.
+ *   - Quantised weights use the MLX affine layout (uint32-packed codes,
+ *     LSB-first; fp16 scale and bias per 64-column group), stacked per expert:
+ *       w      uint32 [n_experts, out_dim, in_dim * bits / 32]
+ *       scales fp16   [n_experts, out_dim, in_dim / 64]
+ *       biases fp16   [n_experts, out_dim, in_dim / 64]
+ *     dequant(w)[o, i] = scales[o, i/64] * q[o, i] + biases[o, i/64].
+ *   - Routing: indices are bit-exact with the CPU oracle (fp32 logits in a
+ *     fixed lane-interleaved order, top-k by (score desc, index asc)).
+ *   - Handles are not thread-safe; use one per stream.
+ *
+ * Reference interfaces replaced (paths relative to the reference checkout):
+ *   ef_moe_forward        streaming_moe_forward(moe_module, x, expert_cache)  ef_engine.py:598-706
+ *   ef_router_topk        moe_module.gate(x) + argpartition/softmax        ef_engine.py:609-619
+ *   ef_quantized_matmul   mx.quantized_matmul(x, w, s, b, transpose=True)  ef_engine.py:689-694
+ *   ef_dequantize         mx.dequantize(w, s, b, group_size, bits)         ef_cpu_fast.py:70-75
+ *   ef_gather_qmm         QuantizedSwitchLinear.__call__(x, indices)        ef_engine_v4.py:52-64
+ *   ef_moe_experts_forward  per-(row, expert) SwiGLU loop                  ef_engine.py:678-695
+ *   ef_slotpool_*         FrequencyWeightedCache get/put/trim              ef_engine.py:48-104
+ *                         + mmap page-in of misses                        ef_engine.py:650-675
+ */
+#ifndef EFMOE_H
+#define EFMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int ef_status;
+#define EF_OK 0
+#define EF_ERR_INVALID (-1)     /* bad shape, null or misaligned pointer */
+#define EF_ERR_UNSUPPORTED (-2) /* bits / group / dtype / size not supported */
+#define EF_ERR_CUDA (-3)        /* a CUDA runtime call failed */
+#define EF_ERR_WORKSPACE (-4)   /* workspace too small */
+#define EF_ERR_TIMEOUT (-5)     /* a bounded device-side wait ran out */
+#define EF_ERR_SLOT_MISS (-6)   /* expert not resident in the slot pool */
+#define EF_ERR_RANGE (-7)       /* activation outside the fp16 range */
+#define EF_ERR_NOT_READY (-8)   /* no CUDA device / extension not initialised */
+
+enum { EF_DT_BF16 = 0, EF_DT_F16 = 1, EF_DT_F32 = 2 };
+enum { EF_ROUTER_SOFTMAX = 0, EF_ROUTER_SIGMOID_GROUP = 1 };
+enum { EF_PATH_AUTO = 0, EF_PATH_GEMV = 1, EF_PATH_GEMM = 2 };
+
+/* One stack of quantised projections (see layout above). */
+typedef struct {
+  const uint32_t* w;
+  const uint16_t* scales;
+  const uint16_t* biases;
+} ef_qweight;
+
+/* Layer configuration: the attributes the reference reads from an mlx_lm MoE
+ * module (num_experts_per_tok, switch_mlp.*.bits/group_size, shared_experts)
+ * plus the gate's routing parameters. */
+typedef struct {
+  int hidden;         /* H, multiple of 256 */
+  int inter;          /* I (per routed expert), multiple of 256 */
+  int n_experts;      /* E, 1..512 */
+  int top_k;          /* k, 1..16 */
+  int bits;           /* 4 or 8 */
+  int group_size;     /* 64 */
+  int router_mode;    /* EF_ROUTER_* */
+  int norm_topk;      /* softmax: renormalise over k; sigmoid: divide by the sum */
+  int n_group;        /* sigmoid_group: expert groups (1 = no group limit), <= 32 */
+  int topk_group;     /* sigmoid_group: groups kept */
+  float routed_scaling;
+  int n_shared;       /* 0 or 1 shared expert (always-on, weight 1.0) */
+  int shared_inter;   /* I of the shared expert */
+  int act_dtype;      /* EF_DT_BF16 or EF_DT_F16 (x and y) */
+  int gate_dtype;     /* EF_DT_F16 or EF_DT_BF16 (router weight) */
+  int path;           /* EF_PATH_AUTO / GEMV (decode kernels) / GEMM (tcgen05 grouped GEMM) */
+} ef_moe_cfg;
+
+/* ---- library ---------------------------------------------------------- */
+const char* ef_version(void);
+const char* ef_status_string(ef_status s);
+/* Detail of the last error returned on the calling host thread. */
+const char* ef_last_error_message(void);
+/* Reads and clears the device-side error word (set by bounded waits that ran
+ * out, or by an out-of-range activation); synchronises `stream`. */
+ef_status ef_get_device_error(void* stream, int* code);
+
+/* ---- whole layer ------------------------------------------------------ */
+/* Bytes of workspace ef_moe_forward needs for T tokens (256-byte aligned). */
+size_t ef_moe_workspace_size(const ef_moe_cfg* cfg, int T);
+
+/* y[T, H] = sum_k w[t,k] * SwiGLU_{e[t,k]}(x[t]) (+ shared(x[t])), routing by
+ * the gate (gate_w fp16/bf16 [E, H], e_bias fp32 [E] or NULL).  inds_out
+ * [T, k] int32 and wts_out [T, k] fp32 are optional (NULL to skip).
+ * Replaces streaming_moe_forward, ef_engine.py:598-706. */
+ef_status ef_moe_forward(const ef_moe_cfg* cfg, const void* x, int T, const void* gate_w, const float* e_bias,
+                         ef_qweight gate, ef_qweight up, ef_qweight down, const ef_qweight* shared_gate,
+                         const ef_qweight* shared_up, const ef_qweight* shared_down, void* y, int32_t* inds_out,
+                         float* wts_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- router ----------------------------------------------------------- */
+/* inds [T, k] int32 in rank order, weights [T, k] fp32.  Replaces
+ * moe_module.gate(x) + argpartition/take_along_axis/softmax, ef_engine.py:609-619. */
+size_t ef_router_workspace_size(const ef_moe_cfg* cfg, int T);
+ef_status ef_router_topk(const ef_moe_cfg* cfg, const void* x, int T, const void* gate_w, const float* e_bias,
+                         int32_t* inds, float* weights, float* logits_out, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* ---- experts on routed rows --------------------------------------------- */
+/* Rows x[N, H] (act dtype), row_expert[N] in [0, n_experts) (or n_experts for
+ * the shared expert when shared_* is given); y_rows[N, H] fp32 = expert(x row).
+ * The per-(row, expert) SwiGLU of ef_engine.py:678-695 without the weighting;
+ * used by expert-parallel dispatch (rows received from peers). */
+size_t ef_experts_workspace_size(const ef_moe_cfg* cfg, int N);
+ef_status ef_moe_experts_forward(const ef_moe_cfg* cfg, const void* x_rows, int N, const int32_t* row_expert,
+                                 ef_qweight gate, ef_qweight up, ef_qweight down, const ef_qweight* shared_gate,
+                                 const ef_qweight* shared_up, const ef_qweight* shared_down, float* y_rows,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- MLX op equivalents ------------------------------------------------- */
+/* y[M, out] = x[M, in] @ dequant(w)^T  (x, y act dtype).  Replaces
+ * mx.quantized_matmul(x, w, s, b, transpose=True, group_size, bits). */
+size_t ef_quantized_matmul_workspace_size(int M, int out_dim, int in_dim);
+ef_status ef_quantized_matmul(const void* x, int act_dtype, int M, const uint32_t* w, const uint16_t* scales,
+                              const uint16_t* biases, int out_dim, int in_dim, int bits, int group_size, void* y,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[rows, cols] (EF_DT_F32 / F16 / BF16) = dequant(w).  Replaces mx.dequantize. */
+ef_status ef_dequantize(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, int rows, int cols,
+                        int bits, int group_size, void* out, int out_dtype, void* stream);
+
+/* y[T, k, out] = x[t] @ dequant(w[indices[t, j]])^T.  Replaces gather_qmm
+ * (QuantizedSwitchLinear.__call__, ef_engine_v4.py:52-64). */
+size_t ef_gather_qmm_workspace_size(int T, int k, int n_experts, int out_dim, int in_dim);
+ef_status ef_gather_qmm(const void* x, int act_dtype, int T, const int32_t* indices, int k, ef_qweight w,
+                        int n_experts, int out_dim, int in_dim, int bits, int group_size, void* y, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EFMOE_H */

@@ -18,9 +18,10 @@
  *
  * Canonical rules fixed here (the reference's argpartition gives no order or
  * tie guarantee, ef_engine.py:616), shared bit-for-bit with the CUDA kernels:
- *   - router logits: fp32, exact 16x16-bit products, lane-interleaved order:
- *     element i goes to lane (i/8) % 32, each lane sums its elements in
- *     increasing i, then lanes combine by a xor butterfly 16,8,4,2,1.
+ *   - router logits: fp32, exact 16x16-bit products, slot-interleaved order:
+ *     element i belongs to chunk c = i/8 and slot s = c % 128; each slot sums
+ *     its elements in increasing i; slots 32g..32g+31 (g = 0..3) combine by a
+ *     xor butterfly 16,8,4,2,1 into G[g]; logit = (G0 + G1) + (G2 + G3).
  *   - top-k order: (score desc, expert index asc); ties go to the lowest index.
  *   - exp(): Cody-Waite reduction x = n ln2 + r with ln2 split into a 16-bit
  *     head and a tail, degree-7 Taylor polynomial of e^r in Horner form, then
@@ -104,25 +105,30 @@ float efo_sigmoidf(float x) { return 1.0f / (1.0f + efo_expf(-x)); }
 /* router logits, canonical order                                      */
 /* ------------------------------------------------------------------ */
 static float dot_canonical(const uint16_t* x, int x_bf16, const uint16_t* w, int w_bf16, int H) {
-    float lane[32];
-    for (int l = 0; l < 32; ++l) lane[l] = 0.0f;
+    float slot[128];
+    for (int l = 0; l < 128; ++l) slot[l] = 0.0f;
     int nch = H / 8;
     for (int c = 0; c < nch; ++c) {
-        int l = c & 31;
-        float a = lane[l];
+        int l = c & 127;
+        float a = slot[l];
         for (int i = 0; i < 8; ++i) {
             float xv = in2f(x[8 * c + i], x_bf16);
             float wv = in2f(w[8 * c + i], w_bf16);
             a = a + xv * wv; /* product exact in fp32 */
         }
-        lane[l] = a;
+        slot[l] = a;
     }
-    for (int off = 16; off >= 1; off >>= 1) {
-        float nb[32];
-        for (int l = 0; l < 32; ++l) nb[l] = lane[l] + lane[l ^ off];
-        for (int l = 0; l < 32; ++l) lane[l] = nb[l];
+    float G[4];
+    for (int g = 0; g < 4; ++g) {
+        float* lane = slot + 32 * g;
+        for (int off = 16; off >= 1; off >>= 1) {
+            float nb[32];
+            for (int l = 0; l < 32; ++l) nb[l] = lane[l] + lane[l ^ off];
+            for (int l = 0; l < 32; ++l) lane[l] = nb[l];
+        }
+        G[g] = lane[0];
     }
-    return lane[0];
+    return (G[0] + G[1]) + (G[2] + G[3]);
 }
 
 /* logits[T,E] = x[T,H] . wg[E,H]^T ; H % 8 == 0 */

@@ -158,7 +158,7 @@ def _butterfly(acc: np.ndarray) -> np.ndarray:
 
 
 def np_router_logits(x_bits: np.ndarray, x_bf16: bool, w_bits: np.ndarray, w_bf16: bool) -> np.ndarray:
-    """Canonical-order fp32 logits [T, E] (see ef_oracle.c)."""
+    """Canonical-order fp32 logits [T, E] (slot-interleaved, see ef_oracle.c)."""
     xf = bits_to_f32(x_bits, x_bf16)
     wf = bits_to_f32(w_bits, w_bf16)
     T, H = xf.shape
@@ -167,15 +167,16 @@ def np_router_logits(x_bits: np.ndarray, x_bf16: bool, w_bits: np.ndarray, w_bf1
     nch = H // 8
     xc = xf.reshape(T, nch, 8)
     wc = wf.reshape(E, nch, 8)
-    acc = np.zeros((T, E, 32), dtype=np.float32)
-    for r in range((nch + 31) // 32):
-        c0 = r * 32
-        c1 = min(nch, c0 + 32)
+    acc = np.zeros((T, E, 128), dtype=np.float32)
+    for r in range((nch + 127) // 128):
+        c0 = r * 128
+        c1 = min(nch, c0 + 128)
         nl = c1 - c0
         for i in range(8):
             prod = xc[:, None, c0:c1, i] * wc[None, :, c0:c1, i]
             acc[:, :, :nl] = (acc[:, :, :nl] + prod).astype(np.float32)
-    return _butterfly(acc)
+    G = _butterfly(acc.reshape(T, E, 4, 32))
+    return ((G[..., 0] + G[..., 1]).astype(np.float32) + (G[..., 2] + G[..., 3]).astype(np.float32)).astype(np.float32)
 
 
 def _topk_rank(v: np.ndarray, k: int) -> np.ndarray:
@@ -391,6 +392,8 @@ class RouterSpec:
 
 def route(logits, spec: RouterSpec, e_bias=None, use_c=True):
     if spec.mode == "softmax":
+        if e_bias is not None:  # optional per-expert logit bias (fp32 add)
+            logits = (np.asarray(logits, np.float32) + np.asarray(e_bias, np.float32)[None, :]).astype(np.float32)
         f = c_route_softmax if use_c else np_route_softmax
         return f(logits, spec.k, spec.norm_topk)
     f = c_route_sigmoid_group if use_c else np_route_sigmoid_group

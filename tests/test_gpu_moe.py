@@ -1,0 +1,266 @@
+"""GPU parity of the MoE-layer hot path against the CPU oracle and the golden
+fixtures produced by the reference's own code.  All calls go through the C ABI
+(libefmoe.so) via the package's host layer."""
+import glob
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import assert_ffn_close
+from expertflow_b200 import synthetic
+from expertflow_b200.spec import MoESpec
+from expertflow_b200.spec import QWEN3_30B_A3B, DEEPSEEK_V3, DEEPSEEK_V3_PREFILL_8BIT, MIXTRAL_SMALL
+from oracle import oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _built():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from expertflow_b200 import build
+
+    build.build()
+    yield
+    from expertflow_b200 import moe
+
+    assert moe.device_error() == 0, "a kernel reported a device-side error"
+
+
+def _moe():
+    from expertflow_b200 import moe
+
+    return moe
+
+
+def _spec_router(spec):
+    return O.RouterSpec(mode=spec.router, k=spec.top_k, norm_topk=spec.norm_topk, n_group=spec.n_group,
+                        topk_group=spec.topk_group, scaling=spec.routed_scaling)
+
+
+def _x_tensor(bits_np, spec):
+    dt = torch.bfloat16 if spec.act_dtype == "bfloat16" else torch.float16
+    return torch.from_numpy(bits_np.view(np.int16)).cuda().view(dt)
+
+
+def _bits_of(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+# ---------------------------------------------------------------- golden fixtures
+GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "moe_*.npz")))
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p)[:-4] for p in GOLDEN])
+def test_layer_matches_reference_golden(path):
+    moe = _moe()
+    z = np.load(path)
+    spec = MoESpec(**json.loads(str(z["spec"])))
+    layer = synthetic.make_layer_np(spec, int(z["seed"]))
+    assert synthetic.layer_digest(layer) == str(z["digest"])
+    xb = synthetic.make_x_np(spec, int(z["T"]), int(z["x_seed"]))
+    m = moe.MoELayer.from_arrays(spec, layer)
+    x = _x_tensor(xb, spec)
+    T, k = x.shape[0], spec.top_k
+    inds = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    wts = torch.empty((T, k), dtype=torch.float32, device="cuda")
+    y = m(x, inds_out=inds, wts_out=wts)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(inds.cpu().numpy(), z["inds"])
+    np.testing.assert_allclose(wts.cpu().numpy(), z["scores"], rtol=2e-6, atol=1e-7)
+    assert_ffn_close(y.float().cpu().numpy(), z["y"], what=os.path.basename(path))
+    # the drop-in entry point gives the same result
+    y2 = moe.streaming_moe_forward(m, x[None])[0]
+    assert torch.equal(y2, y)
+
+
+# ---------------------------------------------------------------- router bit-exactness
+@pytest.mark.parametrize("spec,T", [(QWEN3_30B_A3B, 1), (QWEN3_30B_A3B, 64), (DEEPSEEK_V3, 1), (DEEPSEEK_V3, 256),
+                                    (DEEPSEEK_V3_PREFILL_8BIT, 4096), (MIXTRAL_SMALL, 3),
+                                    (QWEN3_30B_A3B.with_(norm_topk=False), 33)])
+def test_router_indices_bit_exact(spec, T):
+    moe = _moe()
+    rng = np.random.default_rng(T)
+    gate = rng.normal(0, spec.gate_std, (spec.n_experts, spec.hidden)).astype(np.float16)
+    eb = rng.normal(0, 0.01, spec.n_experts).astype(np.float32) if spec.router == "sigmoid_group" else None
+    xb = synthetic.act_bits_np(rng.standard_normal((T, spec.hidden), dtype=np.float32), spec.act_dtype)
+    g = moe.MoEGate(torch.from_numpy(gate).cuda(), spec.top_k, spec.router, spec.norm_topk, spec.n_group,
+                    spec.topk_group, spec.routed_scaling, None if eb is None else torch.from_numpy(eb).cuda())
+    logits = torch.empty((T, spec.n_experts), dtype=torch.float32, device="cuda")
+    inds, wts = g(_x_tensor(xb, spec), logits_out=logits)
+    lg_ref = O.c_router_logits(xb, spec.act_dtype == "bfloat16", gate.view(np.uint16), False)
+    np.testing.assert_array_equal(logits.cpu().numpy().view(np.uint32), lg_ref.view(np.uint32))
+    i_ref, w_ref = O.route(lg_ref, _spec_router(spec), eb)
+    np.testing.assert_array_equal(inds.cpu().numpy(), i_ref)
+    np.testing.assert_array_equal(wts.cpu().numpy().view(np.uint32), w_ref.view(np.uint32))
+
+
+def test_router_ties_and_masking():
+    moe = _moe()
+    E, H = 64, 256
+    gate = np.zeros((E, H), np.float16)
+    gate[[3, 5, 9], 0] = 1.0  # three-way tie
+    x = np.zeros((2, H), np.float32)
+    x[:, 0] = 1.0
+    xb = synthetic.act_bits_np(x, "bfloat16")
+    g = moe.MoEGate(torch.from_numpy(gate).cuda(), 2)
+    inds, wts = g(_x_tensor(xb, QWEN3_30B_A3B))
+    assert inds.cpu().tolist() == [[3, 5], [3, 5]]
+    # all tied -> lowest indices; sigmoid groups tied -> lowest groups
+    g2 = moe.MoEGate(torch.zeros((E, H), dtype=torch.float16, device="cuda"), 4, "sigmoid_group", True, 8, 2, 2.5,
+                     torch.zeros(E, dtype=torch.float32, device="cuda"))
+    inds, wts = g2(_x_tensor(xb, QWEN3_30B_A3B))
+    assert inds.cpu().tolist() == [[0, 1, 2, 3]] * 2
+    np.testing.assert_allclose(wts.cpu().numpy(), 2.5 / 4)
+
+
+# ---------------------------------------------------------------- full-size layers
+def _torch_layer(spec, seed=0):
+    return synthetic.make_layer_torch(spec, seed)
+
+
+def _to_np_qmat(m):
+    w, s, b = m
+    return (w.cpu().numpy().view(np.uint32), s.cpu().numpy(), b.cpu().numpy())
+
+
+def _oracle_sampled(spec, layer_t, xb, inds, wts, tokens):
+    """Oracle FFN output for a subset of tokens (independent per token)."""
+    sub_inds = inds[tokens]
+    needed = sorted(set(sub_inds.reshape(-1).tolist()))
+    remap = {e: i for i, e in enumerate(needed)}
+    sel = torch.tensor(needed, dtype=torch.long, device="cuda")
+
+    def take(m):
+        return tuple(a.index_select(0, sel) for a in m)
+
+    g, u, d = (_to_np_qmat(take(layer_t[n])) for n in ("gate", "up", "down"))
+    sh = None
+    if layer_t["shared"] is not None:
+        sh = tuple(tuple(a.cpu().numpy().view(np.uint32) if a.dtype == torch.int32 else a.cpu().numpy() for a in m)
+                   for m in layer_t["shared"])
+    ri = np.vectorize(remap.get)(sub_inds).astype(np.int32)
+    return O.c_moe_ffn(xb[tokens], spec.act_dtype == "bfloat16", ri, wts[tokens], g, u, d, spec.bits,
+                       spec.group_size, sh)
+
+
+@pytest.mark.parametrize("spec,T", [(QWEN3_30B_A3B, 1), (QWEN3_30B_A3B, 8), (QWEN3_30B_A3B, 32),
+                                    (QWEN3_30B_A3B, 64), (DEEPSEEK_V3, 1), (DEEPSEEK_V3, 64),
+                                    (DEEPSEEK_V3, 256), (MIXTRAL_SMALL, 1)])
+def test_full_size_layer_sampled_parity(spec, T):
+    moe = _moe()
+    layer = _torch_layer(spec, seed=11)
+    m = moe.MoELayer.from_arrays(spec, layer)
+    x = synthetic.make_x_torch(spec, T, seed=5)
+    inds = torch.empty((T, spec.top_k), dtype=torch.int32, device="cuda")
+    wts = torch.empty((T, spec.top_k), dtype=torch.float32, device="cuda")
+    y = m(x, inds_out=inds, wts_out=wts)
+    torch.cuda.synchronize()
+    xb = _bits_of(x)
+    gate = layer["gate_w"].cpu().numpy()
+    eb = layer["e_bias"].cpu().numpy() if layer["e_bias"] is not None else None
+    lg = O.c_router_logits(xb, spec.act_dtype == "bfloat16", gate.view(np.uint16), False)
+    i_ref, w_ref = O.route(lg, _spec_router(spec), eb)
+    np.testing.assert_array_equal(inds.cpu().numpy(), i_ref)
+    np.testing.assert_array_equal(wts.cpu().numpy().view(np.uint32), w_ref.view(np.uint32))
+    rng = np.random.default_rng(T)
+    tokens = np.sort(rng.choice(T, size=min(T, 6), replace=False))
+    y_ref = _oracle_sampled(spec, layer, xb, i_ref, w_ref, tokens)
+    assert_ffn_close(y.float().cpu().numpy()[tokens], y_ref, what=f"{spec.hidden}/{T}")
+
+
+def test_layer_deterministic_and_repeatable():
+    moe = _moe()
+    spec = QWEN3_30B_A3B
+    m = moe.MoELayer.from_arrays(spec, _torch_layer(spec, 3))
+    x = synthetic.make_x_torch(spec, 40, seed=9)
+    a = m(x)
+    b = m(x)
+    assert torch.equal(a, b)
+    # a token's output does not depend on the other tokens in the batch
+    c = m(x[7:8].contiguous())
+    assert torch.equal(a[7:8], c)
+
+
+# ---------------------------------------------------------------- MLX op equivalents
+@pytest.mark.parametrize("bits", [4, 8])
+def test_dequantize_bit_exact(bits):
+    moe = _moe()
+    spec = MoESpec(hidden=512, n_experts=2, top_k=1, inter=256, bits=bits)
+    layer = synthetic.make_layer_np(spec, 2)
+    w, s, b = (a[1] for a in layer["gate"])
+    got = moe.dequantize(torch.from_numpy(w.view(np.int32)).cuda(), torch.from_numpy(s).cuda(),
+                         torch.from_numpy(b).cuda(), 64, bits)
+    ref = O.c_dequantize(w, s, b, bits, 64)
+    np.testing.assert_array_equal(got.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    got16 = moe.dequantize(torch.from_numpy(w.view(np.int32)).cuda(), torch.from_numpy(s).cuda(),
+                           torch.from_numpy(b).cuda(), 64, bits, torch.float16)
+    np.testing.assert_array_equal(got16.cpu().numpy(), ref.astype(np.float16))
+
+
+@pytest.mark.parametrize("bits,M", [(4, 1), (4, 5), (8, 3), (4, 70)])
+def test_quantized_matmul(bits, M):
+    moe = _moe()
+    spec = MoESpec(hidden=1024, n_experts=1, top_k=1, inter=512, bits=bits)
+    layer = synthetic.make_layer_np(spec, 4)
+    w, s, b = (a[0] for a in layer["gate"])  # [512, 1024]
+    xb = synthetic.make_x_np(spec, M, 8)
+    x = _x_tensor(xb, spec)
+    y = moe.quantized_matmul(x, torch.from_numpy(w.view(np.int32)).cuda(), torch.from_numpy(s).cuda(),
+                             torch.from_numpy(b).cuda(), True, 64, bits)
+    ref = O.bits_to_f32(xb, True).astype(np.float64) @ O.np_dequantize(w, s, b, bits, 64, np.float64).T
+    assert_ffn_close(y.float().cpu().numpy(), ref, max_abs=2e-2, rel=4e-3, what="qmm (bf16 output)")
+
+
+def test_gather_qmm_contract():
+    moe = _moe()
+    spec = MoESpec(hidden=512, n_experts=6, top_k=2, inter=256, bits=4)
+    layer = synthetic.make_layer_np(spec, 6)
+    w, s, b = layer["up"]
+    lin = moe.QuantizedSwitchLinear(torch.from_numpy(w.view(np.int32)).cuda(), torch.from_numpy(s).cuda(),
+                                    torch.from_numpy(b).cuda(), 64, 4)
+    xb = synthetic.make_x_np(spec, 6, 3)
+    x = _x_tensor(xb, spec).reshape(2, 3, 1, 1, 512)
+    idx = torch.tensor([[[0, 5], [2, 2], [1, 3]], [[4, 0], [5, 5], [3, 1]]], dtype=torch.int32, device="cuda")
+    y = lin(x, idx)
+    assert tuple(y.shape) == (2, 3, 2, 1, 256)
+    xf = O.bits_to_f32(xb, True).astype(np.float64)
+    ii = idx.cpu().numpy().reshape(6, 2)
+    for t in range(6):
+        for j in range(2):
+            ref = xf[t] @ O.np_dequantize(w[ii[t, j]], s[ii[t, j]], b[ii[t, j]], 4, 64, np.float64).T
+            assert_ffn_close(y.reshape(6, 2, 256)[t, j].float().cpu().numpy(), ref, max_abs=2e-2, rel=4e-3)
+
+
+def test_experts_forward_rows():
+    moe = _moe()
+    spec = MoESpec(hidden=512, n_experts=8, top_k=1, inter=256, bits=4)
+    layer = synthetic.make_layer_np(spec, 12)
+    m = moe.MoELayer.from_arrays(spec, layer)
+    xb = synthetic.make_x_np(spec, 37, 1)
+    ids = np.random.default_rng(0).integers(0, 8, 37).astype(np.int32)
+    y = moe.experts_forward(m.switch_mlp, _x_tensor(xb, spec), torch.from_numpy(ids).cuda())
+    ref = O.c_moe_ffn(xb, True, ids[:, None], np.ones((37, 1), np.float32), layer["gate"], layer["up"],
+                      layer["down"], 4, 64, None)
+    assert_ffn_close(y.cpu().numpy(), ref, what="experts_forward")
+
+
+def test_empty_and_single_token_edges():
+    moe = _moe()
+    spec = QWEN3_30B_A3B
+    m = moe.MoELayer.from_arrays(spec, _torch_layer(spec, 1))
+    x = synthetic.make_x_torch(spec, 0)
+    assert m(x).shape == (0, spec.hidden)
+    # every token routed to the same experts: a full 32-row segment plus a ragged one
+    gate = m.gate.weight.clone()
+    m.gate.weight = torch.zeros_like(gate)
+    x = synthetic.make_x_torch(spec, 45, seed=2)
+    inds = torch.empty((45, spec.top_k), dtype=torch.int32, device="cuda")
+    y = m(x, inds_out=inds)
+    assert (inds.cpu().numpy() == np.arange(spec.top_k)[None]).all()
+    m.gate.weight = gate
+    assert torch.isfinite(y.float()).all()
