@@ -59,6 +59,7 @@ class MoECfg(ctypes.Structure):
         ("act_dtype", ctypes.c_int),
         ("gate_dtype", ctypes.c_int),
         ("path", ctypes.c_int),
+        ("out_f32", ctypes.c_int),
     ]
 
 
@@ -75,6 +76,8 @@ SIGNATURES = {
     "ef_status_string": (ctypes.c_char_p, [_I]),
     "ef_last_error_message": (ctypes.c_char_p, []),
     "ef_get_device_error": (_I, [_P, ctypes.POINTER(_I)]),
+    "ef_trace_enable": (_I, [_I]),
+    "ef_trace_read": (_I, [_P, _I]),
     "ef_moe_workspace_size": (_SZ, [_CFGP, _I]),
     "ef_moe_forward": (_I, [_CFGP, _P, _I, _P, _P, _QW, _QW, _QW, _QWP, _QWP, _QWP, _P, _P, _P, _P, _SZ, _P]),
     "ef_router_workspace_size": (_SZ, [_CFGP, _I]),
@@ -114,3 +117,18 @@ def check(status: int) -> None:
 
 def version() -> str:
     return lib().ef_version().decode()
+
+
+class TraceRec(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("ms", ctypes.c_float)]
+
+
+def trace_enable(on: bool) -> None:
+    lib().ef_trace_enable(int(on))
+
+
+def trace_read(max_recs: int = 1 << 16) -> list:
+    """[(kernel name, milliseconds)] for every launch since the last read."""
+    buf = (TraceRec * max_recs)()
+    n = lib().ef_trace_read(ctypes.cast(buf, ctypes.c_void_p), max_recs)
+    return [(buf[i].name.decode(), float(buf[i].ms)) for i in range(n)]

@@ -9,6 +9,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/efmoe.h"
 #include "ef_common.cuh"
@@ -47,6 +48,13 @@ ef_status fail(ef_status s, const char* fmt, ...) {
   return s;
 }
 
+#define EF_LAUNCH(name, call)                                                               \
+  do {                                                                                      \
+    TraceScope _ts(st, name);                                                               \
+    cudaError_t _e = (call);                                                                \
+    if (_e != cudaSuccess) return fail(EF_ERR_CUDA, "%s: %s", name, cudaGetErrorString(_e)); \
+  } while (0)
+
 #define EF_CUDA(call)                                                                         \
   do {                                                                                        \
     cudaError_t _e = (call);                                                                  \
@@ -54,6 +62,44 @@ ef_status fail(ef_status s, const char* fmt, ...) {
   } while (0)
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- tracing: CUDA events around each launch (off by default)
+struct TraceRec {
+  const char* name;
+  cudaEvent_t a, b;
+};
+std::mutex g_trace_mu;
+bool g_trace_on = false;
+std::vector<TraceRec> g_trace;
+std::vector<cudaEvent_t> g_event_pool;
+
+cudaEvent_t trace_event() {
+  if (!g_event_pool.empty()) {
+    cudaEvent_t e = g_event_pool.back();
+    g_event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+struct TraceScope {
+  cudaStream_t st;
+  TraceRec rec{nullptr, nullptr, nullptr};
+  TraceScope(cudaStream_t s, const char* name) : st(s) {
+    if (!g_trace_on) return;
+    std::lock_guard<std::mutex> lk(g_trace_mu);
+    rec = {name, trace_event(), trace_event()};
+    cudaEventRecord(rec.a, st);
+  }
+  ~TraceScope() {
+    if (!rec.name) return;
+    cudaEventRecord(rec.b, st);
+    std::lock_guard<std::mutex> lk(g_trace_mu);
+    g_trace.push_back(rec);
+  }
+};
 
 // ---- tensor-map encoder from the driver (no link-time libcuda dependency)
 typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -134,9 +180,9 @@ void carve_ffn(Carver& c, int n_ent, int n_rows_x, int n_bins, int n_rows, int H
   f.pb.seg_nrows = c.take<int>(max_segs);
   f.pb.n_seg = c.take<int>(1);
   f.x16 = c.take<uint16_t>((size_t)n_rows_x * H);
-  f.xsum = c.take<float>((size_t)n_rows_x * (H / 64));
+  f.xsum = c.take<float>((size_t)n_rows_x * sum_ld(H));
   f.h16 = c.take<uint16_t>((size_t)n_rows * I);
-  f.hsum = c.take<float>((size_t)n_rows * (I / 64));
+  f.hsum = c.take<float>((size_t)n_rows * sum_ld(I));
   f.yrows = c.take<float>((size_t)n_rows * H);
 }
 
@@ -144,8 +190,8 @@ ef_status check_cfg(const ef_moe_cfg* c) {
   if (!c) return fail(EF_ERR_INVALID, "cfg is NULL");
   if (c->bits != 4 && c->bits != 8) return fail(EF_ERR_UNSUPPORTED, "bits must be 4 or 8 (got %d)", c->bits);
   if (c->group_size != 64) return fail(EF_ERR_UNSUPPORTED, "group_size must be 64 (got %d)", c->group_size);
-  if (c->hidden <= 0 || c->hidden % 256) return fail(EF_ERR_UNSUPPORTED, "hidden must be a positive multiple of 256");
-  if (c->inter <= 0 || c->inter % 256) return fail(EF_ERR_UNSUPPORTED, "inter must be a positive multiple of 256");
+  if (c->hidden <= 0 || c->hidden % 64) return fail(EF_ERR_UNSUPPORTED, "hidden must be a positive multiple of 64");
+  if (c->inter <= 0 || c->inter % 64) return fail(EF_ERR_UNSUPPORTED, "inter must be a positive multiple of 64");
   if (c->n_experts < 1 || c->n_experts > 512) return fail(EF_ERR_UNSUPPORTED, "n_experts must be in 1..512");
   if (c->top_k < 1 || c->top_k > 16 || c->top_k > c->n_experts)
     return fail(EF_ERR_UNSUPPORTED, "top_k must be in 1..min(16, n_experts)");
@@ -203,7 +249,7 @@ ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, const int* row_src_
   p0.seg_expert = f.pb.seg_expert; p0.seg_row0 = f.pb.seg_row0; p0.seg_nrows = f.pb.seg_nrows; p0.n_seg = f.pb.n_seg;
   p0.K = H; p0.R = I; p0.n_experts = E;
   p0.h_out = f.h16; p0.hsum_out = f.hsum; p0.y_out = nullptr;
-  EF_CUDA(launch_qmv(bits, 0, p0, nsm, st));
+  EF_LAUNCH("qmv_gate_up", launch_qmv(bits, 0, p0, nsm, st));
   // mode 1: K = I, R = H
   QmvParams p1 = make_params_common();
   if ((s = encode_codes_map(&p1.tm_w0, down.w, (long long)E * H, I * bits / 32))) return s;
@@ -219,7 +265,7 @@ ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, const int* row_src_
   p1.seg_expert = f.pb.seg_expert; p1.seg_row0 = f.pb.seg_row0; p1.seg_nrows = f.pb.seg_nrows; p1.n_seg = f.pb.n_seg;
   p1.K = I; p1.R = H; p1.n_experts = E;
   p1.y_out = f.yrows;
-  EF_CUDA(launch_qmv(bits, 1, p1, nsm, st));
+  EF_LAUNCH("qmv_down", launch_qmv(bits, 1, p1, nsm, st));
   return EF_OK;
 }
 
@@ -251,6 +297,27 @@ const char* ef_status_string(ef_status s) {
 }
 
 const char* ef_last_error_message(void) { return g_last_msg.c_str(); }
+
+ef_status ef_trace_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_trace_mu);
+  g_trace_on = on != 0;
+  return EF_OK;
+}
+
+int ef_trace_read(ef_trace_rec* recs, int max_recs) {
+  std::lock_guard<std::mutex> lk(g_trace_mu);
+  int n = 0;
+  for (const TraceRec& r : g_trace) {
+    float ms = -1.0f;
+    if (cudaEventSynchronize(r.b) == cudaSuccess) cudaEventElapsedTime(&ms, r.a, r.b);
+    if (recs && n < max_recs) recs[n] = ef_trace_rec{r.name, ms};
+    ++n;
+    g_event_pool.push_back(r.a);
+    g_event_pool.push_back(r.b);
+  }
+  g_trace.clear();
+  return recs ? (n < max_recs ? n : max_recs) : n;
+}
 
 ef_status ef_get_device_error(void* stream, int* code) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -288,10 +355,10 @@ ef_status ef_router_topk(const ef_moe_cfg* cfg, const void* x, int T, const void
     Carver c{static_cast<uint8_t*>(workspace)};
     logits = c.take<float>((size_t)T * cfg->n_experts);
   }
-  EF_CUDA(launch_router_logits(static_cast<const uint16_t*>(x), cfg->act_dtype == EF_DT_BF16,
+  EF_LAUNCH("router_logits", launch_router_logits(static_cast<const uint16_t*>(x), cfg->act_dtype == EF_DT_BF16,
                                static_cast<const uint16_t*>(gate_w), cfg->gate_dtype == EF_DT_BF16, T, cfg->n_experts,
                                cfg->hidden, logits, st));
-  EF_CUDA(launch_router_select(logits, e_bias, T, cfg->n_experts, cfg->top_k, cfg->router_mode, cfg->norm_topk,
+  EF_LAUNCH("router_select", launch_router_select(logits, e_bias, T, cfg->n_experts, cfg->top_k, cfg->router_mode, cfg->norm_topk,
                                cfg->router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg->n_group : 1, cfg->topk_group,
                                cfg->router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg->routed_scaling : 1.0f, inds,
                                weights, st));
@@ -349,21 +416,21 @@ ef_status ef_moe_forward(const ef_moe_cfg* cfg, const void* x, int T, const void
   if (wts_out) wts = wts_out;
   const int H = cfg->hidden, E = cfg->n_experts, k = cfg->top_k;
   const bool bf = cfg->act_dtype == EF_DT_BF16;
-  EF_CUDA(launch_router_logits(static_cast<const uint16_t*>(x), bf, static_cast<const uint16_t*>(gate_w),
+  EF_LAUNCH("router_logits", launch_router_logits(static_cast<const uint16_t*>(x), bf, static_cast<const uint16_t*>(gate_w),
                                cfg->gate_dtype == EF_DT_BF16, T, E, H, logits, st));
-  EF_CUDA(launch_router_select(logits, e_bias, T, E, k, cfg->router_mode, cfg->norm_topk,
+  EF_LAUNCH("router_select", launch_router_select(logits, e_bias, T, E, k, cfg->router_mode, cfg->norm_topk,
                                cfg->router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg->n_group : 1, cfg->topk_group,
                                cfg->router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg->routed_scaling : 1.0f, inds, wts,
                                st));
   const int n_sh = cfg->n_shared ? T : 0;
-  EF_CUDA(launch_permute(inds, T * k, k, E, n_sh, kTokChunk, f.pb, st));
-  EF_CUDA(launch_prep_act(static_cast<const uint16_t*>(x), bf, T, H, f.x16, f.xsum, st));
+  EF_LAUNCH("permute", launch_permute(inds, T * k, k, E, n_sh, kTokChunk, f.pb, st));
+  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), bf, T, H, f.x16, f.xsum, st));
   if ((s = run_experts(cfg, f, f.pb.row_src, gate, up, down, cfg->n_shared ? sg : nullptr,
                        cfg->n_shared ? su : nullptr, cfg->n_shared ? sd : nullptr, st)))
     return s;
   // shared rows start at offsets[E] == T*k
-  EF_CUDA(launch_combine(f.yrows, f.pb.inv, wts, T, k, H, cfg->n_shared ? T * k : -1, y,
-                         bf ? EF_DT_BF16 : EF_DT_F16, st));
+  EF_LAUNCH("combine", launch_combine(f.yrows, f.pb.inv, wts, T, k, H, cfg->n_shared ? T * k : -1, y,
+                         cfg->out_f32 ? EF_DT_F32 : (bf ? EF_DT_BF16 : EF_DT_F16), st));
   return EF_OK;
 }
 
@@ -393,10 +460,10 @@ ef_status ef_moe_experts_forward(const ef_moe_cfg* cfg, const void* x_rows, int 
   FfnBufs f;
   carve_ffn(c, N, N, cfg->n_experts + 1, N, cfg->hidden, cfg->inter, f);
   const bool bf = cfg->act_dtype == EF_DT_BF16;
-  EF_CUDA(launch_permute(row_expert, N, 1, cfg->n_experts, 0, kTokChunk, f.pb, st));
-  EF_CUDA(launch_prep_act(static_cast<const uint16_t*>(x_rows), bf, N, cfg->hidden, f.x16, f.xsum, st));
+  EF_LAUNCH("permute", launch_permute(row_expert, N, 1, cfg->n_experts, 0, kTokChunk, f.pb, st));
+  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x_rows), bf, N, cfg->hidden, f.x16, f.xsum, st));
   if ((s = run_experts(cfg, f, f.pb.row_src, gate, up, down, nullptr, nullptr, nullptr, st))) return s;
-  EF_CUDA(launch_combine(f.yrows, f.pb.inv, nullptr, N, 1, cfg->hidden, -1, y_rows, EF_DT_F32, st));
+  EF_LAUNCH("combine", launch_combine(f.yrows, f.pb.inv, nullptr, N, 1, cfg->hidden, -1, y_rows, EF_DT_F32, st));
   return EF_OK;
 }
 
@@ -413,7 +480,7 @@ static size_t qmm_ws(int M, int k, int n_exp, int out_dim, int in_dim, Carver& c
   f.pb.seg_nrows = c.take<int>(max_segs);
   f.pb.n_seg = c.take<int>(1);
   f.x16 = c.take<uint16_t>((size_t)n_rows_x * in_dim);
-  f.xsum = c.take<float>((size_t)n_rows_x * (in_dim / 64));
+  f.xsum = c.take<float>((size_t)n_rows_x * sum_ld(in_dim));
   f.yrows = c.take<float>((size_t)n_ent * out_dim);
   f.ids = c.take<int>((size_t)M);  // expert ids (all zero) for the single-matrix case
   return c.off;
@@ -422,7 +489,7 @@ static size_t qmm_ws(int M, int k, int n_exp, int out_dim, int in_dim, Carver& c
 static ef_status check_qmm(int out_dim, int in_dim, int bits, int group) {
   if (bits != 4 && bits != 8) return fail(EF_ERR_UNSUPPORTED, "bits must be 4 or 8");
   if (group != 64) return fail(EF_ERR_UNSUPPORTED, "group_size must be 64");
-  if (in_dim <= 0 || in_dim % 256) return fail(EF_ERR_UNSUPPORTED, "in_dim must be a positive multiple of 256");
+  if (in_dim <= 0 || in_dim % 64) return fail(EF_ERR_UNSUPPORTED, "in_dim must be a positive multiple of 64");
   if (out_dim <= 0 || out_dim % 64) return fail(EF_ERR_UNSUPPORTED, "out_dim must be a positive multiple of 64");
   if (qmv_smem_required(bits, 1, in_dim) > 227 * 1024) return fail(EF_ERR_UNSUPPORTED, "in_dim too large");
   return EF_OK;
@@ -439,7 +506,7 @@ static ef_status run_single_matrix(const ef_qweight& w, int n_exp, int out_dim, 
   p.seg_expert = f.pb.seg_expert; p.seg_row0 = f.pb.seg_row0; p.seg_nrows = f.pb.seg_nrows; p.n_seg = f.pb.n_seg;
   p.K = in_dim; p.R = out_dim; p.n_experts = n_exp;
   p.y_out = f.yrows;
-  EF_CUDA(launch_qmv(bits, 1, p, sm_count(), st));
+  EF_LAUNCH("qmv_down", launch_qmv(bits, 1, p, sm_count(), st));
   return EF_OK;
 }
 
@@ -469,10 +536,10 @@ ef_status ef_quantized_matmul(const void* x, int act_dtype, int M, const uint32_
   qmm_ws(M, 1, 1, out_dim, in_dim, c, f, M);
   int* ids = f.ids;
   EF_CUDA(cudaMemsetAsync(ids, 0, sizeof(int) * (size_t)M, st));
-  EF_CUDA(launch_permute(ids, M, 1, 1, 0, kTokChunk, f.pb, st));
-  EF_CUDA(launch_prep_act(static_cast<const uint16_t*>(x), act_dtype == EF_DT_BF16, M, in_dim, f.x16, f.xsum, st));
+  EF_LAUNCH("permute", launch_permute(ids, M, 1, 1, 0, kTokChunk, f.pb, st));
+  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), act_dtype == EF_DT_BF16, M, in_dim, f.x16, f.xsum, st));
   if ((s = run_single_matrix(q, 1, out_dim, in_dim, bits, f, f.pb.row_src, st))) return s;
-  EF_CUDA(launch_combine(f.yrows, f.pb.inv, nullptr, M, 1, out_dim, -1, y, act_dtype, st));
+  EF_LAUNCH("combine", launch_combine(f.yrows, f.pb.inv, nullptr, M, 1, out_dim, -1, y, act_dtype, st));
   return EF_OK;
 }
 
@@ -499,10 +566,10 @@ ef_status ef_gather_qmm(const void* x, int act_dtype, int T, const int32_t* indi
   Carver c{static_cast<uint8_t*>(workspace)};
   FfnBufs f;
   qmm_ws(T, k, n_experts, out_dim, in_dim, c, f, T);
-  EF_CUDA(launch_permute(indices, T * k, k, n_experts, 0, kTokChunk, f.pb, st));
-  EF_CUDA(launch_prep_act(static_cast<const uint16_t*>(x), act_dtype == EF_DT_BF16, T, in_dim, f.x16, f.xsum, st));
+  EF_LAUNCH("permute", launch_permute(indices, T * k, k, n_experts, 0, kTokChunk, f.pb, st));
+  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), act_dtype == EF_DT_BF16, T, in_dim, f.x16, f.xsum, st));
   if ((s = run_single_matrix(w, n_experts, out_dim, in_dim, bits, f, f.pb.row_src, st))) return s;
-  EF_CUDA(launch_combine(f.yrows, f.pb.inv, nullptr, T * k, 1, out_dim, -1, y, act_dtype, st));
+  EF_LAUNCH("combine", launch_combine(f.yrows, f.pb.inv, nullptr, T * k, 1, out_dim, -1, y, act_dtype, st));
   return EF_OK;
 }
 
@@ -514,7 +581,8 @@ ef_status ef_dequantize(const uint32_t* w, const uint16_t* scales, const uint16_
   if (out_dtype < EF_DT_BF16 || out_dtype > EF_DT_F32) return fail(EF_ERR_UNSUPPORTED, "out_dtype");
   if (rows == 0 || cols == 0) return EF_OK;
   if (!w || !scales || !biases || !out) return fail(EF_ERR_INVALID, "null pointer");
-  EF_CUDA(launch_dequantize(w, scales, biases, rows, cols, bits, out, out_dtype, static_cast<cudaStream_t>(stream)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  EF_LAUNCH("dequantize", launch_dequantize(w, scales, biases, rows, cols, bits, out, out_dtype, st));
   return EF_OK;
 }
 

@@ -174,7 +174,11 @@ __global__ void prep_act_kernel(const uint16_t* __restrict__ act, int is_bf16, i
   s += __shfl_xor_sync(0xffffffffu, s, 1);
   s += __shfl_xor_sync(0xffffffffu, s, 2);
   s += __shfl_xor_sync(0xffffffffu, s, 4);
-  if (valid && (gid & 7) == 0) sums[gid >> 3] = s;
+  if (valid && (gid & 7) == 0) {
+    const long long row = gid / nblk;
+    const int grp = (int)((gid - row * nblk) >> 3);
+    sums[row * sum_ld(K) + grp] = s;
+  }
 }
 
 // ---------------------------------------------------------------- combine

@@ -50,7 +50,7 @@ __host__ __device__ inline size_t qmv_smem_bytes(int K) {
   size_t b = 1024;  // alignment slack
   b += (size_t)kStages * S::STAGE_BYTES;
   b += (size_t)S::NMAT * 2 * kRowTile * ng * 2;  // scales + biases
-  b += (size_t)kTokChunk * ng * 4;              // activation group sums
+  b += (size_t)kTokChunk * sum_ld(K) * 4;       // activation group sums
   b += (size_t)kTokChunk * kRowTile * 2;         // h staging (mode 0)
   b += 128;                                      // barriers
   return b;
@@ -88,7 +88,8 @@ EF_DEV bool qmv_consume(const QmvParams& p, const WorkItem& it, uint8_t* stage_b
   const int lane = threadIdx.x & 31, cw = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int ng = p.K / 64;
-  const int nstages = p.K / S::KT;
+  const int xs_ld = sum_ld(p.K);
+  const int nstages = (p.K + S::KT - 1) / S::KT;
   const int rA = cw * 16 + g, rB = rA + 8;
   float y[S::NMAT][NT][4];
 #pragma unroll
@@ -104,8 +105,10 @@ EF_DEV bool qmv_consume(const QmvParams& p, const WorkItem& it, uint8_t* stage_b
     if (!mbar_wait(&full[slot], parity, kDevErrTimeoutFull)) return false;
     const uint8_t* codes = stage_base + (size_t)slot * S::STAGE_BYTES;
     const uint8_t* act = codes + S::CODE_BYTES;
+    const int gvalid = min(S::GPS, ng - st * S::GPS);  // last stage may be partial
 #pragma unroll
     for (int G = 0; G < S::GPS; ++G) {
+      if (G >= gvalid) break;
       const int Gabs = st * S::GPS + G;
       // ---- B operands (activation rows nt*8 + g)
       uint4 blk0[NT], blk1[NT];
@@ -163,7 +166,7 @@ EF_DEV bool qmv_consume(const QmvParams& p, const WorkItem& it, uint8_t* stage_b
         const float bA = h16_to_f32(bm[rA * ng + Gabs]) - sA, bB = h16_to_f32(bm[rB * ng + Gabs]) - sB;
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
-          const float x0 = s_xs[(n * 8 + 2 * t) * ng + Gabs], x1 = s_xs[(n * 8 + 2 * t + 1) * ng + Gabs];
+          const float x0 = s_xs[(n * 8 + 2 * t) * xs_ld + Gabs], x1 = s_xs[(n * 8 + 2 * t + 1) * xs_ld + Gabs];
           y[m][n][0] = fmaf(sA, D[n][0], fmaf(bA, x0, y[m][n][0]));
           y[m][n][1] = fmaf(sA, D[n][1], fmaf(bA, x1, y[m][n][1]));
           y[m][n][2] = fmaf(sB, D[n][2], fmaf(bB, x0, y[m][n][2]));
@@ -204,7 +207,7 @@ EF_DEV bool qmv_consume(const QmvParams& p, const WorkItem& it, uint8_t* stage_b
       const int tok = threadIdx.x;
       float s = 0.0f;
       for (int c = 0; c < kRowTile; ++c) s += h16_to_f32(s_h[tok * kRowTile + c]);
-      p.hsum_out[(size_t)(it.row0_seg + tok) * (R / 64) + it.rt] = s;
+      p.hsum_out[(size_t)(it.row0_seg + tok) * sum_ld(R) + it.rt] = s;
     }
     // staging buffer free again before the next item writes it
     __syncwarp();
@@ -232,8 +235,9 @@ __global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_consta
   const int ng = p.K / 64;
   uint8_t* stage_base = smem;
   uint16_t* s_sb = reinterpret_cast<uint16_t*>(stage_base + (size_t)kStages * S::STAGE_BYTES);
+  const int xs_ld = sum_ld(p.K);
   float* s_xs = reinterpret_cast<float*>(s_sb + (size_t)S::NMAT * 2 * kRowTile * ng);
-  uint16_t* s_h = reinterpret_cast<uint16_t*>(s_xs + (size_t)kTokChunk * ng);
+  uint16_t* s_h = reinterpret_cast<uint16_t*>(s_xs + (size_t)kTokChunk * xs_ld);
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_h + (size_t)kTokChunk * kRowTile);
   uint64_t* full = bars;
   uint64_t* empty = bars + kStages;
@@ -257,7 +261,7 @@ __global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_consta
 
   const int n_rt = p.R / kRowTile;
   const int n_work = (*p.n_seg) * n_rt;
-  const int nstages = p.K / S::KT;
+  const int nstages = (p.K + S::KT - 1) / S::KT;
 
   if (warp == kComputeWarps) {
     // ------------------------------------------------------------ producer
@@ -273,7 +277,7 @@ __global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_consta
         // scales / biases / group sums for this item
         if (item > 0 && !mbar_wait(sb_empty, (item - 1) & 1u, kDevErrTimeoutScales)) { ok = false; break; }
         const uint32_t sb_bytes = (uint32_t)(kRowTile * ng * 2);
-        const uint32_t xs_bytes = (uint32_t)(ng * 4);
+        const uint32_t xs_bytes = (uint32_t)(xs_ld * 4);
         mbar_arrive_expect_tx(sb_full, S::NMAT * 2 * sb_bytes + it.nrows * xs_bytes);
         const uint16_t* src_s0 = shared ? p.ss0 : p.s0;
         const uint16_t* src_b0 = shared ? p.sb0 : p.b0;
@@ -287,7 +291,7 @@ __global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_consta
         }
         for (int r = 0; r < it.nrows; ++r) {
           const int src_row = p.row_src ? p.row_src[it.row0_seg + r] : it.row0_seg + r;
-          bulk_load(s_xs + r * ng, p.act_sum + (size_t)src_row * ng, xs_bytes, sb_full);
+          bulk_load(s_xs + r * xs_ld, p.act_sum + (size_t)src_row * xs_ld, xs_bytes, sb_full);
         }
         const CUtensorMap* m0 = shared ? &p.tm_sw0 : &p.tm_w0;
         const CUtensorMap* m1 = shared ? &p.tm_sw1 : &p.tm_w1;
@@ -299,14 +303,15 @@ __global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_consta
             break;
           }
           uint8_t* dst = stage_base + (size_t)slot * S::STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[slot], S::CODE_BYTES + it.nrows * S::KT * 2);
+          const int kcols = min(S::KT, p.K - st * S::KT);  // partial last stage: TMA zero-fills codes
+          mbar_arrive_expect_tx(&full[slot], S::CODE_BYTES + it.nrows * kcols * 2);
           const int kw = st * (S::KT * BITS / 32);
           tma_load_2d(dst, m0, kw, (int)rowg, &full[slot]);
           if (MODE == 0) tma_load_2d(dst + kRowTile * S::ROWB, m1, kw, (int)rowg, &full[slot]);
           uint8_t* adst = dst + S::CODE_BYTES;
           for (int r = 0; r < it.nrows; ++r) {
             const int src_row = p.row_src ? p.row_src[it.row0_seg + r] : it.row0_seg + r;
-            bulk_load(adst + r * S::ACT_PITCH, p.act + (size_t)src_row * p.K + (size_t)st * S::KT, S::KT * 2,
+            bulk_load(adst + r * S::ACT_PITCH, p.act + (size_t)src_row * p.K + (size_t)st * S::KT, kcols * 2,
                       &full[slot]);
           }
         }

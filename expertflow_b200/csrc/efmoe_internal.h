@@ -14,6 +14,10 @@ constexpr int kComputeWarps = 4;
 constexpr int kQmvThreads = (kComputeWarps + 1) * 32;
 constexpr int kActPad = 16;         // bytes of padding per staged activation row
 
+// Row stride (floats) of the per-64-column group sums of a K-wide activation:
+// padded to 4 groups so that every row is a whole number of 16-byte units.
+__host__ __device__ inline int sum_ld(int K) { return ((K / 64) + 3) & ~3; }
+
 // error codes written to the device error word
 constexpr int kDevErrTimeoutFull = 1001;
 constexpr int kDevErrTimeoutEmpty = 1002;

@@ -238,15 +238,19 @@ class MoELayer(torch.nn.Module):
         return c
 
     def forward(self, x: torch.Tensor, inds_out: Optional[torch.Tensor] = None,
-                wts_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                wts_out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        """y = MoE(x) in x's dtype, or fp32 (the un-rounded combine) with out_dtype=torch.float32."""
         H = self.switch_mlp.gate_proj.input_dims
         xf = x.reshape(-1, H).contiguous()
         _need_cuda(xf)
         T = xf.shape[0]
-        y = torch.empty_like(xf)
+        if out_dtype not in (None, xf.dtype, torch.float32):
+            raise TypeError("out_dtype must be None, x.dtype or torch.float32")
+        y = torch.empty(xf.shape, dtype=out_dtype or xf.dtype, device=xf.device)
         if T == 0:
             return y.reshape(x.shape)
         cfg = self.cfg(_act_dt(xf))
+        cfg.out_f32 = int(y.dtype == torch.float32)
         n = L.lib().ef_moe_workspace_size(ctypes.byref(cfg), T)
         ws = workspace(n, xf.device)
         sp = self.switch_mlp

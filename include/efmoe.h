@@ -65,8 +65,8 @@ typedef struct {
  * module (num_experts_per_tok, switch_mlp.*.bits/group_size, shared_experts)
  * plus the gate's routing parameters. */
 typedef struct {
-  int hidden;         /* H, multiple of 256 */
-  int inter;          /* I (per routed expert), multiple of 256 */
+  int hidden;         /* H, multiple of 64 */
+  int inter;          /* I (per routed expert), multiple of 64 */
   int n_experts;      /* E, 1..512 */
   int top_k;          /* k, 1..16 */
   int bits;           /* 4 or 8 */
@@ -81,6 +81,7 @@ typedef struct {
   int act_dtype;      /* EF_DT_BF16 or EF_DT_F16 (x and y) */
   int gate_dtype;     /* EF_DT_F16 or EF_DT_BF16 (router weight) */
   int path;           /* EF_PATH_AUTO / GEMV (decode kernels) / GEMM (tcgen05 grouped GEMM) */
+  int out_f32;        /* 1: y is fp32 (the combine's accumulator); 0: y has act_dtype */
 } ef_moe_cfg;
 
 /* ---- library ---------------------------------------------------------- */
@@ -91,6 +92,19 @@ const char* ef_last_error_message(void);
 /* Reads and clears the device-side error word (set by bounded waits that ran
  * out, or by an out-of-range activation); synchronises `stream`. */
 ef_status ef_get_device_error(void* stream, int* code);
+
+/* ---- tracing ------------------------------------------------------------ */
+/* When enabled, every kernel the library launches is bracketed by two CUDA
+ * events recorded on the launching stream.  ef_trace_read waits for the
+ * recorded events, writes up to max_recs (name, milliseconds) records in launch
+ * order, returns how many were written and clears the trace.  The reference
+ * times its phases with time.time() buckets (experiments/ef_profile_moe.py). */
+typedef struct {
+  const char* name;
+  float ms;
+} ef_trace_rec;
+ef_status ef_trace_enable(int on);
+int ef_trace_read(ef_trace_rec* recs, int max_recs);
 
 /* ---- whole layer ------------------------------------------------------ */
 /* Bytes of workspace ef_moe_forward needs for T tokens (256-byte aligned). */

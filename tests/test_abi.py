@@ -64,7 +64,7 @@ def test_workspace_sizes_grow_with_tokens(L):
 
 
 @pytest.mark.parametrize("kw,status", [
-    (dict(bits=3), -2), (dict(group_size=32), -2), (dict(hidden=1000), -2), (dict(top_k=0), -2),
+    (dict(bits=3), -2), (dict(group_size=32), -2), (dict(hidden=1000), -2), (dict(inter=96), -2), (dict(top_k=0), -2),
     (dict(n_experts=0), -2), (dict(router_mode=7), -1), (dict(router_mode=1, n_group=3), -2),
     (dict(router_mode=1, n_group=8, topk_group=9), -1), (dict(n_shared=1, shared_inter=512), -2),
     (dict(act_dtype=2), -2),
@@ -97,6 +97,7 @@ def test_forward_rejects_null_and_misaligned_pointers(L):
 def test_qmm_and_dequant_validation(L):
     lib = L.lib()
     assert lib.ef_quantized_matmul(16, 0, 4, 16, 16, 16, 64, 100, 4, 64, 16, 16, 1 << 30, None) == -2
+    assert lib.ef_quantized_matmul(16, 0, 4, 16, 16, 16, 64, 96, 4, 64, 16, 16, 1 << 30, None) == -2
     assert lib.ef_quantized_matmul(16, 0, 4, 16, 16, 16, 60, 256, 4, 64, 16, 16, 1 << 30, None) == -2
     assert lib.ef_dequantize(16, 16, 16, 4, 64, 5, 64, 16, 2, None) == -2
     assert lib.ef_dequantize(16, 16, 16, 0, 64, 4, 64, 16, 2, None) == 0
