@@ -22,8 +22,8 @@ cudaError_t launch_router_select(const float* logits, const float* e_bias, int T
                                  cudaStream_t st);
 cudaError_t launch_permute(const int* entries, int n_ent, int k, int n_exp, int n_sh, int seg_chunk,
                            const PermBufs& pb, cudaStream_t st);
-cudaError_t launch_prep_act(const uint16_t* act, int is_bf16, int n, int K, uint16_t* out, float* sums,
-                            cudaStream_t st);
+cudaError_t launch_prep_act(const uint16_t* act, const int* row_src, int is_bf16, int n, int K, int bits,
+                            uint16_t* out, float* sums, cudaStream_t st);
 cudaError_t launch_combine(const float* rows, const int* inv, const float* wts, int T, int k, int H, int sh_base,
                            void* out, int out_dtype, cudaStream_t st);
 cudaError_t launch_qmv(int bits, int mode, const QmvParams& p, int n_sm, cudaStream_t st);
@@ -134,6 +134,21 @@ ef_status encode_codes_map(CUtensorMap* m, const uint32_t* w, long long rows, in
   return EF_OK;
 }
 
+// 2-D map over fp16 activation rows [rows, K]: box 64 columns x 8 rows, 128-B swizzle.
+ef_status encode_act_map(CUtensorMap* m, const uint16_t* act, long long rows, int K) {
+  PFN_encodeTiled_t enc = get_encoder();
+  if (!enc) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)(rows > 0 ? rows : 1)};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)kTokChunk};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(act), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(EF_ERR_INVALID, "activation tensor map encode failed (%d)", (int)r);
+  return EF_OK;
+}
+
 int sm_count() {
   static int cache[64] = {0};
   int dev = 0;
@@ -169,7 +184,9 @@ struct FfnBufs {
   int* ids;
 };
 
-void carve_ffn(Carver& c, int n_ent, int n_rows_x, int n_bins, int n_rows, int H, int I, FfnBufs& f) {
+// Routed rows (n_rows = entries + shared rows) carry their own gathered copy of
+// the activation row (x16), so segments are contiguous for the GEMV tiles.
+void carve_ffn(Carver& c, int n_ent, int n_bins, int n_rows, int H, int I, FfnBufs& f) {
   const int max_segs = (n_rows + kTokChunk - 1) / kTokChunk + n_bins + 2;
   f.pb.counts = c.take<int>(n_bins + 1);
   f.pb.offsets = c.take<int>(n_bins + 2);
@@ -179,8 +196,8 @@ void carve_ffn(Carver& c, int n_ent, int n_rows_x, int n_bins, int n_rows, int H
   f.pb.seg_row0 = c.take<int>(max_segs);
   f.pb.seg_nrows = c.take<int>(max_segs);
   f.pb.n_seg = c.take<int>(1);
-  f.x16 = c.take<uint16_t>((size_t)n_rows_x * H);
-  f.xsum = c.take<float>((size_t)n_rows_x * sum_ld(H));
+  f.x16 = c.take<uint16_t>((size_t)n_rows * H);
+  f.xsum = c.take<float>((size_t)n_rows * sum_ld(H));
   f.h16 = c.take<uint16_t>((size_t)n_rows * I);
   f.hsum = c.take<float>((size_t)n_rows * sum_ld(I));
   f.yrows = c.take<float>((size_t)n_rows * H);
@@ -226,7 +243,7 @@ QmvParams make_params_common() {
 }
 
 // gate/up (mode 0) then down (mode 1) over permuted rows already described by f.pb.
-ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, const int* row_src_x, const ef_qweight& gate,
+ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, const ef_qweight& gate,
                       const ef_qweight& up, const ef_qweight& down, const ef_qweight* sg, const ef_qweight* su,
                       const ef_qweight* sd, cudaStream_t st) {
   const int H = c->hidden, I = c->inter, E = c->n_experts, bits = c->bits;
@@ -234,6 +251,7 @@ ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, const int* row_src_
   ef_status s;
   // mode 0: K = H, R = I
   QmvParams p0 = make_params_common();
+  p0.w0 = gate.w; p0.w1 = up.w; p0.sw0 = sg ? sg->w : gate.w; p0.sw1 = su ? su->w : up.w;
   if ((s = encode_codes_map(&p0.tm_w0, gate.w, (long long)E * I, H * bits / 32))) return s;
   if ((s = encode_codes_map(&p0.tm_w1, up.w, (long long)E * I, H * bits / 32))) return s;
   if (sg) {
@@ -245,13 +263,15 @@ ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, const int* row_src_
     p0.ss0 = gate.scales; p0.sb0 = gate.biases; p0.ss1 = up.scales; p0.sb1 = up.biases;
   }
   p0.s0 = gate.scales; p0.b0 = gate.biases; p0.s1 = up.scales; p0.b1 = up.biases;
-  p0.act = f.x16; p0.act_sum = f.xsum; p0.row_src = row_src_x;
+  if ((s = encode_act_map(&p0.tm_act, f.x16, n_rows, H))) return s;
+  p0.act_sum = f.xsum;
   p0.seg_expert = f.pb.seg_expert; p0.seg_row0 = f.pb.seg_row0; p0.seg_nrows = f.pb.seg_nrows; p0.n_seg = f.pb.n_seg;
   p0.K = H; p0.R = I; p0.n_experts = E;
   p0.h_out = f.h16; p0.hsum_out = f.hsum; p0.y_out = nullptr;
   EF_LAUNCH("qmv_gate_up", launch_qmv(bits, 0, p0, nsm, st));
   // mode 1: K = I, R = H
   QmvParams p1 = make_params_common();
+  p1.w0 = down.w; p1.w1 = down.w; p1.sw0 = sd ? sd->w : down.w; p1.sw1 = p1.sw0;
   if ((s = encode_codes_map(&p1.tm_w0, down.w, (long long)E * H, I * bits / 32))) return s;
   if (sd) {
     if ((s = encode_codes_map(&p1.tm_sw0, sd->w, H, I * bits / 32))) return s;
@@ -261,7 +281,8 @@ ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, const int* row_src_
   }
   p1.tm_w1 = p1.tm_w0; p1.tm_sw1 = p1.tm_sw0;
   p1.s0 = down.scales; p1.b0 = down.biases;
-  p1.act = f.h16; p1.act_sum = f.hsum; p1.row_src = nullptr;
+  if ((s = encode_act_map(&p1.tm_act, f.h16, n_rows, I))) return s;
+  p1.act_sum = f.hsum;
   p1.seg_expert = f.pb.seg_expert; p1.seg_row0 = f.pb.seg_row0; p1.seg_nrows = f.pb.seg_nrows; p1.n_seg = f.pb.n_seg;
   p1.K = I; p1.R = H; p1.n_experts = E;
   p1.y_out = f.yrows;
@@ -371,7 +392,7 @@ static size_t moe_ws(const ef_moe_cfg* cfg, int T, Carver& c, float** logits, in
   *logits = c.take<float>((size_t)T * E);
   *inds = c.take<int>((size_t)n_ent);
   *wts = c.take<float>((size_t)n_ent);
-  carve_ffn(c, n_ent, T, E + 1, n_rows, cfg->hidden, cfg->inter, *f);
+  carve_ffn(c, n_ent, E + 1, n_rows, cfg->hidden, cfg->inter, *f);
   return c.off;
 }
 
@@ -424,8 +445,9 @@ ef_status ef_moe_forward(const ef_moe_cfg* cfg, const void* x, int T, const void
                                st));
   const int n_sh = cfg->n_shared ? T : 0;
   EF_LAUNCH("permute", launch_permute(inds, T * k, k, E, n_sh, kTokChunk, f.pb, st));
-  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), bf, T, H, f.x16, f.xsum, st));
-  if ((s = run_experts(cfg, f, f.pb.row_src, gate, up, down, cfg->n_shared ? sg : nullptr,
+  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), f.pb.row_src, bf, T * k + n_sh, H, cfg->bits,
+                                        f.x16, f.xsum, st));
+  if ((s = run_experts(cfg, f, T * k + n_sh, gate, up, down, cfg->n_shared ? sg : nullptr,
                        cfg->n_shared ? su : nullptr, cfg->n_shared ? sd : nullptr, st)))
     return s;
   // shared rows start at offsets[E] == T*k
@@ -438,7 +460,7 @@ size_t ef_experts_workspace_size(const ef_moe_cfg* cfg, int N) {
   if (!cfg || N < 0) return 0;
   Carver c{nullptr};
   FfnBufs f;
-  carve_ffn(c, N, N, cfg->n_experts + 1, N, cfg->hidden, cfg->inter, f);
+  carve_ffn(c, N, cfg->n_experts + 1, N, cfg->hidden, cfg->inter, f);
   return c.off + 256;
 }
 
@@ -458,11 +480,12 @@ ef_status ef_moe_experts_forward(const ef_moe_cfg* cfg, const void* x_rows, int 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Carver c{static_cast<uint8_t*>(workspace)};
   FfnBufs f;
-  carve_ffn(c, N, N, cfg->n_experts + 1, N, cfg->hidden, cfg->inter, f);
+  carve_ffn(c, N, cfg->n_experts + 1, N, cfg->hidden, cfg->inter, f);
   const bool bf = cfg->act_dtype == EF_DT_BF16;
   EF_LAUNCH("permute", launch_permute(row_expert, N, 1, cfg->n_experts, 0, kTokChunk, f.pb, st));
-  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x_rows), bf, N, cfg->hidden, f.x16, f.xsum, st));
-  if ((s = run_experts(cfg, f, f.pb.row_src, gate, up, down, nullptr, nullptr, nullptr, st))) return s;
+  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x_rows), f.pb.row_src, bf, N, cfg->hidden,
+                                        cfg->bits, f.x16, f.xsum, st));
+  if ((s = run_experts(cfg, f, N, gate, up, down, nullptr, nullptr, nullptr, st))) return s;
   EF_LAUNCH("combine", launch_combine(f.yrows, f.pb.inv, nullptr, N, 1, cfg->hidden, -1, y_rows, EF_DT_F32, st));
   return EF_OK;
 }
@@ -479,8 +502,9 @@ static size_t qmm_ws(int M, int k, int n_exp, int out_dim, int in_dim, Carver& c
   f.pb.seg_row0 = c.take<int>(max_segs);
   f.pb.seg_nrows = c.take<int>(max_segs);
   f.pb.n_seg = c.take<int>(1);
-  f.x16 = c.take<uint16_t>((size_t)n_rows_x * in_dim);
-  f.xsum = c.take<float>((size_t)n_rows_x * sum_ld(in_dim));
+  (void)n_rows_x;
+  f.x16 = c.take<uint16_t>((size_t)n_ent * in_dim);
+  f.xsum = c.take<float>((size_t)n_ent * sum_ld(in_dim));
   f.yrows = c.take<float>((size_t)n_ent * out_dim);
   f.ids = c.take<int>((size_t)M);  // expert ids (all zero) for the single-matrix case
   return c.off;
@@ -496,13 +520,15 @@ static ef_status check_qmm(int out_dim, int in_dim, int bits, int group) {
 }
 
 static ef_status run_single_matrix(const ef_qweight& w, int n_exp, int out_dim, int in_dim, int bits,
-                                   const FfnBufs& f, const int* row_src, cudaStream_t st) {
+                                   const FfnBufs& f, int n_rows, cudaStream_t st) {
   QmvParams p = make_params_common();
   ef_status s;
+  p.w0 = w.w; p.w1 = w.w; p.sw0 = w.w; p.sw1 = w.w;
   if ((s = encode_codes_map(&p.tm_w0, w.w, (long long)n_exp * out_dim, in_dim * bits / 32))) return s;
   p.tm_w1 = p.tm_w0; p.tm_sw0 = p.tm_w0; p.tm_sw1 = p.tm_w0;
   p.s0 = w.scales; p.b0 = w.biases; p.ss0 = w.scales; p.sb0 = w.biases;
-  p.act = f.x16; p.act_sum = f.xsum; p.row_src = row_src;
+  if ((s = encode_act_map(&p.tm_act, f.x16, n_rows, in_dim))) return s;
+  p.act_sum = f.xsum;
   p.seg_expert = f.pb.seg_expert; p.seg_row0 = f.pb.seg_row0; p.seg_nrows = f.pb.seg_nrows; p.n_seg = f.pb.n_seg;
   p.K = in_dim; p.R = out_dim; p.n_experts = n_exp;
   p.y_out = f.yrows;
@@ -537,8 +563,9 @@ ef_status ef_quantized_matmul(const void* x, int act_dtype, int M, const uint32_
   int* ids = f.ids;
   EF_CUDA(cudaMemsetAsync(ids, 0, sizeof(int) * (size_t)M, st));
   EF_LAUNCH("permute", launch_permute(ids, M, 1, 1, 0, kTokChunk, f.pb, st));
-  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), act_dtype == EF_DT_BF16, M, in_dim, f.x16, f.xsum, st));
-  if ((s = run_single_matrix(q, 1, out_dim, in_dim, bits, f, f.pb.row_src, st))) return s;
+  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), f.pb.row_src, act_dtype == EF_DT_BF16, M,
+                                        in_dim, bits, f.x16, f.xsum, st));
+  if ((s = run_single_matrix(q, 1, out_dim, in_dim, bits, f, M, st))) return s;
   EF_LAUNCH("combine", launch_combine(f.yrows, f.pb.inv, nullptr, M, 1, out_dim, -1, y, act_dtype, st));
   return EF_OK;
 }
@@ -567,8 +594,9 @@ ef_status ef_gather_qmm(const void* x, int act_dtype, int T, const int32_t* indi
   FfnBufs f;
   qmm_ws(T, k, n_experts, out_dim, in_dim, c, f, T);
   EF_LAUNCH("permute", launch_permute(indices, T * k, k, n_experts, 0, kTokChunk, f.pb, st));
-  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), act_dtype == EF_DT_BF16, T, in_dim, f.x16, f.xsum, st));
-  if ((s = run_single_matrix(w, n_experts, out_dim, in_dim, bits, f, f.pb.row_src, st))) return s;
+  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), f.pb.row_src, act_dtype == EF_DT_BF16,
+                                        T * k, in_dim, bits, f.x16, f.xsum, st));
+  if ((s = run_single_matrix(w, n_experts, out_dim, in_dim, bits, f, T * k, st))) return s;
   EF_LAUNCH("combine", launch_combine(f.yrows, f.pb.inv, nullptr, T * k, 1, out_dim, -1, y, act_dtype, st));
   return EF_OK;
 }

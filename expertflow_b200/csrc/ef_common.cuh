@@ -74,6 +74,11 @@ EF_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Prefetch a contiguous global range into L2 (bytes % 16 == 0, 16-byte aligned).
+EF_DEV void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
 EF_DEV void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -114,6 +119,15 @@ EF_DEV uint16_t f32_to_h16_sat(float v) {
   return __half_as_ushort(__float2half_rn(v));
 }
 
-// Position of column c (within its 8-column block) in the pair-ordered
-// activation layout [c0 c4 c1 c5 c2 c6 c3 c7].
-EF_DEV int pair_pos(int c) { return ((c & 3) << 1) | ((c >> 2) & 1); }
+// Activation layout seen by the GEMV kernel: each 8-column block is stored
+// permuted so that the pairs of codes unpacked into one 32-bit register meet
+// the matching 32-bit pair of activations.
+//   4-bit codes: [c0 c4 c1 c5 c2 c6 c3 c7]   (nibbles s and s+4 of a word)
+//   8-bit codes: [c0 c2 c4 c6 c1 c3 c5 c7]   (bytes 0/2 and 1/3 of a word)
+// act_pos: position of column c (0..7) in its block; act_col: the inverse.
+__host__ __device__ __forceinline__ int act_pos(int c, int bits) {
+  return bits == 4 ? (((c & 3) << 1) | ((c >> 2) & 1)) : (((c & 1) << 2) | (c >> 1));
+}
+__host__ __device__ __forceinline__ int act_col(int p, int bits) {
+  return bits == 4 ? ((p >> 1) | ((p & 1) << 2)) : (((p & 3) << 1) | (p >> 2));
+}

@@ -137,15 +137,20 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(const int* __rest
 }
 
 // ---------------------------------------------------------------- prep
-// act [n, K] (bf16 or fp16) -> out [n, K] fp16 pair-ordered, sums [n, K/64].
-__global__ void prep_act_kernel(const uint16_t* __restrict__ act, int is_bf16, int n, int K,
-                                uint16_t* __restrict__ out, float* __restrict__ sums) {
+// Output row j = act[row_src[j]] (or act[j] when row_src is null), converted
+// to fp16 in the GEMV activation layout (act_pos for `bits`), plus the sums
+// [n, sum_ld(K)] of each 64-column group.  Gathering the routed rows here makes
+// every segment's rows contiguous for the GEMV kernel's tile loads.
+__global__ void prep_act_kernel(const uint16_t* __restrict__ act, const int* __restrict__ row_src, int is_bf16, int n,
+                                int K, int bits, uint16_t* __restrict__ out, float* __restrict__ sums) {
   const int nblk = K >> 3;
   long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   long long total = (long long)n * nblk;
   bool valid = gid < total;
   long long g = valid ? gid : 0;
-  uint4 v = reinterpret_cast<const uint4*>(act)[g];
+  const long long orow = g / nblk;
+  const long long irow = row_src ? __ldg(row_src + orow) : orow;
+  uint4 v = reinterpret_cast<const uint4*>(act)[irow * nblk + (g - orow * nblk)];
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
   float f[8];
 #pragma unroll
@@ -153,23 +158,22 @@ __global__ void prep_act_kernel(const uint16_t* __restrict__ act, int is_bf16, i
     f[2 * i] = act_to_f32(static_cast<uint16_t>(w[i] & 0xffffu), is_bf16);
     f[2 * i + 1] = act_to_f32(static_cast<uint16_t>(w[i] >> 16), is_bf16);
   }
-  __half h[8];
+  uint16_t h[8];
   float s = 0.0f;
   bool bad = false;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     if (!(fabsf(f[i]) <= 65504.0f)) bad = true;
-    h[i] = __float2half_rn(f[i]);
-    s += __half2float(h[i]);
+    __half hv = __float2half_rn(f[i]);
+    h[i] = __half_as_ushort(hv);
+    s += __half2float(hv);
   }
   if (valid && bad) ef_set_error(kDevErrRange);
-  // pair order: (c0,c4) (c1,c5) (c2,c6) (c3,c7)
-  uint4 o;
-  o.x = (uint32_t)__half_as_ushort(h[0]) | ((uint32_t)__half_as_ushort(h[4]) << 16);
-  o.y = (uint32_t)__half_as_ushort(h[1]) | ((uint32_t)__half_as_ushort(h[5]) << 16);
-  o.z = (uint32_t)__half_as_ushort(h[2]) | ((uint32_t)__half_as_ushort(h[6]) << 16);
-  o.w = (uint32_t)__half_as_ushort(h[3]) | ((uint32_t)__half_as_ushort(h[7]) << 16);
-  if (valid) reinterpret_cast<uint4*>(out)[g] = o;
+  uint32_t o[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    o[q] = (uint32_t)h[act_col(2 * q, bits)] | ((uint32_t)h[act_col(2 * q + 1, bits)] << 16);
+  if (valid) reinterpret_cast<uint4*>(out)[g] = make_uint4(o[0], o[1], o[2], o[3]);
   // 8 consecutive threads cover one 64-column group (nblk is a multiple of 8)
   s += __shfl_xor_sync(0xffffffffu, s, 1);
   s += __shfl_xor_sync(0xffffffffu, s, 2);
@@ -233,13 +237,13 @@ cudaError_t launch_permute(const int* entries, int n_ent, int k, int n_exp, int 
   return cudaGetLastError();
 }
 
-cudaError_t launch_prep_act(const uint16_t* act, int is_bf16, int n, int K, uint16_t* out, float* sums,
-                            cudaStream_t st) {
+cudaError_t launch_prep_act(const uint16_t* act, const int* row_src, int is_bf16, int n, int K, int bits,
+                            uint16_t* out, float* sums, cudaStream_t st) {
   long long total = (long long)n * (K / 8);
   if (total == 0) return cudaSuccess;
   int threads = 256;
   long long blocks = (total + threads - 1) / threads;
-  prep_act_kernel<<<(unsigned)blocks, threads, 0, st>>>(act, is_bf16, n, K, out, sums);
+  prep_act_kernel<<<(unsigned)blocks, threads, 0, st>>>(act, row_src, is_bf16, n, K, bits, out, sums);
   return cudaGetLastError();
 }
 

@@ -4,31 +4,36 @@
 // (gate, up, silu*up, down) for small token counts, where the layer is bound by
 // HBM bandwidth on the packed weights.
 //
-// Work item = (segment of <= 32 rows routed to one expert) x (64 weight rows).
-// A CTA is 4 compute warps + 1 producer warp and loops over work items
-// (persistent).  The producer streams, per 256-column (4-bit) / 128-column
-// (8-bit) stage, the 64-row code tile(s) with a 2-D TMA load (128-byte
-// swizzle) and the segment's activation rows with 1-D bulk copies into a
-// 4-deep mbarrier ring; per work item it also bulk-loads the tile's fp16
-// scales/biases and the rows' group sums.
+// Work item = (segment of <= 8 rows routed to one expert) x (64 weight rows).
+// A CTA has 4 compute warps (16 rows each), a TMA producer warp and a scale
+// producer warp, and loops over work items (persistent; two CTAs per SM when
+// shared memory allows).  The TMA warp streams, per 256-column (4-bit) /
+// 128-column (8-bit) stage, the 64-row code tile of each matrix with a 2-D TMA
+// load (128-byte swizzle) and the segment's activation rows with 1-D bulk
+// copies into an mbarrier ring.  The scale warp bulk-loads, per work item, the
+// tile's fp16 scales/biases (row pitch padded against bank conflicts when the
+// row length allows) and the rows' group sums into one of two slots, so the
+// next item's loads overlap this item's math.
 //
-// Dot products run on the tensor cores with exact operands: a code q is
-// unpacked into the fp16 value 1 + q/16 (4-bit: nibble moved to mantissa bits
-// 6..9 with one shift and one LOP3 per pair) or 1 + q/1024 (8-bit: byte into
-// bits 0..7 with PRMT + LOP3), activations are fp16, products accumulate in
-// fp32 per 64-column group:
-//     D_g = sum_i x_i (1 + q_i / Q)
-//     y  += (Q s_g) D_g + (b_g - Q s_g) sum_i x_i        (= sum_i x_i (s_g q_i + b_g))
+// Dot products run on the tensor cores with exact operands: a code q becomes
+// the fp16 value 1 + q/1024 by masking it into the low mantissa bits (one LOP3
+// per pair of codes plus one shift per nibble/byte position); activations are
+// fp16; products accumulate in fp32 per 64-column group in two independent MMA
+// chains per matrix:
+//     D_g = sum_i x_i (1 + q_i / 1024)
+//     y  += (1024 s_g) D_g + (b_g - 1024 s_g) sum_i x_i    (= sum_i x_i (s_g q_i + b_g))
 // The k order inside mma.m16n8k16 is permuted consistently for codes and
-// activations (activations are stored in "pair order"), which leaves every
-// dot product unchanged.
+// activations (see act_pos), which leaves every dot product unchanged.
 //
 // mode 0: gate and up tiles together, epilogue h = silu(g) * u stored as fp16
-//         pair-ordered rows + group sums (input of mode 1).
+//         rows in the activation layout + group sums (input of mode 1).
 // mode 1: down projection, fp32 rows for the combine.
 #include "ef_common.cuh"
 
 namespace ef {
+
+constexpr int kTmaWarp = kComputeWarps;
+constexpr int kScaleWarp = kComputeWarps + 1;
 
 template <int BITS, int MODE>
 struct QmvShape {
@@ -37,34 +42,41 @@ struct QmvShape {
   static constexpr int ROWB = KT * BITS / 8;          // bytes per code row per stage (128)
   static constexpr int NMAT = MODE == 0 ? 2 : 1;
   static constexpr int CODE_BYTES = NMAT * kRowTile * ROWB;
-  static constexpr int ACT_PITCH = KT * 2 + kActPad;
-  static constexpr int ACT_BYTES = kTokChunk * ACT_PITCH;
+  static constexpr int ACT_BOX = kTokChunk * 128;     // one 64-column group of 8 activation rows
+  static constexpr int ACT_BYTES = GPS * ACT_BOX;
   static constexpr int STAGE_BYTES = ((CODE_BYTES + ACT_BYTES) + 1023) / 1024 * 1024;
-  static constexpr float Q = BITS == 4 ? 16.0f : 1024.0f;
 };
+constexpr float kQ = 1024.0f;
+
+// Group sums and scales/biases are copied as contiguous blocks (one copy per
+// array per item): their shared-memory row pitch is the global one.
+__host__ __device__ inline int xs_pitch(int K) { return sum_ld(K); }
+__host__ __device__ inline int sb_pitch(int K) { return K / 64; }
 
 template <int BITS, int MODE>
-__host__ __device__ inline size_t qmv_smem_bytes(int K) {
+__host__ __device__ inline size_t qmv_sb_bytes(int K) {  // scales + biases of one item
+  return (size_t)QmvShape<BITS, MODE>::NMAT * 2 * kRowTile * sb_pitch(K) * 2;
+}
+__host__ __device__ inline size_t qmv_xs_bytes(int K) { return (size_t)kTokChunk * xs_pitch(K) * 4; }
+template <int BITS, int MODE>
+__host__ __device__ inline size_t qmv_slot_bytes(int K) {
+  return (qmv_sb_bytes<BITS, MODE>(K) + 127) / 128 * 128 + (qmv_xs_bytes(K) + 127) / 128 * 128;
+}
+
+// Shared memory: `ns` pipeline stages, two per-item slots (scales/biases and
+// group sums), the h staging tile and the barriers.
+template <int BITS, int MODE>
+__host__ __device__ inline size_t qmv_smem_bytes(int K, int ns) {
   using S = QmvShape<BITS, MODE>;
-  const int ng = K / 64;
   size_t b = 1024;  // alignment slack
-  b += (size_t)kStages * S::STAGE_BYTES;
-  b += (size_t)S::NMAT * 2 * kRowTile * ng * 2;  // scales + biases
-  b += (size_t)kTokChunk * sum_ld(K) * 4;       // activation group sums
-  b += (size_t)kTokChunk * kRowTile * 2;         // h staging (mode 0)
-  b += 128;                                      // barriers
+  b += (size_t)ns * S::STAGE_BYTES;
+  b += 2 * qmv_slot_bytes<BITS, MODE>(K);
+  b += (size_t)kTokChunk * kRowTile * 2;  // h staging (mode 0)
+  b += 256;                               // barriers
   return b;
 }
 
-EF_DEV uint32_t pair4(uint32_t w, int s) {
-  // nibbles s and s+4 -> fp16 pair (1 + q_s/16, 1 + q_{s+4}/16)
-  uint32_t v = (s == 0) ? (w << 6) : (s == 1) ? (w << 2) : (s == 2) ? (w >> 2) : (w >> 6);
-  return lop3_and_or(v, 0x03C003C0u, 0x3C003C00u);
-}
-EF_DEV uint32_t pair8(uint32_t a, uint32_t b, int s) {
-  // byte s of a and byte s of b -> fp16 pair (1 + qa/1024, 1 + qb/1024)
-  return lop3_and_or(prmt(a, b, (uint32_t)(s | ((4 + s) << 8))), 0x00FF00FFu, 0x3C003C00u);
-}
+EF_DEV uint32_t mag(uint32_t v, uint32_t mask) { return lop3_and_or(v, mask, 0x3C003C00u); }
 
 struct WorkItem {
   int expert, row0_seg, nrows, rt;
@@ -74,187 +86,255 @@ EF_DEV WorkItem decode_work(const QmvParams& p, int w, int n_rt) {
   WorkItem it;
   int seg = w / n_rt;
   it.rt = w - seg * n_rt;
-  it.expert = p.seg_expert[seg];
-  it.row0_seg = p.seg_row0[seg];
-  it.nrows = p.seg_nrows[seg];
+  it.expert = __ldg(p.seg_expert + seg);
+  it.row0_seg = __ldg(p.seg_row0 + seg);
+  it.nrows = __ldg(p.seg_nrows + seg);
   return it;
 }
 
-template <int BITS, int MODE, int NT>
-EF_DEV bool qmv_consume(const QmvParams& p, const WorkItem& it, uint8_t* stage_base, const uint16_t* s_sb,
-                        const float* s_xs, uint16_t* s_h, uint64_t* full, uint64_t* empty, uint64_t* sb_empty,
-                        uint64_t* epi, uint32_t item, uint32_t& fill_it) {
+// Bounded barrier among the compute warps built from an mbarrier.
+EF_DEV bool warps_sync(uint64_t* bar, uint32_t parity) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+  return mbar_wait(bar, parity, kDevErrTimeoutFull);
+}
+
+struct QmvSmem {
+  uint8_t* stage_base;
+  uint8_t* slot_base;
+  uint16_t* s_h;
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* sb_full;   // [2]
+  uint64_t* sb_empty;  // [2]
+  uint64_t* sync;      // [2] epilogue staging
+};
+
+// Dot products of one 64-column group for rows rA, rB of matrix m and the
+// segment's 8 tokens; folds the group's affine scale into y.
+template <int BITS, int MODE>
+EF_DEV void qmv_group(const uint8_t* cm, const uint4 (&blk)[2], int G, int rA, int rB, int t, float sA, float sB,
+                      float bA, float bB, float x0, float x1, float (&y)[4]) {
+  float D[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  if constexpr (BITS == 4) {
+    const int chunk = 2 * G + (t >> 1);
+    const uint2 va = *reinterpret_cast<const uint2*>(cm + rA * 128 + ((chunk ^ (rA & 7)) << 4) + 8 * (t & 1));
+    const uint2 vb = *reinterpret_cast<const uint2*>(cm + rB * 128 + ((chunk ^ (rB & 7)) << 4) + 8 * (t & 1));
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t wa = h ? va.y : va.x, wb = h ? vb.y : vb.x;
+      // nibble pairs (s, s+4): P_s = ((w >> 4s) & 0x000F000F) | 1.0h
+      const uint32_t a0[4] = {mag(wa, 0x000F000Fu), mag(wb, 0x000F000Fu), mag(wa >> 4, 0x000F000Fu),
+                              mag(wb >> 4, 0x000F000Fu)};
+      const uint32_t a1[4] = {mag(wa >> 8, 0x000F000Fu), mag(wb >> 8, 0x000F000Fu), mag(wa >> 12, 0x000F000Fu),
+                              mag(wb >> 12, 0x000F000Fu)};
+      mma_16816(D[0], a0, blk[h].x, blk[h].y);
+      mma_16816(D[1], a1, blk[h].z, blk[h].w);
+    }
+  } else {
+    const int chunk = 4 * G + t;
+    const uint4 va = *reinterpret_cast<const uint4*>(cm + rA * 128 + ((chunk ^ (rA & 7)) << 4));
+    const uint4 vb = *reinterpret_cast<const uint4*>(cm + rB * 128 + ((chunk ^ (rB & 7)) << 4));
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t wa0 = h ? va.z : va.x, wa1 = h ? va.w : va.y;  // row A: cols 0-3, 4-7 of block h
+      const uint32_t wb0 = h ? vb.z : vb.x, wb1 = h ? vb.w : vb.y;
+      // bytes (0,2) and (1,3) of a word: ((w >> 8k) & 0x00FF00FF) | 1.0h
+      const uint32_t a0[4] = {mag(wa0, 0x00FF00FFu), mag(wb0, 0x00FF00FFu), mag(wa1, 0x00FF00FFu),
+                              mag(wb1, 0x00FF00FFu)};
+      const uint32_t a1[4] = {mag(wa0 >> 8, 0x00FF00FFu), mag(wb0 >> 8, 0x00FF00FFu), mag(wa1 >> 8, 0x00FF00FFu),
+                              mag(wb1 >> 8, 0x00FF00FFu)};
+      mma_16816(D[0], a0, blk[h].x, blk[h].y);
+      mma_16816(D[1], a1, blk[h].z, blk[h].w);
+    }
+  }
+  y[0] = fmaf(sA, D[0][0] + D[1][0], fmaf(bA, x0, y[0]));
+  y[1] = fmaf(sA, D[0][1] + D[1][1], fmaf(bA, x1, y[1]));
+  y[2] = fmaf(sB, D[0][2] + D[1][2], fmaf(bB, x0, y[2]));
+  y[3] = fmaf(sB, D[0][3] + D[1][3], fmaf(bB, x1, y[3]));
+}
+
+// One work item for one compute warp.  Returns false after a failed wait.
+template <int BITS, int MODE>
+EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, int q, uint32_t item,
+                     uint32_t fill_base, int ns) {
   using S = QmvShape<BITS, MODE>;
   const int lane = threadIdx.x & 31, cw = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int ng = p.K / 64;
-  const int xs_ld = sum_ld(p.K);
+  const int xp = xs_pitch(p.K), sp = sb_pitch(p.K);
   const int nstages = (p.K + S::KT - 1) / S::KT;
   const int rA = cw * 16 + g, rB = rA + 8;
-  float y[S::NMAT][NT][4];
+  const uint8_t* slot = sm.slot_base + (size_t)q * qmv_slot_bytes<BITS, MODE>(p.K);
+  const uint16_t* s_sb = reinterpret_cast<const uint16_t*>(slot);
+  const float* s_xs = reinterpret_cast<const float*>(slot + (qmv_sb_bytes<BITS, MODE>(p.K) + 127) / 128 * 128);
+  const bool vec_ok = (ng & 3) == 0;  // stage groups 8-byte aligned in the scale rows
+
+  float y[S::NMAT][4];
 #pragma unroll
   for (int m = 0; m < S::NMAT; ++m)
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) y[m][n][i] = 0.0f;
+    for (int i = 0; i < 4; ++i) y[m][i] = 0.0f;
 
-  for (int st = 0; st < nstages; ++st, ++fill_it) {
-    const int slot = fill_it % kStages;
-    const uint32_t parity = (fill_it / kStages) & 1u;
-    if (!mbar_wait(&full[slot], parity, kDevErrTimeoutFull)) return false;
-    const uint8_t* codes = stage_base + (size_t)slot * S::STAGE_BYTES;
-    const uint8_t* act = codes + S::CODE_BYTES;
+  for (int st = 0; st < nstages; ++st) {
+    const uint32_t f = fill_base + st;
+    const int slot_i = f % ns;
+    if (!mbar_wait(&sm.full[slot_i], (f / ns) & 1u, kDevErrTimeoutFull)) return false;
+    const uint8_t* codes = sm.stage_base + (size_t)slot_i * S::STAGE_BYTES;
+    // activation box of group G: [8 rows][128 B], 16-byte chunk c of row r at chunk c ^ r
+    const uint8_t* act = codes + S::CODE_BYTES + (size_t)g * 128;
     const int gvalid = min(S::GPS, ng - st * S::GPS);  // last stage may be partial
+    const int g0 = st * S::GPS;
+    if (gvalid == S::GPS && vec_ok) {
+      // ---- full stage: all loads of the stage issued up front, groups unguarded
+      float xa[S::GPS], xb[S::GPS];
+      if constexpr (S::GPS == 4) {
+        const float4 u = *reinterpret_cast<const float4*>(s_xs + (2 * t) * xp + g0);
+        const float4 v = *reinterpret_cast<const float4*>(s_xs + (2 * t + 1) * xp + g0);
+        xa[0] = u.x; xa[1] = u.y; xa[2] = u.z; xa[3] = u.w;
+        xb[0] = v.x; xb[1] = v.y; xb[2] = v.z; xb[3] = v.w;
+      } else {
+        const float2 u = *reinterpret_cast<const float2*>(s_xs + (2 * t) * xp + g0);
+        const float2 v = *reinterpret_cast<const float2*>(s_xs + (2 * t + 1) * xp + g0);
+        xa[0] = u.x; xa[1] = u.y;
+        xb[0] = v.x; xb[1] = v.y;
+      }
+      uint4 blk[S::GPS][2];
 #pragma unroll
-    for (int G = 0; G < S::GPS; ++G) {
-      if (G >= gvalid) break;
-      const int Gabs = st * S::GPS + G;
-      // ---- B operands (activation rows nt*8 + g)
-      uint4 blk0[NT], blk1[NT];
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        const uint8_t* ar = act + (size_t)(n * 8 + g) * S::ACT_PITCH + (size_t)(8 * G + 2 * t) * 16;
-        blk0[n] = *reinterpret_cast<const uint4*>(ar);
-        blk1[n] = *reinterpret_cast<const uint4*>(ar + 16);
+      for (int G = 0; G < S::GPS; ++G) {
+        blk[G][0] = *reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t) ^ g) << 4));
+        blk[G][1] = *reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t + 1) ^ g) << 4));
       }
 #pragma unroll
       for (int m = 0; m < S::NMAT; ++m) {
-        const uint8_t* cm = codes + (size_t)m * kRowTile * S::ROWB;
-        float D[NT][4];
+        const uint16_t* ms = s_sb + (size_t)m * 2 * kRowTile * sp;
+        const uint16_t* mb = ms + (size_t)kRowTile * sp;
+        uint16_t hsA[S::GPS], hsB[S::GPS], hbA[S::GPS], hbB[S::GPS];
+        if constexpr (S::GPS == 4) {
+          const uint2 a = *reinterpret_cast<const uint2*>(ms + rA * sp + g0);
+          const uint2 b = *reinterpret_cast<const uint2*>(ms + rB * sp + g0);
+          const uint2 c = *reinterpret_cast<const uint2*>(mb + rA * sp + g0);
+          const uint2 d = *reinterpret_cast<const uint2*>(mb + rB * sp + g0);
+          const uint32_t wa[2] = {a.x, a.y}, wb[2] = {b.x, b.y}, wc[2] = {c.x, c.y}, wd[2] = {d.x, d.y};
 #pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) D[n][i] = 0.0f;
-        if constexpr (BITS == 4) {
-          const int chunk = 2 * G + (t >> 1);
-          const uint2 wa = *reinterpret_cast<const uint2*>(cm + rA * 128 + ((chunk ^ (rA & 7)) << 4) + 8 * (t & 1));
-          const uint2 wb = *reinterpret_cast<const uint2*>(cm + rB * 128 + ((chunk ^ (rB & 7)) << 4) + 8 * (t & 1));
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t ga = (j >> 1) ? wa.y : wa.x;
-            const uint32_t gb = (j >> 1) ? wb.y : wb.x;
-            const int s0 = 2 * (j & 1);
-            uint32_t a[4] = {pair4(ga, s0), pair4(gb, s0), pair4(ga, s0 + 1), pair4(gb, s0 + 1)};
-#pragma unroll
-            for (int n = 0; n < NT; ++n) {
-              const uint4& bk = (j >> 1) ? blk1[n] : blk0[n];
-              mma_16816(D[n], a, (j & 1) ? bk.z : bk.x, (j & 1) ? bk.w : bk.y);
-            }
+          for (int G = 0; G < 4; ++G) {
+            hsA[G] = (uint16_t)(wa[G >> 1] >> (16 * (G & 1)));
+            hsB[G] = (uint16_t)(wb[G >> 1] >> (16 * (G & 1)));
+            hbA[G] = (uint16_t)(wc[G >> 1] >> (16 * (G & 1)));
+            hbB[G] = (uint16_t)(wd[G >> 1] >> (16 * (G & 1)));
           }
         } else {
-          const int chunk = 4 * G + t;
-          const uint4 wa = *reinterpret_cast<const uint4*>(cm + rA * 128 + ((chunk ^ (rA & 7)) << 4));
-          const uint4 wb = *reinterpret_cast<const uint4*>(cm + rB * 128 + ((chunk ^ (rB & 7)) << 4));
+          const uint32_t a = *reinterpret_cast<const uint32_t*>(ms + rA * sp + g0);
+          const uint32_t b = *reinterpret_cast<const uint32_t*>(ms + rB * sp + g0);
+          const uint32_t c = *reinterpret_cast<const uint32_t*>(mb + rA * sp + g0);
+          const uint32_t d = *reinterpret_cast<const uint32_t*>(mb + rB * sp + g0);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t aA = (j >> 1) ? wa.z : wa.x, aB = (j >> 1) ? wa.w : wa.y;
-            const uint32_t bA = (j >> 1) ? wb.z : wb.x, bB = (j >> 1) ? wb.w : wb.y;
-            const int s0 = 2 * (j & 1);
-            uint32_t a[4] = {pair8(aA, aB, s0), pair8(bA, bB, s0), pair8(aA, aB, s0 + 1), pair8(bA, bB, s0 + 1)};
-#pragma unroll
-            for (int n = 0; n < NT; ++n) {
-              const uint4& bk = (j >> 1) ? blk1[n] : blk0[n];
-              mma_16816(D[n], a, (j & 1) ? bk.z : bk.x, (j & 1) ? bk.w : bk.y);
-            }
+          for (int G = 0; G < 2; ++G) {
+            hsA[G] = (uint16_t)(a >> (16 * G));
+            hsB[G] = (uint16_t)(b >> (16 * G));
+            hbA[G] = (uint16_t)(c >> (16 * G));
+            hbB[G] = (uint16_t)(d >> (16 * G));
           }
         }
-        // ---- per-group affine epilogue
-        const uint16_t* sm = s_sb + (size_t)m * 2 * kRowTile * ng;
-        const uint16_t* bm = sm + (size_t)kRowTile * ng;
-        const float sA = h16_to_f32(sm[rA * ng + Gabs]) * S::Q, sB = h16_to_f32(sm[rB * ng + Gabs]) * S::Q;
-        const float bA = h16_to_f32(bm[rA * ng + Gabs]) - sA, bB = h16_to_f32(bm[rB * ng + Gabs]) - sB;
+        const uint8_t* cm = codes + (size_t)m * kRowTile * S::ROWB;
 #pragma unroll
-        for (int n = 0; n < NT; ++n) {
-          const float x0 = s_xs[(n * 8 + 2 * t) * xs_ld + Gabs], x1 = s_xs[(n * 8 + 2 * t + 1) * xs_ld + Gabs];
-          y[m][n][0] = fmaf(sA, D[n][0], fmaf(bA, x0, y[m][n][0]));
-          y[m][n][1] = fmaf(sA, D[n][1], fmaf(bA, x1, y[m][n][1]));
-          y[m][n][2] = fmaf(sB, D[n][2], fmaf(bB, x0, y[m][n][2]));
-          y[m][n][3] = fmaf(sB, D[n][3], fmaf(bB, x1, y[m][n][3]));
+        for (int G = 0; G < S::GPS; ++G) {
+          const float sA = h16_to_f32(hsA[G]) * kQ, sB = h16_to_f32(hsB[G]) * kQ;
+          qmv_group<BITS, MODE>(cm, blk[G], G, rA, rB, t, sA, sB, h16_to_f32(hbA[G]) - sA,
+                                h16_to_f32(hbB[G]) - sB, xa[G], xb[G], y[m]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int G = 0; G < S::GPS; ++G) {
+        if (G < gvalid) {
+          const int Gabs = g0 + G;
+          const uint4 blk[2] = {*reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t) ^ g) << 4)),
+                                *reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t + 1) ^ g) << 4))};
+          const float x0 = s_xs[(2 * t) * xp + Gabs], x1 = s_xs[(2 * t + 1) * xp + Gabs];
+#pragma unroll
+          for (int m = 0; m < S::NMAT; ++m) {
+            const uint16_t* ms = s_sb + (size_t)m * 2 * kRowTile * sp;
+            const uint16_t* mb = ms + (size_t)kRowTile * sp;
+            const float sA = h16_to_f32(ms[rA * sp + Gabs]) * kQ, sB = h16_to_f32(ms[rB * sp + Gabs]) * kQ;
+            const float bA = h16_to_f32(mb[rA * sp + Gabs]) - sA, bB = h16_to_f32(mb[rB * sp + Gabs]) - sB;
+            qmv_group<BITS, MODE>(codes + (size_t)m * kRowTile * S::ROWB, blk, G, rA, rB, t, sA, sB, bA, bB, x0,
+                                  x1, y[m]);
+          }
         }
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (lane == 0) mbar_arrive(&sm.empty[slot_i]);
   }
   __syncwarp();
-  if (lane == 0) mbar_arrive(sb_empty);
+  if (lane == 0) mbar_arrive(&sm.sb_empty[q]);  // slot may be reloaded
 
   const int row0 = it.rt * kRowTile;
+  const int R = p.R;
   if constexpr (MODE == 0) {
-    // h = silu(g) * u -> fp16 staging [32][64] in pair order
+    // h = silu(g) * u -> fp16 staging [8][64] in the activation layout
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = (i < 2) ? rA : rB;
-        const int tok = n * 8 + 2 * t + (i & 1);
-        const float gv = y[0][n][i], uv = y[1][n][i];
-        const float h = gv / (1.0f + expf(-gv)) * uv;
-        s_h[tok * kRowTile + (r & ~7) + pair_pos(r & 7)] = f32_to_h16_sat(h);
-      }
-    // all four warps' h values staged (bounded mbarrier sync, not bar.sync)
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&epi[0]);
-    if (!mbar_wait(&epi[0], item & 1u, kDevErrTimeoutFull)) return false;
-    const int R = p.R;
+    for (int i = 0; i < 4; ++i) {
+      const int r = (i < 2) ? rA : rB;
+      const int tok = 2 * t + (i & 1);
+      const float gv = y[0][i], uv = y[1][i];
+      const float h = gv / (1.0f + expf(-gv)) * uv;
+      sm.s_h[tok * kRowTile + (r & ~7) + act_pos(r & 7, BITS)] = f32_to_h16_sat(h);
+    }
+    if (!warps_sync(&sm.sync[0], item & 1u)) return false;
     for (int c = threadIdx.x; c < it.nrows * 8; c += kComputeWarps * 32) {
       const int tok = c >> 3, part = c & 7;
-      const uint4 v = reinterpret_cast<const uint4*>(s_h + tok * kRowTile)[part];
+      const uint4 v = reinterpret_cast<const uint4*>(sm.s_h + tok * kRowTile)[part];
       reinterpret_cast<uint4*>(p.h_out + (size_t)(it.row0_seg + tok) * R + row0)[part] = v;
     }
-    if (threadIdx.x < it.nrows) {
+    if ((int)threadIdx.x < it.nrows) {
       const int tok = threadIdx.x;
       float s = 0.0f;
-      for (int c = 0; c < kRowTile; ++c) s += h16_to_f32(s_h[tok * kRowTile + c]);
+      for (int c = 0; c < kRowTile; ++c) s += h16_to_f32(sm.s_h[tok * kRowTile + c]);
       p.hsum_out[(size_t)(it.row0_seg + tok) * sum_ld(R) + it.rt] = s;
     }
-    // staging buffer free again before the next item writes it
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&epi[1]);
-    if (!mbar_wait(&epi[1], item & 1u, kDevErrTimeoutFull)) return false;
+    if (!warps_sync(&sm.sync[1], item & 1u)) return false;  // staging free for the next item
   } else {
-    const int R = p.R;
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = (i < 2) ? rA : rB;
-        const int tok = n * 8 + 2 * t + (i & 1);
-        if (tok < it.nrows) p.y_out[(size_t)(it.row0_seg + tok) * R + row0 + r] = y[0][n][i];
-      }
+    for (int i = 0; i < 4; ++i) {
+      const int r = (i < 2) ? rA : rB;
+      const int tok = 2 * t + (i & 1);
+      if (tok < it.nrows) p.y_out[(size_t)(it.row0_seg + tok) * R + row0 + r] = y[0][i];
+    }
   }
   return true;
 }
 
 template <int BITS, int MODE>
-__global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_constant__ QmvParams p) {
+__global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_constant__ QmvParams p) {
   using S = QmvShape<BITS, MODE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int ns = p.n_stages;
   const int ng = p.K / 64;
-  uint8_t* stage_base = smem;
-  uint16_t* s_sb = reinterpret_cast<uint16_t*>(stage_base + (size_t)kStages * S::STAGE_BYTES);
-  const int xs_ld = sum_ld(p.K);
-  float* s_xs = reinterpret_cast<float*>(s_sb + (size_t)S::NMAT * 2 * kRowTile * ng);
-  uint16_t* s_h = reinterpret_cast<uint16_t*>(s_xs + (size_t)kTokChunk * xs_ld);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_h + (size_t)kTokChunk * kRowTile);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + kStages;
-  uint64_t* sb_full = bars + 2 * kStages;
-  uint64_t* sb_empty = sb_full + 1;
-  uint64_t* epi = sb_full + 2;  // two epilogue syncs among the compute warps
+  QmvSmem sm;
+  sm.stage_base = smem;
+  sm.slot_base = sm.stage_base + (size_t)ns * S::STAGE_BYTES;
+  sm.s_h = reinterpret_cast<uint16_t*>(sm.slot_base + 2 * qmv_slot_bytes<BITS, MODE>(p.K));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm.s_h + (size_t)kTokChunk * kRowTile);
+  sm.full = bars;
+  sm.empty = bars + ns;
+  sm.sb_full = bars + 2 * ns;
+  sm.sb_empty = sm.sb_full + 2;
+  sm.sync = sm.sb_full + 4;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kComputeWarps);
+    for (int i = 0; i < ns; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], kComputeWarps);
     }
-    mbar_init(sb_full, 1);
-    mbar_init(sb_empty, kComputeWarps);
-    mbar_init(&epi[0], kComputeWarps);
-    mbar_init(&epi[1], kComputeWarps);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.sb_full[i], 1);
+      mbar_init(&sm.sb_empty[i], kComputeWarps);
+      mbar_init(&sm.sync[i], kComputeWarps);
+    }
     mbar_fence_init();
   }
   __syncthreads();
@@ -263,95 +343,136 @@ __global__ void __launch_bounds__(kQmvThreads, 1) qmv_kernel(const __grid_consta
   const int n_work = (*p.n_seg) * n_rt;
   const int nstages = (p.K + S::KT - 1) / S::KT;
 
-  if (warp == kComputeWarps) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tmap(&p.tm_w0);
-      if (MODE == 0) prefetch_tmap(&p.tm_w1);
-      uint32_t fill_it = 0, item = 0;
-      bool ok = true;
-      for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x, ++item) {
-        const WorkItem it = decode_work(p, w, n_rt);
-        const bool shared = it.expert >= p.n_experts;
-        const size_t rowg = (size_t)(shared ? 0 : it.expert) * p.R + (size_t)it.rt * kRowTile;
-        // scales / biases / group sums for this item
-        if (item > 0 && !mbar_wait(sb_empty, (item - 1) & 1u, kDevErrTimeoutScales)) { ok = false; break; }
-        const uint32_t sb_bytes = (uint32_t)(kRowTile * ng * 2);
-        const uint32_t xs_bytes = (uint32_t)(xs_ld * 4);
-        mbar_arrive_expect_tx(sb_full, S::NMAT * 2 * sb_bytes + it.nrows * xs_bytes);
-        const uint16_t* src_s0 = shared ? p.ss0 : p.s0;
-        const uint16_t* src_b0 = shared ? p.sb0 : p.b0;
-        bulk_load(s_sb, src_s0 + rowg * ng, sb_bytes, sb_full);
-        bulk_load(s_sb + kRowTile * ng, src_b0 + rowg * ng, sb_bytes, sb_full);
-        if (MODE == 0) {
-          const uint16_t* src_s1 = shared ? p.ss1 : p.s1;
-          const uint16_t* src_b1 = shared ? p.sb1 : p.b1;
-          bulk_load(s_sb + 2 * kRowTile * ng, src_s1 + rowg * ng, sb_bytes, sb_full);
-          bulk_load(s_sb + 3 * kRowTile * ng, src_b1 + rowg * ng, sb_bytes, sb_full);
+  if (warp == kTmaWarp) {
+    if (lane != 0) return;
+    // ---------------------------------------------------- stage ring (codes + activation rows)
+    prefetch_tmap(&p.tm_w0);
+    if (MODE == 0) prefetch_tmap(&p.tm_w1);
+    prefetch_tmap(&p.tm_act);
+    uint32_t fill_it = 0;
+    bool ok = true;
+    int w = blockIdx.x;
+    WorkItem nxt = w < n_work ? decode_work(p, w, n_rt) : WorkItem{0, 0, 0, 0};
+    for (; w < n_work && ok; w += gridDim.x) {
+      const WorkItem it = nxt;
+      if (w + (int)gridDim.x < n_work) nxt = decode_work(p, w + gridDim.x, n_rt);
+      const bool shared = it.expert >= p.n_experts;
+      const int rowg = (shared ? 0 : it.expert) * p.R + it.rt * kRowTile;
+      const CUtensorMap* m0 = shared ? &p.tm_sw0 : &p.tm_w0;
+      const CUtensorMap* m1 = shared ? &p.tm_sw1 : &p.tm_w1;
+      for (int st = 0; st < nstages; ++st, ++fill_it) {
+        const int slot = fill_it % ns;
+        if (fill_it >= (uint32_t)ns && !mbar_wait(&sm.empty[slot], ((fill_it / ns) - 1) & 1u, kDevErrTimeoutEmpty)) {
+          ok = false;
+          break;
         }
-        for (int r = 0; r < it.nrows; ++r) {
-          const int src_row = p.row_src ? p.row_src[it.row0_seg + r] : it.row0_seg + r;
-          bulk_load(s_xs + r * xs_ld, p.act_sum + (size_t)src_row * xs_ld, xs_bytes, sb_full);
-        }
-        const CUtensorMap* m0 = shared ? &p.tm_sw0 : &p.tm_w0;
-        const CUtensorMap* m1 = shared ? &p.tm_sw1 : &p.tm_w1;
-        for (int st = 0; st < nstages; ++st, ++fill_it) {
-          const int slot = fill_it % kStages;
-          if (fill_it >= (uint32_t)kStages &&
-              !mbar_wait(&empty[slot], ((fill_it / kStages) - 1) & 1u, kDevErrTimeoutEmpty)) {
-            ok = false;
-            break;
-          }
-          uint8_t* dst = stage_base + (size_t)slot * S::STAGE_BYTES;
-          const int kcols = min(S::KT, p.K - st * S::KT);  // partial last stage: TMA zero-fills codes
-          mbar_arrive_expect_tx(&full[slot], S::CODE_BYTES + it.nrows * kcols * 2);
-          const int kw = st * (S::KT * BITS / 32);
-          tma_load_2d(dst, m0, kw, (int)rowg, &full[slot]);
-          if (MODE == 0) tma_load_2d(dst + kRowTile * S::ROWB, m1, kw, (int)rowg, &full[slot]);
-          uint8_t* adst = dst + S::CODE_BYTES;
-          for (int r = 0; r < it.nrows; ++r) {
-            const int src_row = p.row_src ? p.row_src[it.row0_seg + r] : it.row0_seg + r;
-            bulk_load(adst + r * S::ACT_PITCH, p.act + (size_t)src_row * p.K + (size_t)st * S::KT, kcols * 2,
-                      &full[slot]);
-          }
-        }
+        uint8_t* dst = sm.stage_base + (size_t)slot * S::STAGE_BYTES;
+        // partial last stage: the code box past the row end is zero-filled by TMA
+        const int gv = min(S::GPS, ng - st * S::GPS);
+        mbar_arrive_expect_tx(&sm.full[slot], S::CODE_BYTES + gv * S::ACT_BOX);
+        const int kw = st * (S::KT * BITS / 32);
+        tma_load_2d(dst, m0, kw, rowg, &sm.full[slot]);
+        if (MODE == 0) tma_load_2d(dst + kRowTile * S::ROWB, m1, kw, rowg, &sm.full[slot]);
+        uint8_t* adst = dst + S::CODE_BYTES;
+        for (int G = 0; G < gv; ++G)
+          tma_load_2d(adst + G * S::ACT_BOX, &p.tm_act, st * S::KT + 64 * G, it.row0_seg, &sm.full[slot]);
       }
-      // drain: wait (bounded) for the copies this thread issued last
-      const uint32_t n_issued = fill_it;
-      for (uint32_t i = (n_issued > (uint32_t)kStages ? n_issued - kStages : 0); i < n_issued; ++i)
-        mbar_wait(&full[i % kStages], (i / kStages) & 1u, kDevErrTimeoutFull);
     }
+    // drain: wait (bounded) for the copies issued last
+    for (uint32_t i = (fill_it > (uint32_t)ns ? fill_it - ns : 0); i < fill_it; ++i)
+      mbar_wait(&sm.full[i % ns], (i / ns) & 1u, kDevErrTimeoutFull);
     return;
   }
-  // -------------------------------------------------------------- consumers
-  uint32_t fill_it = 0, item = 0;
-  for (int w = blockIdx.x; w < n_work; w += gridDim.x, ++item) {
-    const WorkItem it = decode_work(p, w, n_rt);
-    if (!mbar_wait(sb_full, item & 1u, kDevErrTimeoutScales)) return;
-    const int nt = (it.nrows + 7) >> 3;
-    bool ok;
-    switch (nt) {
-      case 1: ok = qmv_consume<BITS, MODE, 1>(p, it, stage_base, s_sb, s_xs, s_h, full, empty, sb_empty, epi, item, fill_it); break;
-      case 2: ok = qmv_consume<BITS, MODE, 2>(p, it, stage_base, s_sb, s_xs, s_h, full, empty, sb_empty, epi, item, fill_it); break;
-      case 3: ok = qmv_consume<BITS, MODE, 3>(p, it, stage_base, s_sb, s_xs, s_h, full, empty, sb_empty, epi, item, fill_it); break;
-      default: ok = qmv_consume<BITS, MODE, 4>(p, it, stage_base, s_sb, s_xs, s_h, full, empty, sb_empty, epi, item, fill_it); break;
+  if (warp == kScaleWarp) {
+    if (lane != 0) return;
+    // ---------------------------------------------------- per-item scales/biases and group sums
+    const int xs_ld = sum_ld(p.K), sp = sb_pitch(p.K);
+    uint32_t item = 0;
+    int w = blockIdx.x;
+    WorkItem nxt = w < n_work ? decode_work(p, w, n_rt) : WorkItem{0, 0, 0, 0};
+    for (; w < n_work; w += gridDim.x, ++item) {
+      const WorkItem it = nxt;
+      if (w + (int)gridDim.x < n_work) nxt = decode_work(p, w + gridDim.x, n_rt);
+      const bool shared = it.expert >= p.n_experts;
+      const size_t rowg = (size_t)(shared ? 0 : it.expert) * p.R + (size_t)it.rt * kRowTile;
+      const int q = item & 1;
+      if (item >= 2 && !mbar_wait(&sm.sb_empty[q], ((item >> 1) - 1) & 1u, kDevErrTimeoutScales)) break;
+      uint8_t* slot = sm.slot_base + (size_t)q * qmv_slot_bytes<BITS, MODE>(p.K);
+      uint16_t* s_sb = reinterpret_cast<uint16_t*>(slot);
+      float* s_xs = reinterpret_cast<float*>(slot + (qmv_sb_bytes<BITS, MODE>(p.K) + 127) / 128 * 128);
+      const uint32_t row_bytes = (uint32_t)(ng * 2);
+      const uint32_t xs_bytes = (uint32_t)(it.nrows * xs_ld * 4);
+      mbar_arrive_expect_tx(&sm.sb_full[q], S::NMAT * 2 * kRowTile * row_bytes + xs_bytes);
+      const uint16_t* srcs[4] = {shared ? p.ss0 : p.s0, shared ? p.sb0 : p.b0, shared ? p.ss1 : p.s1,
+                                 shared ? p.sb1 : p.b1};
+#pragma unroll
+      for (int a = 0; a < 2 * S::NMAT; ++a) {
+        const uint16_t* gsrc = srcs[a] + rowg * ng;
+        uint16_t* dst = s_sb + (size_t)a * kRowTile * sp;
+        bulk_load(dst, gsrc, kRowTile * row_bytes, &sm.sb_full[q]);
+      }
+      bulk_load(s_xs, p.act_sum + (size_t)it.row0_seg * xs_ld, xs_bytes, &sm.sb_full[q]);
     }
-    if (!ok) return;
+    if (item > 0) mbar_wait(&sm.sb_full[(item - 1) & 1], ((item - 1) >> 1) & 1u, kDevErrTimeoutScales);
+    return;
   }
+  // -------------------------------------------------------------- compute warps
+  uint32_t fill_base = 0, item = 0;
+  int w = blockIdx.x;
+  WorkItem nxt = w < n_work ? decode_work(p, w, n_rt) : WorkItem{0, 0, 0, 0};
+  for (; w < n_work; w += gridDim.x, ++item) {
+    const WorkItem it = nxt;
+    if (w + (int)gridDim.x < n_work) nxt = decode_work(p, w + gridDim.x, n_rt);
+    const int q = item & 1;
+    if (!mbar_wait(&sm.sb_full[q], (item >> 1) & 1u, kDevErrTimeoutScales)) return;
+    if (!qmv_item<BITS, MODE>(p, it, sm, q, item, fill_base, ns)) return;
+    fill_base += nstages;
+  }
+}
+
+// Ring depth and CTAs per SM: two CTAs per SM with >= 3 stages each when they
+// fit in half of the shared memory, else one CTA with the deepest ring.
+template <int BITS, int MODE>
+static int qmv_pick(int K, int* ctas_per_sm) {
+  if (K > 16384) return 0;
+  for (int ns = 6; ns >= 3; --ns)
+    if (qmv_smem_bytes<BITS, MODE>(K, ns) <= 113 * 1024) { *ctas_per_sm = 2; return ns; }
+  for (int ns = 6; ns >= 2; --ns)
+    if (qmv_smem_bytes<BITS, MODE>(K, ns) <= 227 * 1024) { *ctas_per_sm = 1; return ns; }
+  return 0;
 }
 
 template <int BITS, int MODE>
-static cudaError_t launch_qmv_t(const QmvParams& p, int n_sm, cudaStream_t st) {
-  size_t smem = qmv_smem_bytes<BITS, MODE>(p.K);
-  cudaError_t e = cudaFuncSetAttribute(qmv_kernel<BITS, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  qmv_kernel<BITS, MODE><<<n_sm, kQmvThreads, smem, st>>>(p);
+static cudaError_t launch_qmv_t(const QmvParams& p_in, int n_sm, cudaStream_t st) {
+  QmvParams p = p_in;
+  int per_sm = 1;
+  p.n_stages = qmv_pick<BITS, MODE>(p.K, &per_sm);
+  if (p.n_stages == 0) return cudaErrorInvalidValue;
+  const size_t smem = qmv_smem_bytes<BITS, MODE>(p.K, p.n_stages);
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(qmv_kernel<BITS, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         227 * 1024);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  qmv_kernel<BITS, MODE><<<n_sm * per_sm, kQmvThreads, smem, st>>>(p);
   return cudaGetLastError();
 }
 
+// SIZE_MAX when the decode kernel cannot hold a K-wide item in shared memory.
 size_t qmv_smem_required(int bits, int mode, int K) {
-  if (bits == 4) return mode == 0 ? qmv_smem_bytes<4, 0>(K) : qmv_smem_bytes<4, 1>(K);
-  return mode == 0 ? qmv_smem_bytes<8, 0>(K) : qmv_smem_bytes<8, 1>(K);
+  int per = 1, ns;
+  if (bits == 4) {
+    ns = mode == 0 ? qmv_pick<4, 0>(K, &per) : qmv_pick<4, 1>(K, &per);
+    if (!ns) return ~size_t(0);
+    return mode == 0 ? qmv_smem_bytes<4, 0>(K, ns) : qmv_smem_bytes<4, 1>(K, ns);
+  }
+  ns = mode == 0 ? qmv_pick<8, 0>(K, &per) : qmv_pick<8, 1>(K, &per);
+  if (!ns) return ~size_t(0);
+  return mode == 0 ? qmv_smem_bytes<8, 0>(K, ns) : qmv_smem_bytes<8, 1>(K, ns);
 }
 
 cudaError_t launch_qmv(int bits, int mode, const QmvParams& p, int n_sm, cudaStream_t st) {

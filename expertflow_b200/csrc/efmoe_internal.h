@@ -8,11 +8,9 @@ namespace ef {
 
 // ---- quantised grouped GEMV (decode path) ----
 constexpr int kRowTile = 64;        // weight rows per work item (4 warps x 16 rows)
-constexpr int kTokChunk = 32;       // rows (tokens) per segment: up to 4 n-tiles of 8
-constexpr int kStages = 4;          // TMA pipeline depth
-constexpr int kComputeWarps = 4;
-constexpr int kQmvThreads = (kComputeWarps + 1) * 32;
-constexpr int kActPad = 16;         // bytes of padding per staged activation row
+constexpr int kTokChunk = 8;        // rows (tokens) per segment: one n-tile of 8
+constexpr int kComputeWarps = 4;    // 4 x 16 rows
+constexpr int kQmvThreads = (kComputeWarps + 2) * 32;  // + TMA producer warp + scale producer warp
 
 // Row stride (floats) of the per-64-column group sums of a K-wide activation:
 // padded to 4 groups so that every row is a whole number of 16-byte units.
@@ -42,6 +40,10 @@ struct QmvParams {
   CUtensorMap tm_w1;    // routed codes: up (mode 0)
   CUtensorMap tm_sw0;   // shared expert codes
   CUtensorMap tm_sw1;
+  const uint32_t* w0;   // raw code pointers of the four maps (for L2 prefetch of whole items)
+  const uint32_t* w1;
+  const uint32_t* sw0;
+  const uint32_t* sw1;
   const uint16_t* s0;   // routed scales/biases [E*R, K/64]
   const uint16_t* b0;
   const uint16_t* s1;
@@ -50,9 +52,9 @@ struct QmvParams {
   const uint16_t* sb0;
   const uint16_t* ss1;
   const uint16_t* sb1;
-  const uint16_t* act;      // pair-ordered fp16 activation rows [*, K]
-  const float* act_sum;     // [*, K/64] group sums of act
-  const int* row_src;       // mode 0: act row of sorted row j; mode 1: nullptr (identity)
+  CUtensorMap tm_act;       // fp16 activation rows [n_rows, K] in routed-row order and the GEMV
+                            // layout (act_pos); 2-D, box 64 columns x 8 rows, 128-byte swizzle
+  const float* act_sum;     // [n_rows, sum_ld(K)] group sums of the activation rows
   const int* seg_expert;
   const int* seg_row0;
   const int* seg_nrows;
@@ -63,6 +65,7 @@ struct QmvParams {
   uint16_t* h_out;          // mode 0: fp16 pair-ordered [n_rows, R]
   float* hsum_out;          // mode 0: [n_rows, R/64]
   float* y_out;             // mode 1: fp32 [n_rows, R]
+  int n_stages;             // TMA ring depth (set by the launcher)
 };
 
 }  // namespace ef
