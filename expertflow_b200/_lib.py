@@ -80,6 +80,7 @@ SIGNATURES = {
     "ef_trace_read": (_I, [_P, _I]),
     "ef_moe_workspace_size": (_SZ, [_CFGP, _I]),
     "ef_moe_forward": (_I, [_CFGP, _P, _I, _P, _P, _QW, _QW, _QW, _QWP, _QWP, _QWP, _P, _P, _P, _P, _SZ, _P]),
+    "ef_moe_forward_noalloc": (_I, [_CFGP, _P, _I, _P, _P, _QW, _QW, _QW, _QWP, _QWP, _QWP, _P, _P, _P, _P]),
     "ef_router_workspace_size": (_SZ, [_CFGP, _I]),
     "ef_router_topk": (_I, [_CFGP, _P, _I, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "ef_experts_workspace_size": (_SZ, [_CFGP, _I]),

@@ -5,3 +5,4 @@
 #include "ef_dequant.cu"
 #include "ef_qmv.cu"
 #include "ef_api.cu"
+#include "ef_noalloc.cu"

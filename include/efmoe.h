@@ -119,6 +119,22 @@ ef_status ef_moe_forward(const ef_moe_cfg* cfg, const void* x, int T, const void
                          const ef_qweight* shared_up, const ef_qweight* shared_down, void* y, int32_t* inds_out,
                          float* wts_out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Same as ef_moe_forward, for callers that cannot allocate device memory (an
+ * FFI host without a CUDA allocator of its own, or a decode loop that must not
+ * call cudaMalloc): no workspace argument; the scratch is a fixed array of
+ * EF_NOALLOC_SCRATCH_BYTES held in device memory by every GPU that loads the
+ * library.  Returns EF_ERR_WORKSPACE when ef_moe_workspace_size(cfg, T) is
+ * larger.  The first call on each device resolves the array's address (make
+ * it before any stream capture).  All calls share the array: calls that
+ * overlap on the GPU race and must be serialised by the caller.
+ * No counterpart in the reference. */
+#define EF_NOALLOC_SCRATCH_BYTES (64u << 20)
+ef_status ef_moe_forward_noalloc(const ef_moe_cfg* cfg, const void* x, int T, const void* gate_w,
+                                 const float* e_bias, ef_qweight gate, ef_qweight up, ef_qweight down,
+                                 const ef_qweight* shared_gate, const ef_qweight* shared_up,
+                                 const ef_qweight* shared_down, void* y, int32_t* inds_out, float* wts_out,
+                                 void* stream);
+
 /* ---- router ----------------------------------------------------------- */
 /* inds [T, k] int32 in rank order, weights [T, k] fp32.  Replaces
  * moe_module.gate(x) + argpartition/take_along_axis/softmax, ef_engine.py:609-619. */
