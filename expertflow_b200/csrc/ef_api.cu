@@ -28,6 +28,8 @@ cudaError_t launch_combine(const float* rows, const int* inv, const float* wts, 
                            void* out, int out_dtype, cudaStream_t st);
 cudaError_t launch_qmv(int bits, int mode, const QmvParams& p, int n_sm, cudaStream_t st);
 size_t qmv_smem_required(int bits, int mode, int K);
+cudaError_t launch_qgemm(int bits, int mode, const GemmParams& p, int n_sm, cudaStream_t st);
+size_t qgemm_smem_required(int bits);
 cudaError_t launch_dequantize(const uint32_t* w, const uint16_t* s, const uint16_t* b, int rows, int cols, int bits,
                               void* out, int out_dtype, cudaStream_t st);
 }  // namespace ef
@@ -146,6 +148,37 @@ ef_status encode_act_map(CUtensorMap* m, const uint16_t* act, long long rows, in
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(EF_ERR_INVALID, "activation tensor map encode failed (%d)", (int)r);
+  return EF_OK;
+}
+
+// Code tiles for the grouped GEMM: box (chunk of 64 columns) x box_rows rows,
+// swizzle matching the 64-byte (8-bit) / 32-byte (4-bit) row chunk.
+ef_status encode_gemm_codes_map(CUtensorMap* m, const uint32_t* w, long long rows, int words, int bits, int box_rows) {
+  PFN_encodeTiled_t enc = get_encoder();
+  if (!enc) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)words, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)words * 4};
+  cuuint32_t box[2] = {(cuuint32_t)(64 * bits / 32), (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(w), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, bits == 8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(EF_ERR_INVALID, "GEMM code tensor map encode failed (%d)", (int)r);
+  return EF_OK;
+}
+
+// Activation rows for the grouped GEMM: box 64 columns x 128 rows, 128-B swizzle.
+ef_status encode_gemm_act_map(CUtensorMap* m, const uint16_t* act, long long rows, int K) {
+  PFN_encodeTiled_t enc = get_encoder();
+  if (!enc) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(act), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(EF_ERR_INVALID, "GEMM activation tensor map encode failed (%d)", (int)r);
   return EF_OK;
 }
 
@@ -288,6 +321,56 @@ ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, const e
   p1.y_out = f.yrows;
   EF_LAUNCH("qmv_down", launch_qmv(bits, 1, p1, nsm, st));
   return EF_OK;
+}
+
+// Grouped-GEMM (tcgen05) version of run_experts; segments of <= 128 rows.
+ef_status run_experts_gemm(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, const ef_qweight& gate,
+                           const ef_qweight& up, const ef_qweight& down, const ef_qweight* sg, const ef_qweight* su,
+                           const ef_qweight* sd, cudaStream_t st) {
+  const int H = c->hidden, I = c->inter, E = c->n_experts, bits = c->bits;
+  const int nsm = sm_count();
+  ef_status s;
+  GemmParams g0;
+  memset(&g0, 0, sizeof(g0));
+  if ((s = encode_gemm_codes_map(&g0.tm_c0, gate.w, (long long)E * I, H * bits / 32, bits, 64))) return s;
+  if ((s = encode_gemm_codes_map(&g0.tm_c1, up.w, (long long)E * I, H * bits / 32, bits, 64))) return s;
+  if (sg) {
+    if ((s = encode_gemm_codes_map(&g0.tm_sc0, sg->w, I, H * bits / 32, bits, 64))) return s;
+    if ((s = encode_gemm_codes_map(&g0.tm_sc1, su->w, I, H * bits / 32, bits, 64))) return s;
+    g0.ss0 = sg->scales; g0.sb0 = sg->biases; g0.ss1 = su->scales; g0.sb1 = su->biases;
+  } else {
+    g0.tm_sc0 = g0.tm_c0; g0.tm_sc1 = g0.tm_c1;
+    g0.ss0 = gate.scales; g0.sb0 = gate.biases; g0.ss1 = up.scales; g0.sb1 = up.biases;
+  }
+  g0.s0 = gate.scales; g0.b0 = gate.biases; g0.s1 = up.scales; g0.b1 = up.biases;
+  if ((s = encode_gemm_act_map(&g0.tm_act, f.x16, n_rows, H))) return s;
+  g0.seg_expert = f.pb.seg_expert; g0.seg_row0 = f.pb.seg_row0; g0.seg_nrows = f.pb.seg_nrows; g0.n_seg = f.pb.n_seg;
+  g0.K = H; g0.R = I; g0.n_experts = E; g0.h_out = f.h16;
+  EF_LAUNCH("qgemm_gate_up", launch_qgemm(bits, 0, g0, nsm, st));
+  GemmParams g1;
+  memset(&g1, 0, sizeof(g1));
+  if ((s = encode_gemm_codes_map(&g1.tm_c0, down.w, (long long)E * H, I * bits / 32, bits, 128))) return s;
+  if (sd) {
+    if ((s = encode_gemm_codes_map(&g1.tm_sc0, sd->w, H, I * bits / 32, bits, 128))) return s;
+    g1.ss0 = sd->scales; g1.sb0 = sd->biases;
+  } else {
+    g1.tm_sc0 = g1.tm_c0; g1.ss0 = down.scales; g1.sb0 = down.biases;
+  }
+  g1.tm_c1 = g1.tm_c0; g1.tm_sc1 = g1.tm_sc0;
+  g1.s0 = down.scales; g1.b0 = down.biases;
+  if ((s = encode_gemm_act_map(&g1.tm_act, f.h16, n_rows, I))) return s;
+  g1.seg_expert = f.pb.seg_expert; g1.seg_row0 = f.pb.seg_row0; g1.seg_nrows = f.pb.seg_nrows; g1.n_seg = f.pb.n_seg;
+  g1.K = I; g1.R = H; g1.n_experts = E; g1.y_out = f.yrows;
+  EF_LAUNCH("qgemm_down", launch_qgemm(bits, 1, g1, nsm, st));
+  return EF_OK;
+}
+
+// Grouped GEMM for many tokens per expert, decode GEMV otherwise.
+bool use_gemm(const ef_moe_cfg* c, int n_rows, int n_ent) {
+  if (c->hidden % 128 != 0 || n_rows < 128) return false;
+  if (c->path == EF_PATH_GEMM) return true;
+  if (c->path == EF_PATH_GEMV) return false;
+  return (long long)n_ent >= 32LL * c->n_experts;  // >= 32 routed rows per expert on average
 }
 
 size_t smem_check(int bits, int H, int I) {
@@ -444,12 +527,18 @@ ef_status ef_moe_forward(const ef_moe_cfg* cfg, const void* x, int T, const void
                                cfg->router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg->routed_scaling : 1.0f, inds, wts,
                                st));
   const int n_sh = cfg->n_shared ? T : 0;
-  EF_LAUNCH("permute", launch_permute(inds, T * k, k, E, n_sh, kTokChunk, f.pb, st));
+  const bool gemm = use_gemm(cfg, T * k + n_sh, T * k);
+  EF_LAUNCH("permute", launch_permute(inds, T * k, k, E, n_sh, gemm ? 128 : kTokChunk, f.pb, st));
   EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), f.pb.row_src, bf, T * k + n_sh, H, cfg->bits,
                                         f.x16, f.xsum, st));
-  if ((s = run_experts(cfg, f, T * k + n_sh, gate, up, down, cfg->n_shared ? sg : nullptr,
-                       cfg->n_shared ? su : nullptr, cfg->n_shared ? sd : nullptr, st)))
+  if (gemm) {
+    if ((s = run_experts_gemm(cfg, f, T * k + n_sh, gate, up, down, cfg->n_shared ? sg : nullptr,
+                              cfg->n_shared ? su : nullptr, cfg->n_shared ? sd : nullptr, st)))
+      return s;
+  } else if ((s = run_experts(cfg, f, T * k + n_sh, gate, up, down, cfg->n_shared ? sg : nullptr,
+                              cfg->n_shared ? su : nullptr, cfg->n_shared ? sd : nullptr, st))) {
     return s;
+  }
   // shared rows start at offsets[E] == T*k
   EF_LAUNCH("combine", launch_combine(f.yrows, f.pb.inv, wts, T, k, H, cfg->n_shared ? T * k : -1, y,
                          cfg->out_f32 ? EF_DT_F32 : (bf ? EF_DT_BF16 : EF_DT_F16), st));
@@ -482,10 +571,15 @@ ef_status ef_moe_experts_forward(const ef_moe_cfg* cfg, const void* x_rows, int 
   FfnBufs f;
   carve_ffn(c, N, cfg->n_experts + 1, N, cfg->hidden, cfg->inter, f);
   const bool bf = cfg->act_dtype == EF_DT_BF16;
-  EF_LAUNCH("permute", launch_permute(row_expert, N, 1, cfg->n_experts, 0, kTokChunk, f.pb, st));
+  const bool gemm = use_gemm(cfg, N, N);
+  EF_LAUNCH("permute", launch_permute(row_expert, N, 1, cfg->n_experts, 0, gemm ? 128 : kTokChunk, f.pb, st));
   EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x_rows), f.pb.row_src, bf, N, cfg->hidden,
                                         cfg->bits, f.x16, f.xsum, st));
-  if ((s = run_experts(cfg, f, N, gate, up, down, nullptr, nullptr, nullptr, st))) return s;
+  if (gemm) {
+    if ((s = run_experts_gemm(cfg, f, N, gate, up, down, nullptr, nullptr, nullptr, st))) return s;
+  } else if ((s = run_experts(cfg, f, N, gate, up, down, nullptr, nullptr, nullptr, st))) {
+    return s;
+  }
   EF_LAUNCH("combine", launch_combine(f.yrows, f.pb.inv, nullptr, N, 1, cfg->hidden, -1, y_rows, EF_DT_F32, st));
   return EF_OK;
 }

@@ -4,5 +4,6 @@
 #include "ef_router.cu"
 #include "ef_dequant.cu"
 #include "ef_qmv.cu"
+#include "ef_qgemm.cu"
 #include "ef_api.cu"
 #include "ef_noalloc.cu"

@@ -265,3 +265,55 @@ def test_empty_and_single_token_edges():
     assert (inds.cpu().numpy() == np.arange(spec.top_k)[None]).all()
     m.gate.weight = gate
     assert torch.isfinite(y.float()).all()
+
+
+# ---------------------------------------------------------------- grouped GEMM (tcgen05) path
+@pytest.mark.parametrize("bits,shared,T", [(4, False, 160), (8, False, 128), (4, True, 200), (8, True, 300)])
+def test_gemm_path_matches_oracle(bits, shared, T):
+    moe = _moe()
+    from expertflow_b200 import _lib as L
+
+    spec = MoESpec(hidden=1024, n_experts=16, top_k=4, inter=256, bits=bits, router="sigmoid_group" if shared else
+                   "softmax", n_group=4 if shared else 1, topk_group=2 if shared else 1,
+                   routed_scaling=2.5 if shared else 1.0, n_shared=1 if shared else 0, act_dtype="bfloat16",
+                   e_bias_std=0.01)
+    layer = synthetic.make_layer_np(spec, 31 + bits)
+    xb = synthetic.make_x_np(spec, T, 7)
+    x = _x_tensor(xb, spec)
+    out = {}
+    for path in (L.EF_PATH_GEMM, L.EF_PATH_GEMV):
+        m = moe.MoELayer.from_arrays(spec, layer, path=path)
+        inds = torch.empty((T, spec.top_k), dtype=torch.int32, device="cuda")
+        out[path] = (m(x, inds_out=inds, out_dtype=torch.float32), inds)
+    torch.cuda.synchronize()
+    i_ref, w_ref, y_ref = O.moe_forward(xb, True, layer["gate_w"].view(np.uint16), False, _spec_router(spec),
+                                        layer["e_bias"], layer["gate"], layer["up"], layer["down"], bits, 64,
+                                        layer["shared"])
+    for path, (y, inds) in out.items():
+        np.testing.assert_array_equal(inds.cpu().numpy(), i_ref)
+        assert_ffn_close(y.cpu().numpy(), y_ref, what=f"path {path}")
+
+
+def test_prefill_deepseek_v3_8bit_sampled():
+    """DeepSeek-V3-shaped prefill: 4096 tokens, 8-bit, grouped GEMM path."""
+    moe = _moe()
+    from expertflow_b200 import _lib as L
+
+    spec = DEEPSEEK_V3_PREFILL_8BIT
+    T = 4096
+    layer = _torch_layer(spec, seed=41)
+    m = moe.MoELayer.from_arrays(spec, layer, path=L.EF_PATH_GEMM)
+    x = synthetic.make_x_torch(spec, T, seed=9)
+    inds = torch.empty((T, spec.top_k), dtype=torch.int32, device="cuda")
+    wts = torch.empty((T, spec.top_k), dtype=torch.float32, device="cuda")
+    y = m(x, inds_out=inds, wts_out=wts, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    xb = _bits_of(x)
+    lg = O.c_router_logits(xb, True, layer["gate_w"].cpu().numpy().view(np.uint16), False)
+    i_ref, w_ref = O.route(lg, _spec_router(spec), layer["e_bias"].cpu().numpy())
+    np.testing.assert_array_equal(inds.cpu().numpy(), i_ref)
+    tokens = np.array([0, 1, 777, 2048, 4094, 4095])
+    y_ref = _oracle_sampled(spec, layer, xb, i_ref, w_ref, tokens)
+    assert_ffn_close(y.cpu().numpy()[tokens], y_ref, what="prefill 8-bit")
+    del m, layer
+    torch.cuda.empty_cache()
