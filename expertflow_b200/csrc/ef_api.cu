@@ -167,13 +167,13 @@ ef_status encode_gemm_codes_map(CUtensorMap* m, const uint32_t* w, long long row
   return EF_OK;
 }
 
-// Activation rows for the grouped GEMM: box 64 columns x 128 rows, 128-B swizzle.
+// Activation rows for the grouped GEMM: box 64 columns x 32 rows, 128-B swizzle.
 ef_status encode_gemm_act_map(CUtensorMap* m, const uint16_t* act, long long rows, int K) {
   PFN_encodeTiled_t enc = get_encoder();
   if (!enc) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, 32};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(act), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -323,7 +323,7 @@ ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, const e
   return EF_OK;
 }
 
-// Grouped-GEMM (tcgen05) version of run_experts; segments of <= 128 rows.
+// Grouped-GEMM (tcgen05) version of run_experts; segments of <= kGemmSegRows rows.
 ef_status run_experts_gemm(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, const ef_qweight& gate,
                            const ef_qweight& up, const ef_qweight& down, const ef_qweight* sg, const ef_qweight* su,
                            const ef_qweight* sd, cudaStream_t st) {
@@ -332,11 +332,11 @@ ef_status run_experts_gemm(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, co
   ef_status s;
   GemmParams g0;
   memset(&g0, 0, sizeof(g0));
-  if ((s = encode_gemm_codes_map(&g0.tm_c0, gate.w, (long long)E * I, H * bits / 32, bits, 64))) return s;
-  if ((s = encode_gemm_codes_map(&g0.tm_c1, up.w, (long long)E * I, H * bits / 32, bits, 64))) return s;
+  if ((s = encode_gemm_codes_map(&g0.tm_c0, gate.w, (long long)E * I, H * bits / 32, bits, 128))) return s;
+  if ((s = encode_gemm_codes_map(&g0.tm_c1, up.w, (long long)E * I, H * bits / 32, bits, 128))) return s;
   if (sg) {
-    if ((s = encode_gemm_codes_map(&g0.tm_sc0, sg->w, I, H * bits / 32, bits, 64))) return s;
-    if ((s = encode_gemm_codes_map(&g0.tm_sc1, su->w, I, H * bits / 32, bits, 64))) return s;
+    if ((s = encode_gemm_codes_map(&g0.tm_sc0, sg->w, I, H * bits / 32, bits, 128))) return s;
+    if ((s = encode_gemm_codes_map(&g0.tm_sc1, su->w, I, H * bits / 32, bits, 128))) return s;
     g0.ss0 = sg->scales; g0.sb0 = sg->biases; g0.ss1 = su->scales; g0.sb1 = su->biases;
   } else {
     g0.tm_sc0 = g0.tm_c0; g0.tm_sc1 = g0.tm_c1;
@@ -367,7 +367,8 @@ ef_status run_experts_gemm(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, co
 
 // Grouped GEMM for many tokens per expert, decode GEMV otherwise.
 bool use_gemm(const ef_moe_cfg* c, int n_rows, int n_ent) {
-  if (c->hidden % 128 != 0 || n_rows < 128) return false;
+  // code boxes are 128 rows tall: both projections need at least that many rows
+  if (n_rows < 128 || c->inter < 128 || c->hidden < 128) return false;
   if (c->path == EF_PATH_GEMM) return true;
   if (c->path == EF_PATH_GEMV) return false;
   return (long long)n_ent >= 32LL * c->n_experts;  // >= 32 routed rows per expert on average
@@ -528,7 +529,7 @@ ef_status ef_moe_forward(const ef_moe_cfg* cfg, const void* x, int T, const void
                                st));
   const int n_sh = cfg->n_shared ? T : 0;
   const bool gemm = use_gemm(cfg, T * k + n_sh, T * k);
-  EF_LAUNCH("permute", launch_permute(inds, T * k, k, E, n_sh, gemm ? 128 : kTokChunk, f.pb, st));
+  EF_LAUNCH("permute", launch_permute(inds, T * k, k, E, n_sh, gemm ? kGemmSegRows : kTokChunk, f.pb, st));
   EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), f.pb.row_src, bf, T * k + n_sh, H, cfg->bits,
                                         f.x16, f.xsum, st));
   if (gemm) {
@@ -572,7 +573,7 @@ ef_status ef_moe_experts_forward(const ef_moe_cfg* cfg, const void* x_rows, int 
   carve_ffn(c, N, cfg->n_experts + 1, N, cfg->hidden, cfg->inter, f);
   const bool bf = cfg->act_dtype == EF_DT_BF16;
   const bool gemm = use_gemm(cfg, N, N);
-  EF_LAUNCH("permute", launch_permute(row_expert, N, 1, cfg->n_experts, 0, gemm ? 128 : kTokChunk, f.pb, st));
+  EF_LAUNCH("permute", launch_permute(row_expert, N, 1, cfg->n_experts, 0, gemm ? kGemmSegRows : kTokChunk, f.pb, st));
   EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x_rows), f.pb.row_src, bf, N, cfg->hidden,
                                         cfg->bits, f.x16, f.xsum, st));
   if (gemm) {

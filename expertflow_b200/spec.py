@@ -88,10 +88,14 @@ DEEPSEEK_V3 = MoESpec(hidden=7168, n_experts=256, top_k=8, inter=2048, bits=4, r
                       norm_topk=True, n_group=8, topk_group=4, routed_scaling=2.5, n_shared=1,
                       act_dtype="bfloat16", e_bias_std=0.01)
 DEEPSEEK_V3_PREFILL_8BIT = DEEPSEEK_V3.with_(bits=8, gate_std=0.002)
+# The same expert shapes with 32 experts (8 groups of 4): a 1.5 GB layer for
+# profiling the prefill kernels on a small case.
+DEEPSEEK_V3_8BIT_E32 = DEEPSEEK_V3_PREFILL_8BIT.with_(n_experts=32)
 
 WORKLOADS = {
     "mixtral-small-h1024-e16": MIXTRAL_SMALL,
     "qwen3-30b-a3b-moe": QWEN3_30B_A3B,
     "deepseek-v3-moe": DEEPSEEK_V3,
     "deepseek-v3-moe-8bit": DEEPSEEK_V3_PREFILL_8BIT,
+    "deepseek-v3-moe-8bit-e32": DEEPSEEK_V3_8BIT_E32,
 }

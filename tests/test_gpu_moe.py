@@ -268,12 +268,16 @@ def test_empty_and_single_token_edges():
 
 
 # ---------------------------------------------------------------- grouped GEMM (tcgen05) path
-@pytest.mark.parametrize("bits,shared,T", [(4, False, 160), (8, False, 128), (4, True, 200), (8, True, 300)])
-def test_gemm_path_matches_oracle(bits, shared, T):
+@pytest.mark.parametrize("bits,shared,T,H,I", [(4, False, 160, 1024, 256), (8, False, 128, 1024, 256),
+                                               (4, True, 200, 1024, 256), (8, True, 300, 1024, 256),
+                                               # partial weight tiles (I % 128, H % 256 != 0) and experts
+                                               # with more rows than one segment holds
+                                               (8, True, 900, 1152, 192), (4, False, 1000, 1088, 320)])
+def test_gemm_path_matches_oracle(bits, shared, T, H, I):
     moe = _moe()
     from expertflow_b200 import _lib as L
 
-    spec = MoESpec(hidden=1024, n_experts=16, top_k=4, inter=256, bits=bits, router="sigmoid_group" if shared else
+    spec = MoESpec(hidden=H, n_experts=16, top_k=4, inter=I, bits=bits, router="sigmoid_group" if shared else
                    "softmax", n_group=4 if shared else 1, topk_group=2 if shared else 1,
                    routed_scaling=2.5 if shared else 1.0, n_shared=1 if shared else 0, act_dtype="bfloat16",
                    e_bias_std=0.01)
