@@ -12,17 +12,18 @@
 // SwiGLU pair lands in the same TMEM lane of the two accumulators.  The
 // dequantised weights never touch shared memory: they are written to TMEM and
 // consumed there as the UMMA A operand (tcgen05.mma ... [d], [a_tmem], b_desc).
-// One persistent CTA per SM, 15 warps:
+// One persistent CTA per SM, 19 warps:
 //   warp 0      TMA: code tiles (2 x 128 rows x one 64-column group, swizzled)
 //               into a code ring; prefetches code tiles 8 chunks ahead into L2
-//   warp 14     TMA: activation rows of the segment (32-row boxes, 128-B
+//   warp 18     TMA: activation rows of the segment (32-row boxes, 128-B
 //               swizzle = the UMMA K-major canonical layout) into an act ring
 //   warp 1      TMEM allocation (512 columns); lane 0 issues tcgen05.mma
 //               (M=128, N = segment rows rounded to 16, K=16) and commits
 //   warps 2-9   dequantise one weight row each: codes -> exact fp16 q
 //               (mantissa trick + one fp16 FMA) -> fp16 s*q + b (one fp16 FMA,
 //               single rounding) -> tcgen05.st into the A tile of its lane
-//   warps 10-13 epilogue: tcgen05.ld of both accumulators; gate/up pass:
+//   warps 10-17 epilogue (two per TMEM lane quarter, alternate 32-column
+//               blocks): tcgen05.ld of both accumulators; gate/up pass:
 //               h = silu(g) * u -> fp16 rows; down pass: fp32 rows
 // TMEM columns: accumulator 0 [0, 192), accumulator 1 [192, 384), A tiles
 // [384, 512) = 2 buffers x 2 tiles x 32 columns (64 fp16 per lane).
@@ -34,27 +35,51 @@
 
 namespace ef {
 
+// Pipeline depths (compile-time; the TMEM and shared-memory budgets are checked below)
+#ifndef EF_GEMM_ABUFS
+#define EF_GEMM_ABUFS 2
+#endif
+#ifndef EF_GEMM_EPI_WARPS
+#define EF_GEMM_EPI_WARPS 8
+#endif
+#ifndef EF_GEMM_CSTAGES8
+#define EF_GEMM_CSTAGES8 6
+#endif
+#ifndef EF_GEMM_ASTAGES8
+#define EF_GEMM_ASTAGES8 4
+#endif
+#ifndef EF_GEMM_CSTAGES4
+#define EF_GEMM_CSTAGES4 8
+#endif
+#ifndef EF_GEMM_ASTAGES4
+#define EF_GEMM_ASTAGES4 5
+#endif
 constexpr int kGemmTileM = 128;             // rows per UMMA tile
 constexpr int kGemmItemRows = 256;          // weight rows per work item (two tiles)
-constexpr int kGemmNMax = kGemmSegRows;     // routed rows per segment (UMMA N <= 192)
+constexpr int kGemmNMax = kGemmSegRows;     // routed rows per segment (UMMA N)
 constexpr int kGemmKC = 64;                 // K columns per chunk (one quantisation group)
 constexpr int kActBoxRows = 32;             // activation TMA box height
-constexpr int kGemmABufs = 2;               // A tiles in TMEM (double buffer)
+constexpr int kGemmABufs = EF_GEMM_ABUFS;   // A tile pairs in TMEM
 constexpr int kGemmPrefetch = 8;            // code tiles prefetched into L2 ahead of the ring
 constexpr int kGemmDqWarps = 8;
-constexpr int kGemmThreads = 15 * 32;
+constexpr int kGemmEpiWarps = EF_GEMM_EPI_WARPS;  // 4 or 8 (one or two per TMEM lane quarter)
+constexpr int kGemmEpiWarp0 = 2 + kGemmDqWarps;
+constexpr int kGemmActWarp = kGemmEpiWarp0 + kGemmEpiWarps;
+constexpr int kGemmThreads = (kGemmActWarp + 1) * 32;
 constexpr int kTmemCols = 512;
 constexpr int kAccCols = kGemmNMax;         // columns per accumulator
 constexpr int kAColBase = 2 * kAccCols;     // first A-tile column
+static_assert(kGemmNMax % 32 == 0 && kGemmNMax <= 256, "segment rows: whole activation boxes, UMMA N <= 256");
 static_assert(kAColBase + kGemmABufs * 2 * (kGemmKC / 2) <= kTmemCols, "TMEM budget");
+static_assert(kGemmEpiWarps == 4 || kGemmEpiWarps == 8, "epilogue warps");
 
 template <int BITS>
 struct GemmShape {
   static constexpr int CROW = kGemmKC * BITS / 8;               // code bytes per row per chunk (64 / 32)
   static constexpr int CODE_BYTES = kGemmItemRows * CROW;        // 16 KB / 8 KB
-  static constexpr int CODE_STAGES = BITS == 8 ? 6 : 8;
-  static constexpr int ACT_BYTES = kGemmNMax * kGemmKC * 2;      // 24 KB fp16
-  static constexpr int ACT_STAGES = BITS == 8 ? 4 : 5;
+  static constexpr int CODE_STAGES = BITS == 8 ? EF_GEMM_CSTAGES8 : EF_GEMM_CSTAGES4;
+  static constexpr int ACT_BYTES = kGemmNMax * kGemmKC * 2;      // fp16 rows x 128 B
+  static constexpr int ACT_STAGES = BITS == 8 ? EF_GEMM_ASTAGES8 : EF_GEMM_ASTAGES4;
   static constexpr int ACT_BASE = CODE_STAGES * CODE_BYTES;      // 1024-aligned
   static constexpr int BAR_BASE = ACT_BASE + ACT_STAGES * ACT_BYTES;
 };
@@ -62,6 +87,7 @@ struct GemmShape {
 constexpr size_t gemm_smem_bytes(int bits) {
   return 1024 + (size_t)(bits == 4 ? GemmShape<4>::BAR_BASE : GemmShape<8>::BAR_BASE) + 512;
 }
+static_assert(gemm_smem_bytes(8) <= 232448 && gemm_smem_bytes(4) <= 232448, "shared memory budget");
 
 struct GemmParams {
   CUtensorMap tm_c0, tm_c1;    // routed codes (gate/up or down), 2-D [E*R, K*bits/32], box 128 rows
@@ -106,11 +132,14 @@ EF_DEV void umma_commit(uint64_t* bar) {
 }
 EF_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 EF_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-EF_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+EF_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
       : "memory");
 }
@@ -187,15 +216,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* codes = smem;                       // [CS][256 rows][CROW], swizzled
-  uint8_t* acts = smem + S::ACT_BASE;          // [AS][192 rows][128 B], 128-B swizzle
+  uint8_t* acts = smem + S::ACT_BASE;          // [AS][kGemmNMax rows][128 B], 128-B swizzle
   uint64_t* cfull = reinterpret_cast<uint64_t*>(smem + S::BAR_BASE);  // [CS] code tile landed
   uint64_t* cfree = cfull + CS;                // [CS] code tile consumed (8 dequant warps)
   uint64_t* bfull = cfree + CS;                // [AS] activation tile landed
   uint64_t* bfree = bfull + AS;                // [AS] MMAs reading it done (commit)
-  uint64_t* aready = bfree + AS;               // [2] A tiles written to TMEM (8 dequant warps)
-  uint64_t* afree = aready + kGemmABufs;       // [2] MMAs reading them done (commit)
+  uint64_t* aready = bfree + AS;               // [ABUFS] A tiles written to TMEM (8 dequant warps)
+  uint64_t* afree = aready + kGemmABufs;       // [ABUFS] MMAs reading them done (commit)
   uint64_t* accf = afree + kGemmABufs;         // accumulators complete (commit)
-  uint64_t* acce = accf + 1;                   // accumulators drained (4 epilogue warps)
+  uint64_t* acce = accf + 1;                   // accumulators drained (epilogue warps)
   uint64_t* drain = acce + 1;                  // final MMA drain
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
@@ -214,7 +243,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
       mbar_init(&afree[i], 1);
     }
     mbar_init(accf, 1);
-    mbar_init(acce, 4);
+    mbar_init(acce, kGemmEpiWarps);
     mbar_init(drain, 1);
     mbar_fence_init();
   }
@@ -273,7 +302,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
       for (uint32_t i = (f > (uint32_t)CS ? f - CS : 0); i < f; ++i)
         mbar_wait(&cfull[i % CS], (i / CS) & 1u, kDevErrTimeoutFull);
     }
-  } else if (warp == 14) {
+  } else if (warp == kGemmActWarp) {
     // ------------------------------------------------------------------ activation tiles
     if (lane == 0) {
       prefetch_tmap(&p.tm_act);
@@ -451,9 +480,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
         }
       }
     }
-  } else {
-    // ------------------------------------------------------------------ epilogue (warps 10-13)
-    const int quarter = warp & 3;          // TMEM lane quarter this warp may access
+  } else if (warp < kGemmActWarp) {
+    // ------------------------------------------------------------------ epilogue
+    // Warp (quarter, half): TMEM lane quarter warp % 4; with 8 epilogue warps the
+    // two warps of a quarter take alternate 32-column blocks.
+    const int quarter = warp & 3;
+    const int half = kGemmEpiWarps == 8 ? (warp - kGemmEpiWarp0) >> 2 : 0;
+    constexpr int kColStep = 32 * (kGemmEpiWarps / 4);
     const int lr = quarter * 32 + lane;    // accumulator row (= TMEM lane)
     const uint32_t t_lane = tmem_base + ((uint32_t)(quarter * 32) << 16);
     uint32_t item = 0;
@@ -462,18 +495,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
       const GemmItem it = gemm_item(p, w, n_rt);
       if (!mbar_wait(accf, item & 1u, kDevErrTimeoutTc)) { ok = false; break; }
       tc_fence_after();
-      const int ncols = (it.nrows + 15) & ~15;
       if constexpr (MODE == 1) {
         const int o0 = it.rt * kGemmItemRows + lr, o1 = o0 + kGemmTileM;
         float* yrow = p.y_out + (size_t)it.row0_seg * p.R;
-        for (int c0 = 0; c0 < ncols; c0 += 16) {
-          uint32_t r0[16], r1[16];
-          tmem_ld16(t_lane + c0, r0);
-          tmem_ld16(t_lane + kAccCols + c0, r1);
+        for (int c0 = half * 32; c0 < it.nrows; c0 += kColStep) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(t_lane + c0, r0);
+          tmem_ld32(t_lane + kAccCols + c0, r1);
           tmem_wait_ld();
+          const int nc = min(32, it.nrows - c0);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (c0 + j < it.nrows) {
+          for (int j = 0; j < 32; ++j) {
+            if (j < nc) {
               if (o0 < p.R) yrow[(size_t)(c0 + j) * p.R + o0] = __uint_as_float(r0[j]);
               if (o1 < p.R) yrow[(size_t)(c0 + j) * p.R + o1] = __uint_as_float(r1[j]);
             }
@@ -485,14 +518,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
         const bool valid = orow < p.R;
         const size_t col = (size_t)(orow & ~7) + act_pos(orow & 7, BITS);
         uint16_t* hrow = p.h_out + (size_t)it.row0_seg * p.R + col;
-        for (int c0 = 0; c0 < ncols; c0 += 16) {
-          uint32_t g[16], u[16];
-          tmem_ld16(t_lane + c0, g);
-          tmem_ld16(t_lane + kAccCols + c0, u);
+        for (int c0 = half * 32; c0 < it.nrows; c0 += kColStep) {
+          uint32_t g[32], u[32];
+          tmem_ld32(t_lane + c0, g);
+          tmem_ld32(t_lane + kAccCols + c0, u);
           tmem_wait_ld();
+          const int nc = valid ? min(32, it.nrows - c0) : 0;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (valid && c0 + j < it.nrows) {
+          for (int j = 0; j < 32; ++j) {
+            if (j < nc) {
               const float gv = __uint_as_float(g[j]);
               const float h = gv / (1.0f + expf(-gv)) * __uint_as_float(u[j]);
               hrow[(size_t)(c0 + j) * p.R] = f32_to_h16_sat(h);

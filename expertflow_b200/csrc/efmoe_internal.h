@@ -9,7 +9,10 @@ namespace ef {
 // ---- quantised grouped GEMV (decode path) ----
 constexpr int kRowTile = 64;        // weight rows per work item (4 warps x 16 rows)
 constexpr int kTokChunk = 8;        // rows (tokens) per segment: one n-tile of 8
-constexpr int kGemmSegRows = 192;   // rows (tokens) per segment of the grouped GEMM (UMMA N)
+#ifndef EF_GEMM_NMAX
+#define EF_GEMM_NMAX 192
+#endif
+constexpr int kGemmSegRows = EF_GEMM_NMAX;  // rows (tokens) per segment of the grouped GEMM (UMMA N)
 constexpr int kComputeWarps = 4;    // 4 x 16 rows
 constexpr int kQmvThreads = (kComputeWarps + 2) * 32;  // + TMA producer warp + scale producer warp
 
