@@ -63,6 +63,23 @@ class MoECfg(ctypes.Structure):
     ]
 
 
+class PoolCfg(ctypes.Structure):
+    _fields_ = [("n_layers", ctypes.c_int), ("budget", ctypes.c_int), ("headroom", ctypes.c_int),
+                ("policy", ctypes.c_int), ("decay", ctypes.c_double)]
+
+
+class PoolStats(ctypes.Structure):
+    _fields_ = [("accesses", ctypes.c_longlong), ("hits", ctypes.c_longlong), ("misses", ctypes.c_longlong),
+                ("copies_sync", ctypes.c_longlong), ("copies_prefetch", ctypes.c_longlong),
+                ("prefetch_used", ctypes.c_longlong), ("evictions", ctypes.c_longlong),
+                ("tokens", ctypes.c_longlong), ("h2d_bytes", ctypes.c_double), ("copy_ms", ctypes.c_double)]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+EF_POLICY_FREQ, EF_POLICY_LRU = 0, 1
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _SZ = ctypes.c_size_t
@@ -90,6 +107,22 @@ SIGNATURES = {
     "ef_dequantize": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _P]),
     "ef_gather_qmm_workspace_size": (_SZ, [_I, _I, _I, _I, _I]),
     "ef_gather_qmm": (_I, [_P, _I, _I, _P, _I, _QW, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
+    "ef_policy_create": (_I, [_I, _I, ctypes.c_double, _P]),
+    "ef_policy_get": (_I, [_P, ctypes.c_longlong]),
+    "ef_policy_put": (None, [_P, ctypes.c_longlong]),
+    "ef_policy_trim": (_I, [_P, _P, _I]),
+    "ef_policy_size": (_I, [_P]),
+    "ef_policy_keys": (_I, [_P, _P, _I]),
+    "ef_policy_score": (ctypes.c_double, [_P, ctypes.c_longlong]),
+    "ef_policy_destroy": (None, [_P]),
+    "ef_pool_create": (_I, [_CFGP, ctypes.POINTER(PoolCfg), _QWP, _QWP, _QWP, _P]),
+    "ef_pool_workspace_size": (_SZ, [_P, _I]),
+    "ef_pool_moe_forward": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ, _P]),
+    "ef_pool_end_token": (_I, [_P]),
+    "ef_pool_resident": (_I, [_P, _I, _P, _I, ctypes.POINTER(_I)]),
+    "ef_pool_get_stats": (_I, [_P, ctypes.POINTER(PoolStats)]),
+    "ef_pool_reset_stats": (_I, [_P]),
+    "ef_pool_destroy": (_I, [_P]),
 }
 
 _lib = None

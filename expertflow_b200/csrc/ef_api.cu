@@ -470,6 +470,33 @@ ef_status ef_router_topk(const ef_moe_cfg* cfg, const void* x, int T, const void
   return EF_OK;
 }
 
+// permute -> gather -> experts -> weighted combine for T tokens routed by
+// inds [T, k] (ids in [0, cfg->n_experts)) with weights wts [T, k].
+static ef_status moe_tail(const ef_moe_cfg* cfg, const void* x, int T, const int* inds, const float* wts,
+                          const ef_qweight& gate, const ef_qweight& up, const ef_qweight& down, const ef_qweight* sg,
+                          const ef_qweight* su, const ef_qweight* sd, const FfnBufs& f, void* y, cudaStream_t st) {
+  ef_status s;
+  const int H = cfg->hidden, E = cfg->n_experts, k = cfg->top_k;
+  const bool bf = cfg->act_dtype == EF_DT_BF16;
+  const int n_sh = cfg->n_shared ? T : 0;
+  const bool gemm = use_gemm(cfg, T * k + n_sh, T * k);
+  EF_LAUNCH("permute", launch_permute(inds, T * k, k, E, n_sh, gemm ? kGemmSegRows : kTokChunk, f.pb, st));
+  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), f.pb.row_src, bf, T * k + n_sh, H, cfg->bits,
+                                        f.x16, f.xsum, st));
+  if (gemm) {
+    if ((s = run_experts_gemm(cfg, f, T * k + n_sh, gate, up, down, cfg->n_shared ? sg : nullptr,
+                              cfg->n_shared ? su : nullptr, cfg->n_shared ? sd : nullptr, st)))
+      return s;
+  } else if ((s = run_experts(cfg, f, T * k + n_sh, gate, up, down, cfg->n_shared ? sg : nullptr,
+                              cfg->n_shared ? su : nullptr, cfg->n_shared ? sd : nullptr, st))) {
+    return s;
+  }
+  // shared rows start at offsets[E] == T*k
+  EF_LAUNCH("combine", launch_combine(f.yrows, f.pb.inv, wts, T, k, H, cfg->n_shared ? T * k : -1, y,
+                         cfg->out_f32 ? EF_DT_F32 : (bf ? EF_DT_BF16 : EF_DT_F16), st));
+  return EF_OK;
+}
+
 static size_t moe_ws(const ef_moe_cfg* cfg, int T, Carver& c, float** logits, int** inds, float** wts, FfnBufs* f) {
   const int E = cfg->n_experts, k = cfg->top_k;
   const int n_ent = T * k, n_rows = n_ent + (cfg->n_shared ? T : 0);
@@ -527,23 +554,7 @@ ef_status ef_moe_forward(const ef_moe_cfg* cfg, const void* x, int T, const void
                                cfg->router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg->n_group : 1, cfg->topk_group,
                                cfg->router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg->routed_scaling : 1.0f, inds, wts,
                                st));
-  const int n_sh = cfg->n_shared ? T : 0;
-  const bool gemm = use_gemm(cfg, T * k + n_sh, T * k);
-  EF_LAUNCH("permute", launch_permute(inds, T * k, k, E, n_sh, gemm ? kGemmSegRows : kTokChunk, f.pb, st));
-  EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), f.pb.row_src, bf, T * k + n_sh, H, cfg->bits,
-                                        f.x16, f.xsum, st));
-  if (gemm) {
-    if ((s = run_experts_gemm(cfg, f, T * k + n_sh, gate, up, down, cfg->n_shared ? sg : nullptr,
-                              cfg->n_shared ? su : nullptr, cfg->n_shared ? sd : nullptr, st)))
-      return s;
-  } else if ((s = run_experts(cfg, f, T * k + n_sh, gate, up, down, cfg->n_shared ? sg : nullptr,
-                              cfg->n_shared ? su : nullptr, cfg->n_shared ? sd : nullptr, st))) {
-    return s;
-  }
-  // shared rows start at offsets[E] == T*k
-  EF_LAUNCH("combine", launch_combine(f.yrows, f.pb.inv, wts, T, k, H, cfg->n_shared ? T * k : -1, y,
-                         cfg->out_f32 ? EF_DT_F32 : (bf ? EF_DT_BF16 : EF_DT_F16), st));
-  return EF_OK;
+  return moe_tail(cfg, x, T, inds, wts, gate, up, down, sg, su, sd, f, y, st);
 }
 
 size_t ef_experts_workspace_size(const ef_moe_cfg* cfg, int N) {

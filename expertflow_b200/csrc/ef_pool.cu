@@ -1,0 +1,613 @@
+// ef_pool.cu -- expert residency for streaming decode.
+//
+// (1) CachePolicy: the reference's FrequencyWeightedCache (ef_engine.py:48-104)
+//     restated over integer keys: get() on a hit adds 1.0 to the key's score,
+//     put() inserts with score + 1.0, trim() evicts the minimum-score key
+//     (first inserted among equal scores, as min() over an insertion-ordered
+//     dict does) until size <= budget and then multiplies every score by the
+//     decay.  Scores are doubles, so the arithmetic is bit-identical to the
+//     Python floats.  An LRU variant evicts the least recently touched key.
+// (2) ef_slot_pool: the expert pool lives in pinned host memory (stacked
+//     [E, ...] per layer, the MLX layout); every layer owns `budget + headroom`
+//     HBM slots.  A layer forward routes, copies the weights of non-resident
+//     experts into free slots on the pool's copy stream (cudaMemcpyAsync, one
+//     per array), makes the compute stream wait for them, and runs the experts
+//     on slot ids.  The optional next-layer gate predicts the next layer's
+//     experts from the current input (experiments/ef_v16_prefetch.py:92-113)
+//     and their copies start before this layer's expert kernels, so they
+//     overlap compute.  trim() runs once per token (ef_pool_end_token), as the
+//     reference trims after each token; the headroom slots hold the token's
+//     misses until then.
+#include <algorithm>
+#include <unordered_map>
+#include <vector>
+
+namespace ef {
+
+class CachePolicy {
+ public:
+  CachePolicy(int kind, int budget, double decay) : kind_(kind), budget_(budget), decay_(decay) {}
+
+  bool get(long long key) {
+    auto it = ents_.find(key);
+    if (it == ents_.end()) return false;
+    it->second.score += 1.0;
+    it->second.last = ++clock_;
+    return true;
+  }
+  void put(long long key) {
+    auto it = ents_.find(key);
+    if (it != ents_.end()) {  // a put of a resident key only refreshes it (the dict keeps its place)
+      it->second.score += 1.0;
+      it->second.last = ++clock_;
+      return;
+    }
+    Ent e;
+    e.score = 1.0;
+    e.seq = ++seq_;
+    e.last = ++clock_;
+    ents_.emplace(key, e);
+  }
+  bool contains(long long key) const { return ents_.count(key) != 0; }
+  int size() const { return (int)ents_.size(); }
+  // Evicts down to the budget, then decays (FREQ); returns the evicted keys in order.
+  std::vector<long long> trim() {
+    std::vector<long long> out;
+    while ((int)ents_.size() > budget_) {
+      auto victim = ents_.begin();
+      for (auto it = ents_.begin(); it != ents_.end(); ++it) {
+        if (kind_ == EF_POLICY_LRU) {
+          if (it->second.last < victim->second.last) victim = it;
+        } else if (it->second.score < victim->second.score ||
+                   (it->second.score == victim->second.score && it->second.seq < victim->second.seq)) {
+          victim = it;
+        }
+      }
+      out.push_back(victim->first);
+      ents_.erase(victim);
+    }
+    if (kind_ == EF_POLICY_FREQ)
+      for (auto& kv : ents_) kv.second.score *= decay_;
+    return out;
+  }
+  // Resident keys, ascending.
+  std::vector<long long> keys() const {
+    std::vector<long long> k;
+    k.reserve(ents_.size());
+    for (const auto& kv : ents_) k.push_back(kv.first);
+    std::sort(k.begin(), k.end());
+    return k;
+  }
+  double score(long long key) const {
+    auto it = ents_.find(key);
+    return it == ents_.end() ? 0.0 : it->second.score;
+  }
+  // Lowest-priority resident key not in `keep` (or -1): the victim an
+  // immediate eviction would take.
+  long long victim_excluding(const std::vector<char>& keep) const {
+    long long best = -1;
+    const Ent* be = nullptr;
+    for (const auto& kv : ents_) {
+      if (kv.first >= 0 && kv.first < (long long)keep.size() && keep[kv.first]) continue;
+      const Ent& e = kv.second;
+      bool better;
+      if (!be) better = true;
+      else if (kind_ == EF_POLICY_LRU) better = e.last < be->last;
+      else better = e.score < be->score || (e.score == be->score && e.seq < be->seq);
+      if (better) {
+        best = kv.first;
+        be = &e;
+      }
+    }
+    return best;
+  }
+  void erase(long long key) { ents_.erase(key); }
+
+ private:
+  struct Ent {
+    double score;
+    unsigned long long seq;   // insertion order
+    unsigned long long last;  // recency
+  };
+  int kind_, budget_;
+  double decay_;
+  unsigned long long seq_ = 0, clock_ = 0;
+  std::unordered_map<long long, Ent> ents_;
+};
+
+}  // namespace ef
+
+struct ef_cache_policy {
+  ef::CachePolicy p;
+};
+
+// ------------------------------------------------------------------------------ slot pool
+namespace ef {
+
+struct ProjGeom {
+  int rows, words, groups;  // per expert
+  size_t wbytes() const { return (size_t)rows * words * 4; }
+  size_t sbytes() const { return (size_t)rows * groups * 2; }
+};
+
+struct LayerSlots {
+  uint8_t* base = nullptr;                 // device, n_slots experts (9 arrays each)
+  std::vector<int> slot_expert;            // -1: free
+  std::vector<int> expert_slot;            // -1: not in HBM
+  std::vector<char> staged;                // copied by the lookahead, not yet in the policy
+  CachePolicy policy;
+  cudaEvent_t ready = nullptr;             // copy stream: after the last copy into this layer
+  cudaEvent_t last_use = nullptr;          // compute stream: after this layer's last expert kernels
+  bool has_ready = false, has_use = false;
+  explicit LayerSlots(int kind, int budget, double decay) : policy(kind, budget, decay) {}
+};
+
+struct CopyTimer {
+  cudaEvent_t a = nullptr, b = nullptr;
+};
+
+}  // namespace ef
+
+struct ef_slot_pool {
+  ef_moe_cfg cfg;
+  ef_pool_cfg pc;
+  int dev = 0;
+  int n_slots = 0;
+  ef::ProjGeom geom[3];                    // gate, up, down
+  size_t expert_bytes = 0;
+  std::vector<ef_qweight> host[3];         // per layer, stacked [E, ...] in pinned host memory
+  std::vector<ef::LayerSlots> layers;
+  uint8_t* dev_mem = nullptr;
+  cudaStream_t copy = nullptr;
+  int32_t* h_inds = nullptr;               // pinned staging: routed ids, predicted ids, slot ids
+  int32_t* h_pred = nullptr;
+  int32_t* h_slot = nullptr;
+  int h_cap = 0;
+  ef_pool_stats st{};
+  std::vector<ef::CopyTimer> timers;       // one per copy batch, folded into st.copy_ms on demand
+  std::vector<ef::CopyTimer> spare;
+};
+
+namespace {
+
+using ef::CopyTimer;
+using ef::LayerSlots;
+
+// device view of slot s of a layer: the 9 arrays at fixed offsets
+struct SlotView {
+  uint8_t* w[3];
+  uint8_t* s[3];
+  uint8_t* b[3];
+};
+SlotView slot_arrays(const ef_slot_pool* P, const LayerSlots& L) {
+  // layout per layer: for each projection, [n_slots] w, then [n_slots] s, then [n_slots] b
+  SlotView v;
+  uint8_t* p = L.base;
+  for (int j = 0; j < 3; ++j) {
+    v.w[j] = p;
+    p += (size_t)P->n_slots * P->geom[j].wbytes();
+    v.s[j] = p;
+    p += (size_t)P->n_slots * P->geom[j].sbytes();
+    v.b[j] = p;
+    p += (size_t)P->n_slots * P->geom[j].sbytes();
+  }
+  return v;
+}
+
+void fold_timers(ef_slot_pool* P, bool all) {
+  size_t keep_from = 0;
+  for (size_t i = 0; i < P->timers.size(); ++i) {
+    CopyTimer& t = P->timers[i];
+    if (!all && cudaEventQuery(t.b) != cudaSuccess) {
+      keep_from = i;
+      break;
+    }
+    if (all) cudaEventSynchronize(t.b);
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, t.a, t.b) == cudaSuccess) P->st.copy_ms += ms;
+    P->spare.push_back(t);
+    keep_from = i + 1;
+  }
+  P->timers.erase(P->timers.begin(), P->timers.begin() + keep_from);
+}
+
+CopyTimer timer_begin(ef_slot_pool* P) {
+  if (P->timers.size() > 256) fold_timers(P, false);
+  CopyTimer t;
+  if (!P->spare.empty()) {
+    t = P->spare.back();
+    P->spare.pop_back();
+  } else {
+    cudaEventCreate(&t.a);
+    cudaEventCreate(&t.b);
+  }
+  cudaEventRecord(t.a, P->copy);
+  return t;
+}
+
+// Copy expert e of layer l into slot s (9 cudaMemcpyAsync on the copy stream).
+ef_status copy_expert(ef_slot_pool* P, int l, int e, int s) {
+  LayerSlots& L = P->layers[l];
+  const SlotView v = slot_arrays(P, L);
+  for (int j = 0; j < 3; ++j) {
+    const ef_qweight& h = P->host[j][l];
+    const ef::ProjGeom& g = P->geom[j];
+    const size_t wb = g.wbytes(), sb = g.sbytes();
+    if (cudaMemcpyAsync(v.w[j] + (size_t)s * wb, reinterpret_cast<const uint8_t*>(h.w) + (size_t)e * wb, wb,
+                        cudaMemcpyHostToDevice, P->copy) != cudaSuccess ||
+        cudaMemcpyAsync(v.s[j] + (size_t)s * sb, reinterpret_cast<const uint8_t*>(h.scales) + (size_t)e * sb, sb,
+                        cudaMemcpyHostToDevice, P->copy) != cudaSuccess ||
+        cudaMemcpyAsync(v.b[j] + (size_t)s * sb, reinterpret_cast<const uint8_t*>(h.biases) + (size_t)e * sb, sb,
+                        cudaMemcpyHostToDevice, P->copy) != cudaSuccess)
+      return fail(EF_ERR_CUDA, "expert copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+  }
+  L.slot_expert[s] = e;
+  L.expert_slot[e] = s;
+  P->st.h2d_bytes += (double)P->expert_bytes;
+  return EF_OK;
+}
+
+// A free slot of layer l, else the slot of a staged (prefetched, unused)
+// expert not in `keep`; -1 when neither exists.
+int take_slot(ef_slot_pool* P, int l, const std::vector<char>& keep) {
+  LayerSlots& L = P->layers[l];
+  for (int s = 0; s < P->n_slots; ++s)
+    if (L.slot_expert[s] < 0) return s;
+  for (int s = 0; s < P->n_slots; ++s) {
+    const int e = L.slot_expert[s];
+    if (L.staged[e] && !keep[e]) {
+      L.staged[e] = 0;
+      L.expert_slot[e] = -1;
+      L.slot_expert[s] = -1;
+      return s;
+    }
+  }
+  return -1;
+}
+
+void copies_begin(ef_slot_pool* P, LayerSlots& L) {
+  // a slot may still be read by the layer's previous expert kernels
+  if (L.has_use) cudaStreamWaitEvent(P->copy, L.last_use, 0);
+}
+
+std::vector<int> distinct_sorted(const int32_t* ids, int n, int E) {
+  std::vector<int> d;
+  d.reserve(n);
+  for (int i = 0; i < n; ++i)
+    if (ids[i] >= 0 && ids[i] < E) d.push_back(ids[i]);
+  std::sort(d.begin(), d.end());
+  d.erase(std::unique(d.begin(), d.end()), d.end());
+  return d;
+}
+
+struct PoolWs {
+  float* logits;
+  int* inds;
+  float* wts;
+  float* plogits;
+  int* pinds;
+  float* pwts;
+  int* slot_inds;
+  FfnBufs f;
+};
+size_t pool_ws(const ef_slot_pool* P, int T, Carver& c, PoolWs& w) {
+  const ef_moe_cfg& cfg = P->cfg;
+  const int E = cfg.n_experts, k = cfg.top_k;
+  const int n_ent = T * k, n_rows = n_ent + (cfg.n_shared ? T : 0);
+  w.logits = c.take<float>((size_t)T * E);
+  w.inds = c.take<int>((size_t)n_ent);
+  w.wts = c.take<float>((size_t)n_ent);
+  w.plogits = c.take<float>((size_t)T * E);
+  w.pinds = c.take<int>((size_t)n_ent);
+  w.pwts = c.take<float>((size_t)n_ent);
+  w.slot_inds = c.take<int>((size_t)n_ent);
+  carve_ffn(c, n_ent, P->n_slots + 1, n_rows, cfg.hidden, cfg.inter, w.f);
+  return c.off;
+}
+
+ef_status pool_route(const ef_moe_cfg& cfg, const void* x, int T, const void* gw, const float* eb, float* logits, int* inds,
+                float* wts, cudaStream_t st) {
+  const bool bf = cfg.act_dtype == EF_DT_BF16;
+  EF_LAUNCH("router_logits", launch_router_logits(static_cast<const uint16_t*>(x), bf, static_cast<const uint16_t*>(gw),
+                                                  cfg.gate_dtype == EF_DT_BF16, T, cfg.n_experts, cfg.hidden, logits, st));
+  EF_LAUNCH("router_select",
+            launch_router_select(logits, eb, T, cfg.n_experts, cfg.top_k, cfg.router_mode, cfg.norm_topk,
+                                 cfg.router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg.n_group : 1, cfg.topk_group,
+                                 cfg.router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg.routed_scaling : 1.0f, inds, wts, st));
+  return EF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+// ---------------------------------------------------------------- policy (host only)
+ef_status ef_policy_create(int kind, int budget, double decay, ef_cache_policy** out) {
+  if (!out) return fail(EF_ERR_INVALID, "out is NULL");
+  *out = nullptr;
+  if (kind != EF_POLICY_FREQ && kind != EF_POLICY_LRU) return fail(EF_ERR_INVALID, "unknown policy %d", kind);
+  if (budget < 0) return fail(EF_ERR_INVALID, "budget < 0");
+  *out = new ef_cache_policy{ef::CachePolicy(kind, budget, decay)};
+  return EF_OK;
+}
+int ef_policy_get(ef_cache_policy* p, long long key) { return p && p->p.get(key) ? 1 : 0; }
+void ef_policy_put(ef_cache_policy* p, long long key) {
+  if (p) p->p.put(key);
+}
+int ef_policy_trim(ef_cache_policy* p, long long* evicted, int cap) {
+  if (!p) return -1;
+  const std::vector<long long> ev = p->p.trim();
+  for (int i = 0; i < (int)ev.size() && i < cap && evicted; ++i) evicted[i] = ev[i];
+  return (int)ev.size();
+}
+int ef_policy_size(const ef_cache_policy* p) { return p ? p->p.size() : -1; }
+int ef_policy_keys(const ef_cache_policy* p, long long* keys, int cap) {
+  if (!p) return -1;
+  const std::vector<long long> k = p->p.keys();
+  for (int i = 0; i < (int)k.size() && i < cap && keys; ++i) keys[i] = k[i];
+  return (int)k.size();
+}
+double ef_policy_score(const ef_cache_policy* p, long long key) { return p ? p->p.score(key) : 0.0; }
+void ef_policy_destroy(ef_cache_policy* p) { delete p; }
+
+// ---------------------------------------------------------------- slot pool
+ef_status ef_pool_create(const ef_moe_cfg* cfg, const ef_pool_cfg* pc, const ef_qweight* host_gate,
+                         const ef_qweight* host_up, const ef_qweight* host_down, ef_slot_pool** out) {
+  if (!out) return fail(EF_ERR_INVALID, "out is NULL");
+  *out = nullptr;
+  ef_status s = check_cfg(cfg);
+  if (s) return s;
+  if (!pc || !host_gate || !host_up || !host_down) return fail(EF_ERR_INVALID, "null pointer");
+  if (pc->n_layers <= 0 || pc->budget < 0 || pc->headroom < cfg->top_k)
+    return fail(EF_ERR_INVALID, "need n_layers > 0, budget >= 0, headroom >= top_k");
+  if (pc->policy != EF_POLICY_FREQ && pc->policy != EF_POLICY_LRU) return fail(EF_ERR_INVALID, "unknown policy");
+  if (cfg->n_shared) return fail(EF_ERR_UNSUPPORTED, "the slot pool streams routed experts only (n_shared = 0)");
+  const int E = cfg->n_experts;
+  const int n_slots = std::min(E, pc->budget + pc->headroom);
+  for (int l = 0; l < pc->n_layers; ++l) {
+    const ef_qweight* qs[3] = {&host_gate[l], &host_up[l], &host_down[l]};
+    for (int j = 0; j < 3; ++j) {
+      if (!qs[j]->w || !qs[j]->scales || !qs[j]->biases) return fail(EF_ERR_INVALID, "layer %d: null host array", l);
+      cudaPointerAttributes a;
+      if (cudaPointerGetAttributes(&a, qs[j]->w) != cudaSuccess || a.type != cudaMemoryTypeHost) {
+        cudaGetLastError();
+        return fail(EF_ERR_INVALID, "layer %d: expert pool arrays must be pinned host memory", l);
+      }
+    }
+  }
+  ef_slot_pool* P = new ef_slot_pool();
+  P->cfg = *cfg;
+  P->pc = *pc;
+  P->n_slots = n_slots;
+  cudaGetDevice(&P->dev);
+  const int H = cfg->hidden, I = cfg->inter, b = cfg->bits;
+  P->geom[0] = {I, H * b / 32, H / 64};
+  P->geom[1] = P->geom[0];
+  P->geom[2] = {H, I * b / 32, I / 64};
+  for (int j = 0; j < 3; ++j) P->expert_bytes += P->geom[j].wbytes() + 2 * P->geom[j].sbytes();
+  for (int j = 0; j < 3; ++j) P->host[j].assign((j == 0 ? host_gate : j == 1 ? host_up : host_down),
+                                                 (j == 0 ? host_gate : j == 1 ? host_up : host_down) + pc->n_layers);
+  const size_t per_layer = (size_t)n_slots * P->expert_bytes;
+  if (cudaMalloc(&P->dev_mem, per_layer * pc->n_layers) != cudaSuccess) {
+    cudaGetLastError();
+    delete P;
+    return fail(EF_ERR_CUDA, "slot pool: cannot allocate %zu bytes of HBM", per_layer * pc->n_layers);
+  }
+  if (cudaStreamCreateWithFlags(&P->copy, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaFree(P->dev_mem);
+    delete P;
+    return fail(EF_ERR_CUDA, "slot pool: stream creation failed");
+  }
+  P->layers.reserve(pc->n_layers);
+  for (int l = 0; l < pc->n_layers; ++l) {
+    P->layers.emplace_back(pc->policy, pc->budget, pc->decay);
+    LayerSlots& L = P->layers.back();
+    L.base = P->dev_mem + per_layer * l;
+    L.slot_expert.assign(n_slots, -1);
+    L.expert_slot.assign(E, -1);
+    L.staged.assign(E, 0);
+    cudaEventCreateWithFlags(&L.ready, cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&L.last_use, cudaEventDisableTiming);
+  }
+  *out = P;
+  return EF_OK;
+}
+
+size_t ef_pool_workspace_size(const ef_slot_pool* P, int T) {
+  if (!P || T < 0) return 0;
+  Carver c{nullptr};
+  PoolWs w;
+  return pool_ws(P, T, c, w) + 256;
+}
+
+ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, const void* gate_w,
+                              const float* e_bias, const void* next_gate_w, const float* next_e_bias, void* y,
+                              int out_f32, int32_t* inds_out, float* wts_out, void* workspace, size_t ws_bytes,
+                              void* stream) {
+  if (!P) return fail(EF_ERR_INVALID, "pool is NULL");
+  if (layer < 0 || layer >= P->pc.n_layers) return fail(EF_ERR_RANGE, "layer %d out of range", layer);
+  if (T < 0) return fail(EF_ERR_INVALID, "T < 0");
+  if (T == 0) return EF_OK;
+  if (!x || !gate_w || !y) return fail(EF_ERR_INVALID, "null pointer");
+  if (!aligned16(x) || !aligned16(gate_w) || !aligned16(y)) return fail(EF_ERR_INVALID, "x/gate_w/y must be 16-byte aligned");
+  if (next_gate_w && layer + 1 >= P->pc.n_layers) return fail(EF_ERR_RANGE, "no layer after %d to predict", layer);
+  if (ws_bytes < ef_pool_workspace_size(P, T) || !workspace) return fail(EF_ERR_WORKSPACE, "workspace too small");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != P->dev) return fail(EF_ERR_INVALID, "pool belongs to device %d, current device is %d", P->dev, dev);
+  const ef_moe_cfg& cfg = P->cfg;
+  const int E = cfg.n_experts, k = cfg.top_k, n = T * k;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver c{static_cast<uint8_t*>(workspace)};
+  PoolWs w;
+  pool_ws(P, T, c, w);
+  ef_status s;
+  int* inds = inds_out ? inds_out : w.inds;
+  float* wts = wts_out ? wts_out : w.wts;
+  // 1. route this layer, and predict the next layer's experts from the same input
+  if ((s = pool_route(cfg, x, T, gate_w, e_bias, w.logits, inds, wts, st))) return s;
+  if (next_gate_w && (s = pool_route(cfg, x, T, next_gate_w, next_e_bias, w.plogits, w.pinds, w.pwts, st))) return s;
+  if (n > P->h_cap) {
+    if (P->h_inds) cudaFreeHost(P->h_inds);
+    P->h_cap = std::max(n, 256);
+    if (cudaMallocHost(&P->h_inds, 3 * sizeof(int32_t) * P->h_cap) != cudaSuccess) {
+      P->h_inds = nullptr;
+      P->h_cap = 0;
+      return fail(EF_ERR_CUDA, "pinned staging allocation failed");
+    }
+  }
+  P->h_pred = P->h_inds + P->h_cap;
+  P->h_slot = P->h_inds + 2 * P->h_cap;
+  cudaMemcpyAsync(P->h_inds, inds, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
+  if (next_gate_w) cudaMemcpyAsync(P->h_pred, w.pinds, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
+  if (cudaStreamSynchronize(st) != cudaSuccess) return fail(EF_ERR_CUDA, "routing failed: %s", cudaGetErrorString(cudaGetLastError()));
+  const std::vector<int> need = distinct_sorted(P->h_inds, n, E);
+  std::vector<char> keep(E, 0);
+  for (int e : need) keep[e] = 1;
+  // 2. lookahead copies for the next layer (overlap this layer's experts)
+  if (next_gate_w) {
+    const int nl = layer + 1;
+    LayerSlots& N = P->layers[nl];
+    const std::vector<int> pred = distinct_sorted(P->h_pred, n, E);
+    std::vector<char> nkeep(E, 0);
+    for (int e : pred) nkeep[e] = 1;
+    bool any = false;
+    CopyTimer t{};
+    for (int e : pred) {
+      if (N.expert_slot[e] >= 0) continue;
+      const int sl = take_slot(P, nl, nkeep);
+      if (sl < 0) break;  // no free slot: the prediction is only a hint
+      if (!any) {
+        copies_begin(P, N);
+        t = timer_begin(P);
+        any = true;
+      }
+      if ((s = copy_expert(P, nl, e, sl))) return s;
+      N.staged[e] = 1;
+      P->st.copies_prefetch++;
+    }
+    if (any) {
+      cudaEventRecord(t.b, P->copy);
+      P->timers.push_back(t);
+      cudaEventRecord(N.ready, P->copy);
+      N.has_ready = true;
+    }
+  }
+  // 3. resolve this layer's experts (ef_engine.py:650-675): policy get, put on a miss
+  LayerSlots& L = P->layers[layer];
+  bool any = false;
+  CopyTimer t{};
+  for (int e : need) {
+    P->st.accesses++;
+    if (L.policy.get(e)) {
+      P->st.hits++;
+      if (L.expert_slot[e] < 0) return fail(EF_ERR_SLOT_MISS, "policy/slot state diverged (layer %d expert %d)", layer, e);
+      continue;
+    }
+    P->st.misses++;
+    L.policy.put(e);
+    if (L.expert_slot[e] >= 0) {  // staged by the lookahead
+      if (L.staged[e]) P->st.prefetch_used++;
+      L.staged[e] = 0;
+      continue;
+    }
+    int sl = take_slot(P, layer, keep);
+    if (sl < 0) {  // full: evict now the lowest-priority resident expert this step does not use
+      const long long v = L.policy.victim_excluding(keep);
+      if (v < 0) return fail(EF_ERR_SLOT_MISS, "layer %d: no slot for expert %d (raise headroom)", layer, e);
+      L.policy.erase(v);
+      sl = L.expert_slot[v];
+      L.expert_slot[v] = -1;
+      L.slot_expert[sl] = -1;
+      P->st.evictions++;
+    }
+    if (!any) {
+      copies_begin(P, L);
+      t = timer_begin(P);
+      any = true;
+    }
+    if ((s = copy_expert(P, layer, e, sl))) return s;
+    P->st.copies_sync++;
+  }
+  if (any) {
+    cudaEventRecord(t.b, P->copy);
+    P->timers.push_back(t);
+    cudaEventRecord(L.ready, P->copy);
+    L.has_ready = true;
+  }
+  if (L.has_ready) cudaStreamWaitEvent(st, L.ready, 0);
+  // 4. experts on slot ids
+  for (int i = 0; i < n; ++i) P->h_slot[i] = L.expert_slot[P->h_inds[i]];
+  cudaMemcpyAsync(w.slot_inds, P->h_slot, sizeof(int32_t) * n, cudaMemcpyHostToDevice, st);
+  ef_moe_cfg sc = cfg;
+  sc.n_experts = P->n_slots;
+  sc.out_f32 = out_f32 ? 1 : 0;
+  const SlotView v = slot_arrays(P, L);
+  const ef_qweight qg{reinterpret_cast<uint32_t*>(v.w[0]), reinterpret_cast<uint16_t*>(v.s[0]), reinterpret_cast<uint16_t*>(v.b[0])};
+  const ef_qweight qu{reinterpret_cast<uint32_t*>(v.w[1]), reinterpret_cast<uint16_t*>(v.s[1]), reinterpret_cast<uint16_t*>(v.b[1])};
+  const ef_qweight qd{reinterpret_cast<uint32_t*>(v.w[2]), reinterpret_cast<uint16_t*>(v.s[2]), reinterpret_cast<uint16_t*>(v.b[2])};
+  if ((s = moe_tail(&sc, x, T, w.slot_inds, wts, qg, qu, qd, nullptr, nullptr, nullptr, w.f, y, st))) return s;
+  cudaEventRecord(L.last_use, st);
+  L.has_use = true;
+  return EF_OK;
+}
+
+ef_status ef_pool_end_token(ef_slot_pool* P) {
+  if (!P) return fail(EF_ERR_INVALID, "pool is NULL");
+  for (auto& L : P->layers) {
+    for (long long e : L.policy.trim()) {
+      const int sl = L.expert_slot[e];
+      if (sl >= 0) L.slot_expert[sl] = -1;
+      L.expert_slot[e] = -1;
+      P->st.evictions++;
+    }
+  }
+  P->st.tokens++;
+  return EF_OK;
+}
+
+ef_status ef_pool_resident(const ef_slot_pool* P, int layer, int32_t* experts, int cap, int* n) {
+  if (!P || !n) return fail(EF_ERR_INVALID, "null pointer");
+  if (layer < 0 || layer >= P->pc.n_layers) return fail(EF_ERR_RANGE, "layer out of range");
+  const std::vector<long long> k = P->layers[layer].policy.keys();
+  *n = (int)k.size();
+  for (int i = 0; i < (int)k.size() && i < cap && experts; ++i) experts[i] = (int32_t)k[i];
+  return EF_OK;
+}
+
+ef_status ef_pool_get_stats(ef_slot_pool* P, ef_pool_stats* out) {
+  if (!P || !out) return fail(EF_ERR_INVALID, "null pointer");
+  cudaStreamSynchronize(P->copy);
+  fold_timers(P, true);
+  *out = P->st;
+  return EF_OK;
+}
+
+ef_status ef_pool_reset_stats(ef_slot_pool* P) {
+  if (!P) return fail(EF_ERR_INVALID, "pool is NULL");
+  cudaStreamSynchronize(P->copy);
+  fold_timers(P, true);
+  P->st = ef_pool_stats{};
+  return EF_OK;
+}
+
+ef_status ef_pool_destroy(ef_slot_pool* P) {
+  if (!P) return EF_OK;
+  cudaStreamSynchronize(P->copy);
+  fold_timers(P, true);
+  for (auto& t : P->spare) {
+    cudaEventDestroy(t.a);
+    cudaEventDestroy(t.b);
+  }
+  for (auto& L : P->layers) {
+    cudaEventDestroy(L.ready);
+    cudaEventDestroy(L.last_use);
+  }
+  cudaStreamDestroy(P->copy);
+  cudaFree(P->dev_mem);
+  if (P->h_inds) cudaFreeHost(P->h_inds);
+  delete P;
+  return EF_OK;
+}
+
+}  // extern "C"

@@ -6,4 +6,5 @@
 #include "ef_qmv.cu"
 #include "ef_qgemm.cu"
 #include "ef_api.cu"
+#include "ef_pool.cu"
 #include "ef_noalloc.cu"

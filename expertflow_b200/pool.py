@@ -1,0 +1,215 @@
+"""Expert residency for streaming decode (the reference's expert cache).
+
+* ``CachePolicy`` -- the reference's ``FrequencyWeightedCache``
+  (ef_engine.py:48-104) over integer keys, via the C ABI (``ef_policy_*``).
+* ``ExpertSlotPool`` -- the experts of many MoE layers in pinned host memory,
+  streamed into HBM slots per layer (``ef_pool_*``); it is the
+  ``expert_cache`` argument of ``streaming_moe_forward``
+  (ef_engine.py:598, :650-675), and it runs the lookahead prediction of
+  experiments/ef_v16_prefetch.py:92-113 (the next layer's gate on the
+  current input) so the predicted experts' copies overlap this layer.
+* ``zipf_layer_bias`` -- per-layer router logit bias log(p) for a shuffled
+  Zipf popularity, the recipe of ef_integrated_engine.py:69-79.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from .moe import MoEGate, _act_dt, _need_cuda, _stream_ptr, workspace
+from .spec import MoESpec
+
+_POLICIES = {"freq": L.EF_POLICY_FREQ, "lru": L.EF_POLICY_LRU}
+
+
+class CachePolicy:
+    """FrequencyWeightedCache(budget, decay) semantics: get / put / trim."""
+
+    def __init__(self, budget: int, decay: float = 0.95, kind: str = "freq"):
+        h = ctypes.c_void_p()
+        L.check(L.lib().ef_policy_create(_POLICIES[kind], budget, decay, ctypes.byref(h)))
+        self._h = h
+
+    def get(self, key: int) -> bool:
+        return bool(L.lib().ef_policy_get(self._h, key))
+
+    def put(self, key: int) -> None:
+        L.lib().ef_policy_put(self._h, key)
+
+    def trim(self) -> list:
+        """Evict down to the budget, decay; returns the evicted keys in eviction order."""
+        cap = max(len(self), 1)
+        buf = (ctypes.c_longlong * cap)()
+        n = L.lib().ef_policy_trim(self._h, ctypes.cast(buf, ctypes.c_void_p), cap)
+        return [int(buf[i]) for i in range(n)]
+
+    def keys(self) -> list:
+        n = L.lib().ef_policy_keys(self._h, None, 0)
+        buf = (ctypes.c_longlong * max(n, 1))()
+        L.lib().ef_policy_keys(self._h, ctypes.cast(buf, ctypes.c_void_p), n)
+        return [int(buf[i]) for i in range(n)]
+
+    def score(self, key: int) -> float:
+        return float(L.lib().ef_policy_score(self._h, key))
+
+    def __len__(self) -> int:
+        return int(L.lib().ef_policy_size(self._h))
+
+    def close(self) -> None:
+        if self._h:
+            L.lib().ef_policy_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def zipf_layer_bias(n_layers: int, n_experts: int, skew: float = 1.1, seed: int = 42) -> np.ndarray:
+    """[n_layers, n_experts] fp32 log-popularity: layer l's Zipf(skew) probabilities
+    permuted by RandomState(seed).permutation per layer, as ef_integrated_engine.py:69-79."""
+    rng = np.random.RandomState(seed)
+    ranks = np.arange(1, n_experts + 1, dtype=np.float64)
+    base = 1.0 / np.power(ranks, skew)
+    out = np.empty((n_layers, n_experts), np.float32)
+    for layer in range(n_layers):
+        p = base[rng.permutation(n_experts)]
+        p /= p.sum()
+        out[layer] = np.log(p).astype(np.float32)
+    return out
+
+
+class StreamedMoELayer:
+    """A MoE layer whose experts live in an ExpertSlotPool: the router (on the
+    device) plus the attributes streaming_moe_forward reads."""
+
+    def __init__(self, gate: MoEGate, layer_idx: int, spec: MoESpec):
+        self.gate = gate
+        self.num_experts_per_tok = gate.top_k
+        self.shared_experts = None
+        self._ef_layer_idx = layer_idx
+        self.spec = spec
+
+
+class ExpertSlotPool:
+    """HBM expert slots over a pinned-host expert pool (see module docstring).
+
+    host_layers: per layer a dict {"gate": (w, s, b), "up": ..., "down": ...}
+    of pinned CPU tensors in the stacked MLX layout ([E, out, in*bits/32]
+    int32 words, [E, out, in/64] fp16 scales and biases).
+    """
+
+    def __init__(self, spec: MoESpec, host_layers: Sequence[dict], budget: int, headroom: Optional[int] = None,
+                 policy: str = "freq", decay: float = 0.95, device=None):
+        if spec.n_shared:
+            raise ValueError("the slot pool streams routed experts only")
+        self.spec = spec
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.n_layers = len(host_layers)
+        self._host = list(host_layers)  # keep the pinned arrays alive
+        for hl in self._host:
+            for k in ("gate", "up", "down"):
+                for a in hl[k]:
+                    if a.is_cuda or not a.is_pinned() or not a.is_contiguous():
+                        raise ValueError("host expert arrays must be contiguous pinned CPU tensors")
+        arr = L.QWeight * self.n_layers
+        self._qw = {k: arr(*[L.QWeight(hl[k][0].data_ptr(), hl[k][1].data_ptr(), hl[k][2].data_ptr())
+                             for hl in self._host]) for k in ("gate", "up", "down")}
+        self.cfg = L.MoECfg(hidden=spec.hidden, inter=spec.inter, n_experts=spec.n_experts, top_k=spec.top_k,
+                            bits=spec.bits, group_size=spec.group_size, n_shared=0, shared_inter=0,
+                            act_dtype=L.EF_DT_BF16 if spec.act_dtype == "bfloat16" else L.EF_DT_F16,
+                            path=L.EF_PATH_AUTO, router_mode=spec.router_mode, norm_topk=int(spec.norm_topk),
+                            n_group=spec.n_group if spec.router != "softmax" else 1,
+                            topk_group=spec.topk_group if spec.router != "softmax" else 1,
+                            routed_scaling=spec.routed_scaling if spec.router != "softmax" else 1.0,
+                            gate_dtype=L.EF_DT_F16 if spec.gate_dtype == "float16" else L.EF_DT_BF16)
+        self.pool_cfg = L.PoolCfg(n_layers=self.n_layers, budget=budget,
+                                  headroom=spec.top_k if headroom is None else headroom,
+                                  policy=_POLICIES[policy], decay=decay)
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            L.check(L.lib().ef_pool_create(ctypes.byref(self.cfg), ctypes.byref(self.pool_cfg), self._qw["gate"],
+                                           self._qw["up"], self._qw["down"], ctypes.byref(h)))
+        self._h = h
+
+    # -- the reference's call -------------------------------------------------
+    def forward_layer(self, moe_module: StreamedMoELayer, x: torch.Tensor, next_moe: Optional[StreamedMoELayer] = None,
+                      inds_out: Optional[torch.Tensor] = None, wts_out: Optional[torch.Tensor] = None,
+                      out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        return self.forward(moe_module._ef_layer_idx, x, moe_module.gate,
+                            next_moe.gate if next_moe is not None else None, inds_out, wts_out, out_dtype)
+
+    def forward(self, layer: int, x: torch.Tensor, gate: MoEGate, next_gate: Optional[MoEGate] = None,
+                inds_out: Optional[torch.Tensor] = None, wts_out: Optional[torch.Tensor] = None,
+                out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        H = self.spec.hidden
+        xf = x.reshape(-1, H).contiguous()
+        _need_cuda(xf, gate.weight)
+        T = xf.shape[0]
+        if _act_dt(xf) != self.cfg.act_dtype:
+            raise TypeError("x dtype does not match the pool's activation dtype")
+        y = torch.empty(xf.shape, dtype=out_dtype or xf.dtype, device=xf.device)
+        if T == 0:
+            return y.reshape(x.shape)
+        n = L.lib().ef_pool_workspace_size(self._h, T)
+        ws = workspace(n, xf.device)
+        eb = gate.e_score_correction_bias
+        ng = next_gate.weight.data_ptr() if next_gate is not None else None
+        neb = next_gate.e_score_correction_bias if next_gate is not None else None
+        L.check(L.lib().ef_pool_moe_forward(
+            self._h, layer, xf.data_ptr(), T, gate.weight.data_ptr(), eb.data_ptr() if eb is not None else None,
+            ng, neb.data_ptr() if neb is not None else None, y.data_ptr(), int(y.dtype == torch.float32),
+            inds_out.data_ptr() if inds_out is not None else None,
+            wts_out.data_ptr() if wts_out is not None else None, ws.data_ptr(), ws.numel(), _stream_ptr(xf.device)))
+        return y.reshape(x.shape)
+
+    def end_token(self) -> None:
+        L.check(L.lib().ef_pool_end_token(self._h))
+
+    def resident(self, layer: int) -> list:
+        n = ctypes.c_int()
+        buf = (ctypes.c_int32 * self.spec.n_experts)()
+        L.check(L.lib().ef_pool_resident(self._h, layer, ctypes.cast(buf, ctypes.c_void_p), self.spec.n_experts,
+                                         ctypes.byref(n)))
+        return [int(buf[i]) for i in range(n.value)]
+
+    def stats(self) -> dict:
+        s = L.PoolStats()
+        L.check(L.lib().ef_pool_get_stats(self._h, ctypes.byref(s)))
+        d = s.as_dict()
+        d["hit_rate"] = d["hits"] / d["accesses"] if d["accesses"] else 0.0
+        d["copy_free_rate"] = 1.0 - d["copies_sync"] / d["accesses"] if d["accesses"] else 0.0
+        return d
+
+    def reset_stats(self) -> None:
+        L.check(L.lib().ef_pool_reset_stats(self._h))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            L.lib().ef_pool_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def make_host_layers(spec: MoESpec, n_layers: int, seed: int = 0, device="cuda") -> list:
+    """Seeded synthetic experts for n_layers layers in pinned host memory
+    (generated on the device one layer at a time, then copied out)."""
+    from .synthetic import make_layer_torch
+
+    out = []
+    for layer in range(n_layers):
+        d = make_layer_torch(spec, seed=seed + layer, device=device)
+        out.append({k: tuple(a.cpu().pin_memory() for a in d[k]) for k in ("gate", "up", "down")})
+        del d
+    return out

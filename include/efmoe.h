@@ -173,6 +173,76 @@ ef_status ef_gather_qmm(const void* x, int act_dtype, int T, const int32_t* indi
                         int n_experts, int out_dim, int in_dim, int bits, int group_size, void* y, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* ---- expert residency: cache policy and HBM slot pool ------------------------------ */
+/* Eviction policies.  EF_POLICY_FREQ is the reference's FrequencyWeightedCache
+ * (ef_engine.py:48-104): a hit adds 1 to the key's score, a put inserts with
+ * score + 1, trim() evicts the lowest score (earliest inserted among equals)
+ * down to the budget and multiplies every score by `decay`.  EF_POLICY_LRU
+ * evicts the least recently used key and does not decay. */
+#define EF_POLICY_FREQ 0
+#define EF_POLICY_LRU 1
+typedef struct ef_cache_policy ef_cache_policy;
+ef_status ef_policy_create(int kind, int budget, double decay, ef_cache_policy** out);
+int ef_policy_get(ef_cache_policy* p, long long key);  /* 1 on a hit (FrequencyWeightedCache.get) */
+void ef_policy_put(ef_cache_policy* p, long long key);  /* FrequencyWeightedCache.put */
+/* FrequencyWeightedCache.trim: returns the number evicted, their keys (in
+ * eviction order) in evicted[0..cap). */
+int ef_policy_trim(ef_cache_policy* p, long long* evicted, int cap);
+int ef_policy_size(const ef_cache_policy* p);
+int ef_policy_keys(const ef_cache_policy* p, long long* keys, int cap); /* resident keys, ascending */
+double ef_policy_score(const ef_cache_policy* p, long long key);
+void ef_policy_destroy(ef_cache_policy* p);
+
+/* Streaming-decode expert pool: the experts of n_layers MoE layers live in
+ * pinned host memory (per layer the stacked MLX arrays [E, ...]); each layer
+ * owns min(E, budget + headroom) HBM slots.  `budget` experts per layer stay
+ * resident across tokens (the policy's budget); `headroom` (>= top_k x tokens
+ * per step) holds a token's misses until ef_pool_end_token trims, as the
+ * reference trims once per token.  Replaces the expert_cache argument of
+ * streaming_moe_forward (ef_engine.py:650-675) and the lookahead prefetch of
+ * experiments/ef_v16_prefetch.py:92-113. */
+typedef struct {
+  int n_layers;
+  int budget;    /* experts per layer kept across tokens */
+  int headroom;  /* extra slots per layer for one step's misses */
+  int policy;    /* EF_POLICY_FREQ | EF_POLICY_LRU */
+  double decay;  /* EF_POLICY_FREQ score decay per token (reference: 0.95) */
+} ef_pool_cfg;
+typedef struct {
+  long long accesses;        /* distinct (layer, expert) resolutions */
+  long long hits;            /* policy hits (FrequencyWeightedCache.get semantics) */
+  long long misses;          /* policy misses */
+  long long copies_sync;     /* misses copied on demand (the step waits for them) */
+  long long copies_prefetch; /* experts copied ahead by the lookahead */
+  long long prefetch_used;   /* prefetched experts the next layer then used */
+  long long evictions;
+  long long tokens;          /* ef_pool_end_token calls */
+  double h2d_bytes;          /* expert bytes copied host -> HBM */
+  double copy_ms;            /* copy-stream time spent in those copies */
+} ef_pool_stats;
+typedef struct ef_slot_pool ef_slot_pool;
+/* cfg: the layer configuration (n_shared must be 0); host_*: n_layers entries of
+ * pinned host arrays.  The pool allocates its HBM slots and a copy stream on
+ * the current device. */
+ef_status ef_pool_create(const ef_moe_cfg* cfg, const ef_pool_cfg* pool_cfg, const ef_qweight* host_gate,
+                         const ef_qweight* host_up, const ef_qweight* host_down, ef_slot_pool** out);
+size_t ef_pool_workspace_size(const ef_slot_pool* pool, int T);
+/* One MoE layer of a streaming decode step: route x (gate_w, e_bias), copy
+ * the weights of experts not in HBM, run the experts, y = weighted combine
+ * (fp32 when out_f32, else the activation dtype).  next_gate_w / next_e_bias
+ * (or NULL): the next layer's gate; its predicted experts are copied ahead on
+ * the pool's stream while this layer computes.  Synchronises `stream` once
+ * (the routing decides the copies). */
+ef_status ef_pool_moe_forward(ef_slot_pool* pool, int layer, const void* x, int T, const void* gate_w,
+                              const float* e_bias, const void* next_gate_w, const float* next_e_bias, void* y,
+                              int out_f32, int32_t* inds_out, float* wts_out, void* workspace,
+                              size_t workspace_bytes, void* stream);
+ef_status ef_pool_end_token(ef_slot_pool* pool); /* trim + decay every layer (once per token) */
+ef_status ef_pool_resident(const ef_slot_pool* pool, int layer, int32_t* experts, int cap, int* n);
+ef_status ef_pool_get_stats(ef_slot_pool* pool, ef_pool_stats* out);
+ef_status ef_pool_reset_stats(ef_slot_pool* pool);
+ef_status ef_pool_destroy(ef_slot_pool* pool);
+
 #ifdef __cplusplus
 }
 #endif

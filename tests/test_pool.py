@@ -1,0 +1,156 @@
+"""Expert residency: the cache policy pinned against the reference's own
+FrequencyWeightedCache trace (tests/golden/cache_trace.npz, made by
+tests/golden/make_golden.py), and the HBM slot pool against the resident
+layer forward."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+
+GOLDEN = os.path.join(REPO, "tests", "golden", "cache_trace.npz")
+
+
+@pytest.fixture(scope="module")
+def P():
+    from expertflow_b200 import build
+
+    build.build()
+    from expertflow_b200 import pool
+
+    return pool
+
+
+def test_policy_replays_reference_cache_trace(P):
+    """Every hit/miss, every per-token eviction count and every resident set of
+    the reference run (budget 96 over 4 layers x 128 experts, decay 0.95)."""
+    z = np.load(GOLDEN)
+    pol = P.CachePolicy(int(z["budget"]), float(z["decay"]))
+    tok = 0
+    for key, hit in zip(z["accesses"].tolist(), z["hits"].tolist()):
+        if key == -1:
+            continue
+        if key == -2:  # end of token: trim
+            ev = pol.trim()
+            assert len(ev) == int(z["evicted"][tok]), tok
+            res = z["resident"][tok]
+            assert pol.keys() == sorted(int(r) for r in res if r >= 0), tok
+            tok += 1
+            continue
+        h = pol.get(key)
+        assert int(h) == hit, (tok, key)
+        if not h:
+            pol.put(key)
+    assert tok == len(z["evicted"])
+    pol.close()
+
+
+def test_policy_tie_breaks_to_first_inserted_and_decays(P):
+    pol = P.CachePolicy(2, 0.5)
+    for k in (7, 3, 9):
+        assert not pol.get(k)
+        pol.put(k)
+    assert pol.trim() == [7]          # equal scores: the first inserted goes
+    assert pol.keys() == [3, 9]
+    assert pol.score(3) == 0.5        # 1.0 decayed once
+    assert pol.get(9) and pol.score(9) == 1.5
+    pol.put(1)                        # scores: 3 -> 0.5, 9 -> 1.5, 1 -> 1.0
+    assert pol.trim() == [3] and pol.keys() == [1, 9]
+    pol.close()
+
+
+def test_policy_lru(P):
+    pol = P.CachePolicy(2, kind="lru")
+    for k in (1, 2, 3):
+        pol.put(k)
+    pol.get(1)
+    assert pol.trim() == [2]
+    assert pol.keys() == [1, 3]
+    pol.close()
+
+
+def test_zipf_bias_rows_are_shuffled_log_probabilities(P):
+    b = P.zipf_layer_bias(4, 128, 1.1, seed=42)
+    assert b.shape == (4, 128) and b.dtype == np.float32
+    np.testing.assert_allclose(np.exp(b.astype(np.float64)).sum(1), 1.0, rtol=1e-5)
+    # the same multiset of probabilities, in a different order per layer
+    np.testing.assert_allclose(np.sort(b[0]), np.sort(b[1]), rtol=1e-6)
+    assert not np.array_equal(b[0], b[1])
+    z = np.load(GOLDEN)  # the reference's layer probabilities for the same recipe and seed
+    np.testing.assert_allclose(np.exp(b.astype(np.float64)), z["layer_probs"], rtol=1e-6)
+
+
+# ---------------------------------------------------------------- GPU
+def _small_spec():
+    from expertflow_b200.spec import MoESpec
+
+    return MoESpec(hidden=1024, n_experts=32, top_k=4, inter=256, bits=4, router="softmax", norm_topk=True,
+                   act_dtype="bfloat16")
+
+
+@pytest.mark.gpu
+def test_pool_forward_matches_resident_layers_and_policy(P):
+    import torch
+    from expertflow_b200 import moe, synthetic
+
+    spec = _small_spec()
+    n_layers, budget, steps = 4, 6, 12
+    dev = torch.device("cuda")
+    host = P.make_host_layers(spec, n_layers, seed=100)
+    bias = torch.from_numpy(P.zipf_layer_bias(n_layers, spec.n_experts, 1.1, seed=3)).to(dev)
+    gates, resident = [], []
+    for layer in range(n_layers):
+        g = torch.Generator(device=dev)
+        g.manual_seed(500 + layer)
+        gw = (torch.randn((spec.n_experts, spec.hidden), generator=g, device=dev) * 0.02).to(torch.float16)
+        gates.append(moe.MoEGate(gw, spec.top_k, "softmax", True, e_score_correction_bias=bias[layer].contiguous()))
+        d = {"gate_w": gw, "e_bias": None, "shared": None}
+        for k in ("gate", "up", "down"):
+            d[k] = tuple(a.to(dev) for a in host[layer][k])
+        m = moe.MoELayer.from_arrays(spec, d)
+        m.gate = gates[layer]
+        resident.append(m)
+    pool = P.ExpertSlotPool(spec, host, budget=budget, headroom=spec.top_k)
+    ref_pol = [P.CachePolicy(budget, 0.95) for _ in range(n_layers)]
+    acc = hits = 0
+    for t in range(steps):
+        x = synthetic.make_x_torch(spec, 1, seed=900 + t)
+        for layer in range(n_layers):
+            inds = torch.empty((1, spec.top_k), dtype=torch.int32, device=dev)
+            nxt = gates[layer + 1] if layer + 1 < n_layers else None
+            y = pool.forward(layer, x, gates[layer], nxt, inds_out=inds, out_dtype=torch.float32)
+            y_ref = resident[layer](x, out_dtype=torch.float32)
+            torch.cuda.synchronize()
+            assert torch.equal(y, y_ref), (t, layer)
+            for e in sorted(set(inds.flatten().tolist())):
+                acc += 1
+                if ref_pol[layer].get(e):
+                    hits += 1
+                else:
+                    ref_pol[layer].put(e)
+            x = (x.float() + y).to(x.dtype)
+        pool.end_token()
+        for layer in range(n_layers):
+            ref_pol[layer].trim()
+            assert pool.resident(layer) == ref_pol[layer].keys(), (t, layer)
+    st = pool.stats()
+    assert st["accesses"] == acc and st["hits"] == hits and st["misses"] == acc - hits
+    assert st["copies_sync"] + st["prefetch_used"] == st["misses"]
+    eb = spec.expert_bytes()
+    assert st["h2d_bytes"] == (st["copies_sync"] + st["copies_prefetch"]) * eb
+    assert st["tokens"] == steps and st["copies_prefetch"] > 0 and st["copy_ms"] > 0
+    from expertflow_b200.moe import device_error
+    assert device_error() == 0
+    pool.close()
+
+
+@pytest.mark.gpu
+def test_pool_rejects_pageable_host_memory(P):
+    import torch
+
+    spec = _small_spec()
+    host = P.make_host_layers(spec, 1, seed=1)
+    host[0]["gate"] = tuple(a.clone() for a in host[0]["gate"])  # pageable copies
+    with pytest.raises(ValueError):
+        P.ExpertSlotPool(spec, host, budget=4)
