@@ -7,18 +7,26 @@
 //     dict does) until size <= budget and then multiplies every score by the
 //     decay.  Scores are doubles, so the arithmetic is bit-identical to the
 //     Python floats.  An LRU variant evicts the least recently touched key.
-// (2) ef_slot_pool: the expert pool lives in pinned host memory (stacked
-//     [E, ...] per layer, the MLX layout); every layer owns `budget + headroom`
-//     HBM slots.  A layer forward routes, copies the weights of non-resident
-//     experts into free slots on the pool's copy stream (cudaMemcpyAsync, one
-//     per array), makes the compute stream wait for them, and runs the experts
-//     on slot ids.  The optional next-layer gate predicts the next layer's
+// (2) ef_slot_pool: the expert pool lives in pinned host memory; at creation
+//     the pool repacks the caller's stacked MLX arrays ([E, ...] per layer)
+//     into one contiguous blob per (layer, expert), so a miss is ONE large
+//     host-to-device copy (about 50 GB/s on this link, against about 32 GB/s
+//     for the nine separate arrays).  Every layer owns `budget + headroom` HBM
+//     slots, stored as stacked per-projection arrays so the expert kernels read
+//     them like any stacked layer.  A layer forward routes, copies each
+//     non-resident expert's blob into a staging ring on the pool's copy stream,
+//     scatters the staged blobs into their slots with one kernel, makes the
+//     compute stream wait, and runs the experts on slot ids (read by the
+//     permute kernel straight from pinned memory, so no small copy queues
+//     behind the expert copies).  The optional next-layer gate predicts the next layer's
 //     experts from the current input (experiments/ef_v16_prefetch.py:92-113)
 //     and their copies start before this layer's expert kernels, so they
 //     overlap compute.  trim() runs once per token (ef_pool_end_token), as the
 //     reference trims after each token; the headroom slots hold the token's
 //     misses until then.
 #include <algorithm>
+#include <cstring>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -146,6 +154,34 @@ struct CopyTimer {
   cudaEvent_t a = nullptr, b = nullptr;
 };
 
+// Staged blobs -> slot arrays.  Blob layout: for each projection j, w then
+// scales then biases (9 arrays, each 16-byte aligned); array a of blob i goes
+// to dst[a] + slot[i] * bytes[a].
+constexpr int kScatterMax = 16;
+struct ScatterParams {
+  const uint8_t* stage;
+  size_t blob_bytes;
+  int n;
+  int slot[kScatterMax];
+  uint8_t* dst[9];
+  size_t off[10];   // array a starts at off[a] of a blob (16-byte aligned), off[9] = used bytes
+  size_t size[9];   // bytes of array a (its stride between slots)
+};
+__global__ void pool_scatter_kernel(const __grid_constant__ ScatterParams p) {
+  const int i = blockIdx.y;
+  if (i >= p.n) return;
+  const uint4* src = reinterpret_cast<const uint4*>(p.stage + (size_t)i * p.blob_bytes);
+  const size_t n16 = p.off[9] / 16;
+  for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < n16; v += (size_t)gridDim.x * blockDim.x) {
+    const size_t o = v * 16;
+    int a = 0;
+#pragma unroll
+    for (int k = 1; k < 9; ++k) a += o >= p.off[k] ? 1 : 0;
+    const size_t r = o - p.off[a];
+    if (r < p.size[a]) *reinterpret_cast<uint4*>(p.dst[a] + (size_t)p.slot[i] * p.size[a] + r) = src[v];
+  }
+}
+
 }  // namespace ef
 
 struct ef_slot_pool {
@@ -155,7 +191,13 @@ struct ef_slot_pool {
   int n_slots = 0;
   ef::ProjGeom geom[3];                    // gate, up, down
   size_t expert_bytes = 0;
-  std::vector<ef_qweight> host[3];         // per layer, stacked [E, ...] in pinned host memory
+  std::vector<ef_qweight> host[3];         // caller's stacked arrays, read during ef_pool_create only
+  size_t blob_bytes = 0;                   // one expert, 9 arrays
+  size_t blob_off[10] = {0};               // array offsets within a blob
+  uint8_t* host_blobs = nullptr;           // pinned [n_layers][E] blobs
+  uint8_t* stage = nullptr;                // device staging ring, kScatterMax blobs
+  int n_staged = 0;
+  ef::ScatterParams scat{};
   std::vector<ef::LayerSlots> layers;
   uint8_t* dev_mem = nullptr;
   cudaStream_t copy = nullptr;
@@ -225,22 +267,38 @@ CopyTimer timer_begin(ef_slot_pool* P) {
   return t;
 }
 
-// Copy expert e of layer l into slot s (9 cudaMemcpyAsync on the copy stream).
+// Scatter the staged blobs into their slots (one kernel on the copy stream).
+ef_status flush_stage(ef_slot_pool* P) {
+  if (P->n_staged == 0) return EF_OK;
+  P->scat.n = P->n_staged;
+  dim3 grid(64, P->n_staged);
+  ef::pool_scatter_kernel<<<grid, 256, 0, P->copy>>>(P->scat);
+  P->n_staged = 0;
+  if (cudaGetLastError() != cudaSuccess) return fail(EF_ERR_CUDA, "slot scatter launch failed");
+  return EF_OK;
+}
+
+// Copy expert e of layer l into slot s: one blob copy into the staging ring
+// (the scatter into the slot arrays follows in flush_stage).
 ef_status copy_expert(ef_slot_pool* P, int l, int e, int s) {
   LayerSlots& L = P->layers[l];
-  const SlotView v = slot_arrays(P, L);
-  for (int j = 0; j < 3; ++j) {
-    const ef_qweight& h = P->host[j][l];
-    const ef::ProjGeom& g = P->geom[j];
-    const size_t wb = g.wbytes(), sb = g.sbytes();
-    if (cudaMemcpyAsync(v.w[j] + (size_t)s * wb, reinterpret_cast<const uint8_t*>(h.w) + (size_t)e * wb, wb,
-                        cudaMemcpyHostToDevice, P->copy) != cudaSuccess ||
-        cudaMemcpyAsync(v.s[j] + (size_t)s * sb, reinterpret_cast<const uint8_t*>(h.scales) + (size_t)e * sb, sb,
-                        cudaMemcpyHostToDevice, P->copy) != cudaSuccess ||
-        cudaMemcpyAsync(v.b[j] + (size_t)s * sb, reinterpret_cast<const uint8_t*>(h.biases) + (size_t)e * sb, sb,
-                        cudaMemcpyHostToDevice, P->copy) != cudaSuccess)
-      return fail(EF_ERR_CUDA, "expert copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+  if (P->n_staged == ef::kScatterMax) {
+    ef_status st = flush_stage(P);
+    if (st) return st;
   }
+  if (P->n_staged == 0) {  // the ring now holds this layer's blobs
+    const SlotView v = slot_arrays(P, L);
+    for (int j = 0; j < 3; ++j) {
+      P->scat.dst[3 * j] = v.w[j];
+      P->scat.dst[3 * j + 1] = v.s[j];
+      P->scat.dst[3 * j + 2] = v.b[j];
+    }
+  }
+  const uint8_t* src = P->host_blobs + ((size_t)l * P->cfg.n_experts + e) * P->blob_bytes;
+  if (cudaMemcpyAsync(P->stage + (size_t)P->n_staged * P->blob_bytes, src, P->blob_bytes, cudaMemcpyHostToDevice,
+                      P->copy) != cudaSuccess)
+    return fail(EF_ERR_CUDA, "expert copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+  P->scat.slot[P->n_staged++] = s;
   L.slot_expert[s] = e;
   L.expert_slot[e] = s;
   P->st.h2d_bytes += (double)P->expert_bytes;
@@ -287,7 +345,6 @@ struct PoolWs {
   float* plogits;
   int* pinds;
   float* pwts;
-  int* slot_inds;
   FfnBufs f;
 };
 size_t pool_ws(const ef_slot_pool* P, int T, Carver& c, PoolWs& w) {
@@ -300,7 +357,6 @@ size_t pool_ws(const ef_slot_pool* P, int T, Carver& c, PoolWs& w) {
   w.plogits = c.take<float>((size_t)T * E);
   w.pinds = c.take<int>((size_t)n_ent);
   w.pwts = c.take<float>((size_t)n_ent);
-  w.slot_inds = c.take<int>((size_t)n_ent);
   carve_ffn(c, n_ent, P->n_slots + 1, n_rows, cfg.hidden, cfg.inter, w.f);
   return c.off;
 }
@@ -368,10 +424,14 @@ ef_status ef_pool_create(const ef_moe_cfg* cfg, const ef_pool_cfg* pc, const ef_
     const ef_qweight* qs[3] = {&host_gate[l], &host_up[l], &host_down[l]};
     for (int j = 0; j < 3; ++j) {
       if (!qs[j]->w || !qs[j]->scales || !qs[j]->biases) return fail(EF_ERR_INVALID, "layer %d: null host array", l);
-      cudaPointerAttributes a;
-      if (cudaPointerGetAttributes(&a, qs[j]->w) != cudaSuccess || a.type != cudaMemoryTypeHost) {
-        cudaGetLastError();
-        return fail(EF_ERR_INVALID, "layer %d: expert pool arrays must be pinned host memory", l);
+      for (const void* ptr : {(const void*)qs[j]->w, (const void*)qs[j]->scales, (const void*)qs[j]->biases}) {
+        cudaPointerAttributes a;
+        if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+          cudaGetLastError();
+          return fail(EF_ERR_INVALID, "layer %d: cannot query an expert array pointer", l);
+        }
+        if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged)
+          return fail(EF_ERR_INVALID, "layer %d: expert pool arrays must be host memory", l);
       }
     }
   }
@@ -385,14 +445,62 @@ ef_status ef_pool_create(const ef_moe_cfg* cfg, const ef_pool_cfg* pc, const ef_
   P->geom[1] = P->geom[0];
   P->geom[2] = {H, I * b / 32, I / 64};
   for (int j = 0; j < 3; ++j) P->expert_bytes += P->geom[j].wbytes() + 2 * P->geom[j].sbytes();
+  {
+    size_t o = 0;
+    for (int j = 0; j < 3; ++j) {
+      const size_t sz[3] = {P->geom[j].wbytes(), P->geom[j].sbytes(), P->geom[j].sbytes()};
+      for (int a = 0; a < 3; ++a) {
+        P->blob_off[3 * j + a] = o;
+        P->scat.size[3 * j + a] = sz[a];
+        o += (sz[a] + 15) & ~size_t(15);
+      }
+    }
+    P->blob_off[9] = o;
+    P->blob_bytes = (o + 255) & ~size_t(255);
+    for (int a = 0; a < 10; ++a) P->scat.off[a] = P->blob_off[a];
+    P->scat.blob_bytes = P->blob_bytes;
+  }
   for (int j = 0; j < 3; ++j) P->host[j].assign((j == 0 ? host_gate : j == 1 ? host_up : host_down),
                                                  (j == 0 ? host_gate : j == 1 ? host_up : host_down) + pc->n_layers);
   const size_t per_layer = (size_t)n_slots * P->expert_bytes;
-  if (cudaMalloc(&P->dev_mem, per_layer * pc->n_layers) != cudaSuccess) {
+  if (cudaMalloc(&P->dev_mem, per_layer * pc->n_layers) != cudaSuccess ||
+      cudaMalloc(&P->stage, (size_t)ef::kScatterMax * P->blob_bytes) != cudaSuccess) {
     cudaGetLastError();
+    if (P->dev_mem) cudaFree(P->dev_mem);
     delete P;
     return fail(EF_ERR_CUDA, "slot pool: cannot allocate %zu bytes of HBM", per_layer * pc->n_layers);
   }
+  const size_t host_bytes = (size_t)pc->n_layers * E * P->blob_bytes;
+  if (cudaMallocHost(&P->host_blobs, host_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(P->dev_mem);
+    cudaFree(P->stage);
+    delete P;
+    return fail(EF_ERR_CUDA, "slot pool: cannot pin %zu bytes of host memory", host_bytes);
+  }
+  {  // repack the stacked arrays into per-expert blobs, layers in parallel
+    const int nt = std::max(1, std::min(16, (int)std::thread::hardware_concurrency()));
+    std::vector<std::thread> th;
+    for (int t = 0; t < nt; ++t) {
+      th.emplace_back([P, t, nt, E]() {
+        for (int l = t; l < P->pc.n_layers; l += nt) {
+          for (int e = 0; e < E; ++e) {
+            uint8_t* dst = P->host_blobs + ((size_t)l * E + e) * P->blob_bytes;
+            for (int j = 0; j < 3; ++j) {
+              const ef_qweight& h = P->host[j][l];
+              const ef::ProjGeom& g = P->geom[j];
+              memcpy(dst + P->blob_off[3 * j], reinterpret_cast<const uint8_t*>(h.w) + (size_t)e * g.wbytes(), g.wbytes());
+              memcpy(dst + P->blob_off[3 * j + 1], reinterpret_cast<const uint8_t*>(h.scales) + (size_t)e * g.sbytes(), g.sbytes());
+              memcpy(dst + P->blob_off[3 * j + 2], reinterpret_cast<const uint8_t*>(h.biases) + (size_t)e * g.sbytes(), g.sbytes());
+            }
+          }
+        }
+      });
+    }
+    for (auto& x : th) x.join();
+  }
+  P->scat.stage = P->stage;
+  for (int j = 0; j < 3; ++j) P->host[j].clear();  // the caller's arrays are not read again
   if (cudaStreamCreateWithFlags(&P->copy, cudaStreamNonBlocking) != cudaSuccess) {
     cudaFree(P->dev_mem);
     delete P;
@@ -487,6 +595,7 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
       P->st.copies_prefetch++;
     }
     if (any) {
+      if ((s = flush_stage(P))) return s;
       cudaEventRecord(t.b, P->copy);
       P->timers.push_back(t);
       cudaEventRecord(N.ready, P->copy);
@@ -530,6 +639,7 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
     P->st.copies_sync++;
   }
   if (any) {
+    if ((s = flush_stage(P))) return s;
     cudaEventRecord(t.b, P->copy);
     P->timers.push_back(t);
     cudaEventRecord(L.ready, P->copy);
@@ -537,8 +647,9 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
   }
   if (L.has_ready) cudaStreamWaitEvent(st, L.ready, 0);
   // 4. experts on slot ids
+  // slot ids stay in pinned memory: the permute kernel reads them over the
+  // link (n ints) instead of a copy that would queue behind the expert copies
   for (int i = 0; i < n; ++i) P->h_slot[i] = L.expert_slot[P->h_inds[i]];
-  cudaMemcpyAsync(w.slot_inds, P->h_slot, sizeof(int32_t) * n, cudaMemcpyHostToDevice, st);
   ef_moe_cfg sc = cfg;
   sc.n_experts = P->n_slots;
   sc.out_f32 = out_f32 ? 1 : 0;
@@ -546,7 +657,7 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
   const ef_qweight qg{reinterpret_cast<uint32_t*>(v.w[0]), reinterpret_cast<uint16_t*>(v.s[0]), reinterpret_cast<uint16_t*>(v.b[0])};
   const ef_qweight qu{reinterpret_cast<uint32_t*>(v.w[1]), reinterpret_cast<uint16_t*>(v.s[1]), reinterpret_cast<uint16_t*>(v.b[1])};
   const ef_qweight qd{reinterpret_cast<uint32_t*>(v.w[2]), reinterpret_cast<uint16_t*>(v.s[2]), reinterpret_cast<uint16_t*>(v.b[2])};
-  if ((s = moe_tail(&sc, x, T, w.slot_inds, wts, qg, qu, qd, nullptr, nullptr, nullptr, w.f, y, st))) return s;
+  if ((s = moe_tail(&sc, x, T, P->h_slot, wts, qg, qu, qd, nullptr, nullptr, nullptr, w.f, y, st))) return s;
   cudaEventRecord(L.last_use, st);
   L.has_use = true;
   return EF_OK;
@@ -605,6 +716,8 @@ ef_status ef_pool_destroy(ef_slot_pool* P) {
   }
   cudaStreamDestroy(P->copy);
   cudaFree(P->dev_mem);
+  cudaFree(P->stage);
+  if (P->host_blobs) cudaFreeHost(P->host_blobs);
   if (P->h_inds) cudaFreeHost(P->h_inds);
   delete P;
   return EF_OK;

@@ -101,8 +101,9 @@ class ExpertSlotPool:
     """HBM expert slots over a pinned-host expert pool (see module docstring).
 
     host_layers: per layer a dict {"gate": (w, s, b), "up": ..., "down": ...}
-    of pinned CPU tensors in the stacked MLX layout ([E, out, in*bits/32]
-    int32 words, [E, out, in/64] fp16 scales and biases).
+    of CPU tensors in the stacked MLX layout ([E, out, in*bits/32] int32
+    words, [E, out, in/64] fp16 scales and biases).  The pool copies them into
+    its own pinned store (one blob per expert) when it is created.
     """
 
     def __init__(self, spec: MoESpec, host_layers: Sequence[dict], budget: int, headroom: Optional[int] = None,
@@ -112,15 +113,15 @@ class ExpertSlotPool:
         self.spec = spec
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.n_layers = len(host_layers)
-        self._host = list(host_layers)  # keep the pinned arrays alive
-        for hl in self._host:
+        host = list(host_layers)
+        for hl in host:
             for k in ("gate", "up", "down"):
                 for a in hl[k]:
-                    if a.is_cuda or not a.is_pinned() or not a.is_contiguous():
-                        raise ValueError("host expert arrays must be contiguous pinned CPU tensors")
+                    if a.is_cuda or not a.is_contiguous():
+                        raise ValueError("host expert arrays must be contiguous CPU tensors")
         arr = L.QWeight * self.n_layers
         self._qw = {k: arr(*[L.QWeight(hl[k][0].data_ptr(), hl[k][1].data_ptr(), hl[k][2].data_ptr())
-                             for hl in self._host]) for k in ("gate", "up", "down")}
+                             for hl in host]) for k in ("gate", "up", "down")}
         self.cfg = L.MoECfg(hidden=spec.hidden, inter=spec.inter, n_experts=spec.n_experts, top_k=spec.top_k,
                             bits=spec.bits, group_size=spec.group_size, n_shared=0, shared_inter=0,
                             act_dtype=L.EF_DT_BF16 if spec.act_dtype == "bfloat16" else L.EF_DT_F16,
@@ -203,13 +204,13 @@ class ExpertSlotPool:
 
 
 def make_host_layers(spec: MoESpec, n_layers: int, seed: int = 0, device="cuda") -> list:
-    """Seeded synthetic experts for n_layers layers in pinned host memory
-    (generated on the device one layer at a time, then copied out)."""
+    """Seeded synthetic experts for n_layers layers in host memory (generated
+    on the device one layer at a time, then copied out)."""
     from .synthetic import make_layer_torch
 
     out = []
     for layer in range(n_layers):
         d = make_layer_torch(spec, seed=seed + layer, device=device)
-        out.append({k: tuple(a.cpu().pin_memory() for a in d[k]) for k in ("gate", "up", "down")})
+        out.append({k: tuple(a.cpu() for a in d[k]) for k in ("gate", "up", "down")})
         del d
     return out

@@ -194,8 +194,10 @@ double ef_policy_score(const ef_cache_policy* p, long long key);
 void ef_policy_destroy(ef_cache_policy* p);
 
 /* Streaming-decode expert pool: the experts of n_layers MoE layers live in
- * pinned host memory (per layer the stacked MLX arrays [E, ...]); each layer
- * owns min(E, budget + headroom) HBM slots.  `budget` experts per layer stay
+ * pinned host memory (the pool copies the caller's per-layer stacked MLX
+ * arrays [E, ...], pinned or pageable, into its own pinned store of one
+ * contiguous blob per expert); each layer owns min(E, budget + headroom) HBM
+ * slots.  `budget` experts per layer stay
  * resident across tokens (the policy's budget); `headroom` (>= top_k x tokens
  * per step) holds a token's misses until ef_pool_end_token trims, as the
  * reference trims once per token.  Replaces the expert_cache argument of
@@ -222,8 +224,9 @@ typedef struct {
 } ef_pool_stats;
 typedef struct ef_slot_pool ef_slot_pool;
 /* cfg: the layer configuration (n_shared must be 0); host_*: n_layers entries of
- * pinned host arrays.  The pool allocates its HBM slots and a copy stream on
- * the current device. */
+ * host arrays (read once, during the call).  The pool allocates its HBM
+ * slots, a staging ring, its pinned store and a copy stream on the current
+ * device. */
 ef_status ef_pool_create(const ef_moe_cfg* cfg, const ef_pool_cfg* pool_cfg, const ef_qweight* host_gate,
                          const ef_qweight* host_up, const ef_qweight* host_down, ef_slot_pool** out);
 size_t ef_pool_workspace_size(const ef_slot_pool* pool, int T);

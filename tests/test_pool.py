@@ -146,11 +146,11 @@ def test_pool_forward_matches_resident_layers_and_policy(P):
 
 
 @pytest.mark.gpu
-def test_pool_rejects_pageable_host_memory(P):
+def test_pool_rejects_device_arrays(P):
     import torch
 
     spec = _small_spec()
     host = P.make_host_layers(spec, 1, seed=1)
-    host[0]["gate"] = tuple(a.clone() for a in host[0]["gate"])  # pageable copies
+    host[0]["gate"] = tuple(a.cuda() for a in host[0]["gate"])
     with pytest.raises(ValueError):
         P.ExpertSlotPool(spec, host, budget=4)
