@@ -37,9 +37,10 @@ def _peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+        return {"hbm": float(p["hbm_gbs"]), "bf16": float(p["bf16_tflops"]),
+                "bf16_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "kind": "measured"}
     except Exception:
-        return 6650.0, 1590.0, "fallback"
+        return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "kind": "fallback"}
 
 
 class ClockSampler:
@@ -173,9 +174,227 @@ def bench_reference(args):
     return 0
 
 
+class _Layers:
+    """Seeded layer copies on one device, rotated per step so that every step
+    reads weights that are not in L2 (each copy is larger than L2 or there
+    are enough copies)."""
+
+    def __init__(self, spec, dev, rank, path=None, min_bytes=1.5e9, seed0=1000):
+        from expertflow_b200 import moe, synthetic, _lib
+
+        self.spec = spec
+        self.layer_bytes = spec.n_experts * spec.expert_bytes()
+        self.n = max(2, math.ceil(min_bytes / self.layer_bytes))
+        p = _lib.EF_PATH_AUTO if path is None else path
+        self.layers = [moe.MoELayer.from_arrays(spec, synthetic.make_layer_torch(spec, seed=seed0 * (rank + 1) + i,
+                                                                                 device=dev), device=dev, path=p)
+                       for i in range(self.n)]
+
+
+def _time_layers(L, T, steps, warmup, pg, dev, trace=False, x_seed=7):
+    """CUDA-event time of `steps` forwards (max over ranks), the distinct
+    experts per step (from the routing indices) and, with trace, the per-launch
+    kernel times of a separate pass."""
+    import torch
+    from expertflow_b200 import synthetic, _lib
+
+    spec = L.spec
+    xs = [synthetic.make_x_torch(spec, T, seed=x_seed + i, device=dev) for i in range(L.n)]
+    uniq = []
+    for i, m in enumerate(L.layers):
+        inds = torch.empty((T, spec.top_k), dtype=torch.int32, device=dev)
+        m(xs[i], inds_out=inds)
+        uniq.append(int(torch.unique(inds).numel()))
+    for s in range(warmup):
+        L.layers[s % L.n](xs[s % L.n])
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for s in range(steps):
+        L.layers[s % L.n](xs[s % L.n])
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if pg:
+        t = torch.tensor([ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    recs = []
+    if trace:
+        _lib.trace_enable(True)
+        _lib.trace_read()
+        for s in range(min(steps, 2 * L.n)):
+            L.layers[s % L.n](xs[s % L.n])
+        torch.cuda.synchronize()
+        recs = _lib.trace_read()
+        _lib.trace_enable(False)
+    ub = [uniq[s % L.n] for s in range(steps)]
+    return ms, ub, recs, xs
+
+
+def _by_kernel(recs):
+    by = {}
+    for name, t in recs:
+        by.setdefault(name, []).append(t)
+    return by
+
+
+def _cpu_sample(spec, m, x_dev, budget_s):
+    """The oracle port on the host cores over a sample of the workload's tokens,
+    with the weights of layer copy m (copied to host memory)."""
+    import numpy as np
+    import torch
+
+    def q(p):
+        return (p["weight"].cpu().numpy().view(np.uint32), p["scales"].cpu().numpy(), p["biases"].cpu().numpy())
+
+    L0 = {"gate_w": m.gate.weight.cpu().numpy(),
+          "e_bias": m.gate.e_score_correction_bias.cpu().numpy() if m.gate.e_score_correction_bias is not None else None,
+          "gate": q(m.switch_mlp.gate_proj), "up": q(m.switch_mlp.up_proj), "down": q(m.switch_mlp.down_proj),
+          "shared": None}
+    if m.shared_experts is not None:
+        sh = m.shared_experts
+        L0["shared"] = tuple(q(pj) for pj in (sh.gate_proj, sh.up_proj, sh.down_proj))
+    xb = x_dev.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    return run_cpu_reference(spec, xb.shape[0], budget_s, layer=L0, xb=xb)
+
+
+def section_decode(name, spec, Ts, args, pg, dev, rank, ws, peaks):
+    """HBM-bound decode sweep on one layer shape (GEMV path)."""
+    L = _Layers(spec, dev, rank)
+    out = {"workload": name, "bound": "hbm", "layer_copies": L.n,
+           "l2": f"rotating {L.n} layer copies of {L.layer_bytes / 1e9:.2f} GB", "points": []}
+    for T in Ts:
+        ms, ub, recs, xs = _time_layers(L, T, args.steps, args.warmup, pg, dev, trace=True)
+        ab = algorithmic_bytes(spec, statistics.mean(ub), T)
+        by = _by_kernel(recs)
+        kern = max(by, key=lambda k: sum(by[k])) if by else None
+        k_ms = statistics.mean(by[kern]) if kern else None
+        k_bytes = {"qmv_gate_up": ab["gate_up"], "qmv_down": ab["down"]}.get(kern)
+        gbs = ab["total"] / (ms * 1e-3) / 1e9
+        pt = {"tokens": T, "tokens_per_s": round(ws * T / (ms * 1e-3), 1), "ms_per_step": round(ms, 5),
+              "unique_experts": round(statistics.mean(ub), 2), "layer_gbs": round(gbs, 1),
+              "layer_frac": round(gbs / peaks["hbm"], 4), "kernel": kern,
+              "kernel_ms": round(k_ms, 5) if k_ms else None,
+              "kernel_gbs": round(k_bytes / (k_ms * 1e-3) / 1e9, 1) if (k_ms and k_bytes) else None}
+        if pt["kernel_gbs"]:
+            pt["kernel_frac"] = round(pt["kernel_gbs"] / peaks["hbm"], 4)
+        out["points"].append(pt)
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        r = _cpu_sample(spec, L.layers[0], xs[0][:1], min(args.cpu_budget, 10.0))
+        out["cpu_baseline"] = {"value": round(r["tokens_per_s"], 3), "unit": UNIT, "cores": r["cores"], "kind": "port",
+                               "sample": f"{r['steps']} single-token forwards of layer copy 0 (median)"}
+    del L
+    return out
+
+
+def section_prefill(name, spec, T, args, pg, dev, rank, ws, peaks):
+    """Tensor-bound prefill on the grouped-GEMM path."""
+    from expertflow_b200 import _lib
+
+    L = _Layers(spec, dev, rank, path=_lib.EF_PATH_GEMM, min_bytes=1.0)
+    steps = max(3, min(args.steps, 10))
+    ms, ub, recs, xs = _time_layers(L, T, steps, args.warmup, pg, dev, trace=True)
+    by = _by_kernel(recs)
+    rows = T * (spec.top_k + spec.n_shared)
+    fl = {"qgemm_gate_up": 4.0 * spec.hidden * spec.inter * rows, "qgemm_down": 2.0 * spec.hidden * spec.inter * rows}
+    kern = {}
+    for k, f in fl.items():
+        if k in by:
+            t = statistics.mean(by[k])
+            tf = f / (t * 1e-3) / 1e12
+            kern[k] = {"ms": round(t, 4), "tflops": round(tf, 1), "frac_sustained": round(tf / peaks["bf16_sustained"], 4),
+                       "frac_burst": round(tf / peaks["bf16"], 4)}
+    gemm_ms = sum(statistics.mean(by[k]) for k in fl if k in by)
+    gemm_tf = sum(fl.values()) / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
+    routed_tflop = 6.0 * spec.hidden * spec.inter * T * spec.top_k / 1e12
+    out = {"workload": name, "bound": "tensor", "tokens": T, "tokens_per_s": round(ws * T / (ms * 1e-3), 1),
+           "ms_per_step": round(ms, 4), "steps": steps, "unique_experts": round(statistics.mean(ub), 2),
+           "routed_tflop": round(routed_tflop, 4),
+           "shared_tflop": round(6.0 * spec.hidden * spec.inter * T * spec.n_shared / 1e12, 4),
+           "layer_tflops": round((routed_tflop + 6.0 * spec.hidden * spec.inter * T * spec.n_shared / 1e12) / (ms * 1e-3), 1),
+           "gemm": kern, "gemm_tflops": round(gemm_tf, 1) if gemm_tf else None,
+           "gemm_frac_sustained": round(gemm_tf / peaks["bf16_sustained"], 4) if gemm_tf else None,
+           "peak_sustained": peaks["bf16_sustained"], "peak_burst": peaks["bf16"],
+           "kernel_shares": {k: round(sum(v) / max(1e-9, sum(sum(x) for x in by.values())), 4) for k, v in by.items()},
+           "l2": f"rotating {L.n} layer copies of {L.layer_bytes / 1e9:.2f} GB"}
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        r = _cpu_sample(spec, L.layers[0], xs[0][:4], min(args.cpu_budget, 10.0))
+        out["cpu_baseline"] = {"value": round(r["tokens_per_s"], 3), "unit": UNIT, "cores": r["cores"], "kind": "port",
+                               "sample": f"{r['steps']} 4-token forwards of layer copy 0 (median)"}
+    del L
+    return out
+
+
+def section_stream(name, spec, args, dev):
+    """48 stacked layers, experts streamed from pinned host memory into HBM
+    slots (25% per layer) with one-layer lookahead; single-token decode."""
+    import numpy as np
+    import torch
+    from expertflow_b200 import moe, synthetic, pool as P
+
+    NL, steps, budget = args.stream_layers, args.stream_steps, spec.n_experts // 4
+    host = P.make_host_layers(spec, NL, seed=3000, device=dev)
+    bias = torch.from_numpy(P.zipf_layer_bias(NL, spec.n_experts, 1.1, seed=42)).to(dev)
+    gates = []
+    for layer in range(NL):
+        g = torch.Generator(device=dev)
+        g.manual_seed(77 + layer)
+        gw = (torch.randn((spec.n_experts, spec.hidden), generator=g, device=dev) * spec.gate_std).to(torch.float16)
+        gates.append(moe.MoEGate(gw, spec.top_k, "softmax", True, e_score_correction_bias=bias[layer].contiguous()))
+    xs = [synthetic.make_x_torch(spec, 1, seed=5000 + t, device=dev) for t in range(steps)]
+
+    def run(pl, lookahead, n):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for t in range(n):
+            r = xs[t % steps].float()
+            for layer in range(NL):  # the MoE input is the normalised residual, as after a pre-MoE norm
+                x = (r * torch.rsqrt(r.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+                y = pl.forward(layer, x, gates[layer], gates[layer + 1] if (lookahead and layer + 1 < NL) else None)
+                r = r + y.float()
+            pl.end_token()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    res = P.ExpertSlotPool(spec, host, budget=spec.n_experts, headroom=spec.top_k)
+    run(res, False, steps)  # every expert the run touches becomes resident
+    res.reset_stats()
+    ms_res = run(res, False, steps)
+    res.close()
+    del res
+    torch.cuda.empty_cache()
+    out = {"workload": name, "layers": NL, "steps": steps, "slots_per_layer": budget + spec.top_k,
+           "budget_per_layer": budget, "policy": "FrequencyWeightedCache (decay 0.95)",
+           "resident_tokens_per_s": round(steps / (ms_res * 1e-3), 2)}
+    for la in (False, True):
+        pl = P.ExpertSlotPool(spec, host, budget=budget, headroom=spec.top_k)
+        run(pl, la, min(16, steps))
+        pl.reset_stats()
+        ms = run(pl, la, steps)
+        st = pl.stats()
+        pl.close()
+        exposed = max(0.0, ms - ms_res)
+        d = {"tokens_per_s": round(steps / (ms * 1e-3), 2), "ms_per_token": round(ms / steps, 4),
+             "hit_rate": round(st["hit_rate"], 4), "copy_free_rate": round(st["copy_free_rate"], 4),
+             "h2d_bytes_per_token": round(st["h2d_bytes"] / steps), "copy_ms": round(st["copy_ms"], 1),
+             "copy_gbs": round(st["h2d_bytes"] / max(st["copy_ms"], 1e-9) / 1e6, 1),
+             "exposed_copy_ms": round(exposed, 1),
+             "h2d_overlap": round(1.0 - exposed / st["copy_ms"], 4) if st["copy_ms"] > 0 else None,
+             "copies_prefetch": st["copies_prefetch"], "prefetch_used": st["prefetch_used"],
+             "copies_sync": st["copies_sync"]}
+        out["lookahead" if la else "no_lookahead"] = d
+    del host
+    return out
+
+
 def bench_ours(args):
     import torch
-    import numpy as np
     from expertflow_b200 import build, moe, synthetic, _lib
     from expertflow_b200.spec import WORKLOADS
 
@@ -191,63 +410,22 @@ def bench_ours(args):
         pg = dist
     build.build()
     spec = WORKLOADS[args.workload]
-    hbm_peak, tf_peak, peak_kind = _peaks()
+    peaks = _peaks()
+    hbm_peak = peaks["hbm"]
 
-    # rotate over layer copies so that the weights touched per step exceed L2
-    layer_bytes = spec.n_experts * spec.expert_bytes()
-    n_copies = max(2, math.ceil(1.5e9 / layer_bytes))
-    layers = [moe.MoELayer.from_arrays(spec, synthetic.make_layer_torch(spec, seed=1000 * rank + i, device=dev),
-                                       device=dev) for i in range(n_copies)]
-
-    def measure(T, steps, warmup, trace=False):
-        xs = [synthetic.make_x_torch(spec, T, seed=7 + i, device=dev) for i in range(n_copies)]
-        # distinct experts per (copy, batch), counted from the routing indices
-        uniq = []
-        for i, m in enumerate(layers):
-            inds = torch.empty((T, spec.top_k), dtype=torch.int32, device=dev)
-            m(xs[i], inds_out=inds)
-            uniq.append(int(torch.unique(inds).numel()))
-        for s in range(warmup):
-            layers[s % n_copies](xs[s % n_copies])
-        torch.cuda.synchronize()
-        if pg:
-            pg.barrier()
-        st = torch.cuda.current_stream()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        if trace:
-            _lib.trace_enable(True)
-            _lib.trace_read()
-        e0.record(st)
-        for s in range(steps):
-            layers[s % n_copies](xs[s % n_copies])
-        e1.record(st)
-        torch.cuda.synchronize()
-        recs = []
-        if trace:
-            recs = _lib.trace_read()
-            _lib.trace_enable(False)
-        ms = e0.elapsed_time(e1) / steps
-        if pg:
-            t = torch.tensor([ms], device=dev)
-            pg.all_reduce(t, op=pg.ReduceOp.MAX)
-            ms = float(t.item())
-        ub = [uniq[s % n_copies] for s in range(steps)]
-        return ms, ub, recs
-
-    # ---- headline: T tokens
+    # ---- headline: T tokens through the configured workload (decode, GEMV)
+    L = _Layers(spec, dev, rank)
     T = args.tokens
     with ClockSampler(local) as clk:
-        ms, ub, _ = measure(T, args.steps, args.warmup)
+        ms, ub, _, _ = _time_layers(L, T, args.steps, args.warmup, pg, dev)
     clocks = clk.summary()
-    ms_tr, ub_tr, recs = measure(T, args.steps, 1, trace=True)
+    ms_tr, ub_tr, recs, _ = _time_layers(L, T, args.steps, 1, pg, dev, trace=True)
     n_u = statistics.mean(ub)
     ab = algorithmic_bytes(spec, n_u, T)
     value = ws * T / (ms * 1e-3)
 
     # dominant kernel (live CUDA events on the launching stream, traced pass)
-    by = {}
-    for name, t in recs:
-        by.setdefault(name, []).append(t)
+    by = _by_kernel(recs)
     kern = max(by, key=lambda k: sum(by[k])) if by else None
     k_ms = statistics.mean(by[kern]) if kern else None
     k_bytes = {"qmv_gate_up": ab["gate_up"], "qmv_down": ab["down"]}.get(kern)
@@ -263,7 +441,7 @@ def bench_ours(args):
     # ---- sweep (same run)
     sweep = []
     for t_s in args.sweep:
-        m_s, u_s, _ = measure(t_s, args.steps, args.warmup)
+        m_s, u_s, _, _ = _time_layers(L, t_s, args.steps, args.warmup, pg, dev)
         ab_s = algorithmic_bytes(spec, statistics.mean(u_s), t_s)
         gbs = ab_s["total"] / (m_s * 1e-3) / 1e9
         sweep.append({"tokens": t_s, "tokens_per_s": round(ws * t_s / (m_s * 1e-3), 1), "ms_per_step": round(m_s, 4),
@@ -271,21 +449,20 @@ def bench_ours(args):
                       "layer_frac": round(gbs / hbm_peak, 4)})
 
     # ---- e2e through the public API with host buffers (pinned), copies inside the timed region
-    m0 = layers[0]
-    xh = [synthetic.make_x_torch(spec, T, seed=7 + i, device=dev).cpu().pin_memory() for i in range(n_copies)]
+    xh = [synthetic.make_x_torch(spec, T, seed=7 + i, device=dev).cpu().pin_memory() for i in range(L.n)]
     yh = torch.empty((T, spec.hidden), dtype=xh[0].dtype).pin_memory()
     st = torch.cuda.current_stream()
     for s in range(args.warmup):
-        xd = xh[s % n_copies].to(dev, non_blocking=True)
-        yh.copy_(moe.streaming_moe_forward(layers[s % n_copies], xd[None])[0], non_blocking=True)
+        xd = xh[s % L.n].to(dev, non_blocking=True)
+        yh.copy_(moe.streaming_moe_forward(L.layers[s % L.n], xd[None])[0], non_blocking=True)
     torch.cuda.synchronize()
     if pg:
         pg.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
     for s in range(args.steps):
-        xd = xh[s % n_copies].to(dev, non_blocking=True)
-        yh.copy_(moe.streaming_moe_forward(layers[s % n_copies], xd[None])[0], non_blocking=True)
+        xd = xh[s % L.n].to(dev, non_blocking=True)
+        yh.copy_(moe.streaming_moe_forward(L.layers[s % L.n], xd[None])[0], non_blocking=True)
     e1.record(st)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
@@ -293,28 +470,40 @@ def bench_ours(args):
         t = torch.tensor([e2e_ms], device=dev)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    del m0
 
     # ---- CPU baseline (rank 0, N = 1 only): the oracle on the same layer/batch
     cpu = None
+    xs0 = synthetic.make_x_torch(spec, T, seed=7, device=dev)
     if rank == 0 and ws == 1 and not args.no_cpu:
-        L0 = {"gate_w": layers[0].gate.weight.cpu().numpy(), "e_bias": None, "shared": None}
-        for n in ("gate", "up", "down"):
-            p = getattr(layers[0].switch_mlp, f"{n}_proj")
-            L0[n] = (p["weight"].cpu().numpy().view(np.uint32), p["scales"].cpu().numpy(),
-                     p["biases"].cpu().numpy())
-        xb = synthetic.make_x_torch(spec, T, seed=7, device=dev).contiguous().view(torch.int16).cpu().numpy()
-        r = run_cpu_reference(spec, T, args.cpu_budget, layer=L0, xb=xb.view(np.uint16))
+        r = _cpu_sample(spec, L.layers[0], xs0, args.cpu_budget)
         cpu = {"value": round(r["tokens_per_s"], 3), "unit": UNIT, "cores": r["cores"], "kind": "port",
                "sample": f"{r['steps']} full {T}-token forwards of layer copy 0 (median), oracle/ef_oracle.c"}
+    n_copies, layer_bytes = L.n, L.layer_bytes
+    del L
+    torch.cuda.empty_cache()
 
-    launches = len(recs)
+    # ---- the other workloads (each its own roofline)
+    sections = {}
+    want = set(args.sections)
+    if "c2" in want:
+        sections["c2"] = section_decode("deepseek-v3-moe", WORKLOADS["deepseek-v3-moe"], [1, 32, 256], args, pg, dev,
+                                        rank, ws, peaks)
+        torch.cuda.empty_cache()
+    if "c4" in want:
+        sections["c4"] = section_prefill("deepseek-v3-moe-8bit", WORKLOADS["deepseek-v3-moe-8bit"], 4096, args, pg,
+                                         dev, rank, ws, peaks)
+        torch.cuda.empty_cache()
+    if "c3" in want and ws == 1:
+        sections["c3"] = section_stream("qwen3-30b-a3b-moe x48 streamed", WORKLOADS["qwen3-30b-a3b-moe"], args, dev)
+        torch.cuda.empty_cache()
+
+    launches = len(recs) // max(1, min(args.steps, 2 * n_copies)) * args.steps if recs else 0
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u4 codes x f16 activations, f32 accumulate",
         "data": "synthetic (seeded; random-init weights of the named shape)",
-        "config": {"workload": WORKLOAD if args.workload == WORKLOAD else args.workload, "tokens": T,
+        "config": {"workload": args.workload, "tokens": T,
                    "hidden": spec.hidden, "experts": spec.n_experts, "top_k": spec.top_k, "inter": spec.inter,
                    "bits": spec.bits, "group": spec.group_size, "parallelism": "replicas" if ws > 1 else "single",
                    "layer_copies": n_copies, "l2": f"rotating {n_copies} layer copies of {layer_bytes/1e6:.0f} MB",
@@ -323,7 +512,7 @@ def bench_ours(args):
         "layer_frac": round(ab["total"] / (ms * 1e-3) / 1e9 / hbm_peak, 4),
         "roofline": {"kernel": kern, "bound": "hbm", "achieved": round(achieved, 1) if achieved else None,
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4) if achieved else None,
-                     "traffic": traffic, "peak_kind": peak_kind, "kernel_ms": round(k_ms, 5) if k_ms else None,
+                     "traffic": traffic, "peak_kind": peaks["kind"], "kernel_ms": round(k_ms, 5) if k_ms else None,
                      "algorithmic_bytes": k_bytes, "timing": "CUDA events around each launch, traced pass",
                      "traced_ms_per_step": round(ms_tr, 5), "kernel_shares": shares},
         "cpu_baseline": cpu,
@@ -333,6 +522,7 @@ def bench_ours(args):
         "gpu_launches": launches,
         "sweep": sweep,
         "clocks": clocks,
+        "workloads": sections,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -353,6 +543,11 @@ def main():
     ap.add_argument("--sweep", type=int, nargs="*", default=[1, 8, 32, 64])
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--sections", nargs="*", default=["c2", "c4", "c3"],
+                    help="other workloads measured after the headline: c2 (DeepSeek-V3 decode), "
+                         "c4 (DeepSeek-V3 8-bit prefill), c3 (48-layer streamed decode)")
+    ap.add_argument("--stream-layers", type=int, default=48)
+    ap.add_argument("--stream-steps", type=int, default=512)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
