@@ -191,6 +191,28 @@ class _Layers:
                        for i in range(self.n)]
 
 
+class _EpLayers:
+    """Expert-parallel copies of one layer: this rank holds experts
+    [rank * E/P, (rank + 1) * E/P) of each copy, the gate and shared expert
+    replicated (experts exchanged with NCCL all-to-all)."""
+
+    def __init__(self, spec, dev, rank, ws, min_bytes=1.5e9, seed0=1000):
+        import torch
+        from expertflow_b200 import synthetic
+        from expertflow_b200.ep import ExpertParallelMoE, shard_layer
+
+        self.spec = spec
+        self.layer_bytes = spec.n_experts // ws * spec.expert_bytes()
+        self.n = max(2, math.ceil(min_bytes / self.layer_bytes))
+        self.layers = []
+        for i in range(self.n):
+            full = synthetic.make_layer_torch(spec, seed=seed0 + i, device=dev)
+            ops = shard_layer(spec, full, rank, ws, device=dev)
+            del full
+            torch.cuda.empty_cache()
+            self.layers.append(ExpertParallelMoE(spec, ops))
+
+
 def _time_layers(L, T, steps, warmup, pg, dev, trace=False, x_seed=7):
     """CUDA-event time of `steps` forwards (max over ranks), the distinct
     experts per step (from the routing indices) and, with trace, the per-launch
@@ -263,9 +285,11 @@ def _cpu_sample(spec, m, x_dev, budget_s):
 
 
 def section_decode(name, spec, Ts, args, pg, dev, rank, ws, peaks):
-    """HBM-bound decode sweep on one layer shape (GEMV path)."""
-    L = _Layers(spec, dev, rank)
+    """HBM-bound decode sweep on one layer shape (GEMV path); expert-parallel
+    across the ranks when there are several."""
+    L = _EpLayers(spec, dev, rank, ws) if ws > 1 else _Layers(spec, dev, rank)
     out = {"workload": name, "bound": "hbm", "layer_copies": L.n,
+           "parallelism": f"ep{ws} (experts sharded, NCCL all-to-all)" if ws > 1 else "single",
            "l2": f"rotating {L.n} layer copies of {L.layer_bytes / 1e9:.2f} GB", "points": []}
     for T in Ts:
         ms, ub, recs, xs = _time_layers(L, T, args.steps, args.warmup, pg, dev, trace=True)
@@ -273,7 +297,8 @@ def section_decode(name, spec, Ts, args, pg, dev, rank, ws, peaks):
         by = _by_kernel(recs)
         kern = max(by, key=lambda k: sum(by[k])) if by else None
         k_ms = statistics.mean(by[kern]) if kern else None
-        k_bytes = {"qmv_gate_up": ab["gate_up"], "qmv_down": ab["down"]}.get(kern)
+        # algorithmic bytes are counted for one whole layer: meaningful on one GPU
+        k_bytes = {"qmv_gate_up": ab["gate_up"], "qmv_down": ab["down"]}.get(kern) if ws == 1 else None
         gbs = ab["total"] / (ms * 1e-3) / 1e9
         pt = {"tokens": T, "tokens_per_s": round(ws * T / (ms * 1e-3), 1), "ms_per_step": round(ms, 5),
               "unique_experts": round(statistics.mean(ub), 2), "layer_gbs": round(gbs, 1),
@@ -295,7 +320,8 @@ def section_prefill(name, spec, T, args, pg, dev, rank, ws, peaks):
     """Tensor-bound prefill on the grouped-GEMM path."""
     from expertflow_b200 import _lib
 
-    L = _Layers(spec, dev, rank, path=_lib.EF_PATH_GEMM, min_bytes=1.0)
+    L = _EpLayers(spec, dev, rank, ws, min_bytes=1.0) if ws > 1 else _Layers(spec, dev, rank, path=_lib.EF_PATH_GEMM,
+                                                                              min_bytes=1.0)
     steps = max(3, min(args.steps, 10))
     ms, ub, recs, xs = _time_layers(L, T, steps, args.warmup, pg, dev, trace=True)
     by = _by_kernel(recs)
@@ -312,6 +338,7 @@ def section_prefill(name, spec, T, args, pg, dev, rank, ws, peaks):
     gemm_tf = sum(fl.values()) / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
     routed_tflop = 6.0 * spec.hidden * spec.inter * T * spec.top_k / 1e12
     out = {"workload": name, "bound": "tensor", "tokens": T, "tokens_per_s": round(ws * T / (ms * 1e-3), 1),
+           "parallelism": f"ep{ws} (experts sharded, NCCL all-to-all)" if ws > 1 else "single",
            "ms_per_step": round(ms, 4), "steps": steps, "unique_experts": round(statistics.mean(ub), 2),
            "routed_tflop": round(routed_tflop, 4),
            "shared_tflop": round(6.0 * spec.hidden * spec.inter * T * spec.n_shared / 1e12, 4),

@@ -107,6 +107,9 @@ SIGNATURES = {
     "ef_dequantize": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _P]),
     "ef_gather_qmm_workspace_size": (_SZ, [_I, _I, _I, _I, _I]),
     "ef_gather_qmm": (_I, [_P, _I, _I, _P, _I, _QW, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
+    "ef_ep_dispatch_workspace_size": (_SZ, [_CFGP, _I]),
+    "ef_ep_dispatch": (_I, [_CFGP, _I, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "ef_ep_combine": (_I, [_CFGP, _P, _P, _P, _I, _I, _P, _P]),
     "ef_policy_create": (_I, [_I, _I, ctypes.c_double, _P]),
     "ef_policy_get": (_I, [_P, ctypes.c_longlong]),
     "ef_policy_put": (None, [_P, ctypes.c_longlong]),

@@ -7,4 +7,5 @@
 #include "ef_qgemm.cu"
 #include "ef_api.cu"
 #include "ef_pool.cu"
+#include "ef_ep.cu"
 #include "ef_noalloc.cu"

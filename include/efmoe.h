@@ -173,6 +173,29 @@ ef_status ef_gather_qmm(const void* x, int act_dtype, int T, const int32_t* indi
                         int n_experts, int out_dim, int in_dim, int bits, int group_size, void* y, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* ---- expert parallelism (experts sharded across ranks) --------------------- */
+/* Expert e lives on rank e / (E / n_ranks); router and shared expert are
+ * replicated; each rank routes its own T tokens.  The exchange steps are
+ * NCCL all-to-alls issued by the host between these calls:
+ *   ef_ep_dispatch -> all-to-all(send_counts) -> all-to-all(send_rows,
+ *   send_expert) -> ef_moe_experts_forward (local experts) -> all-to-all of
+ *   the fp32 outputs back -> ef_ep_combine.
+ * Replaces the single-host per-(token, k) expert loop of ef_engine.py:678-703. */
+size_t ef_ep_dispatch_workspace_size(const ef_moe_cfg* cfg, int T);
+/* Route x [T, H]; send_rows [T*k, H] (act dtype) = the routed token rows sorted
+ * by expert (so by destination rank), send_expert [T*k] = the destination's
+ * local expert id, send_counts [n_ranks] = rows per rank, inv_out [T*k] =
+ * sorted row of entry (t, j), wts_out [T*k] = routing weights, inds_out
+ * [T*k] = global expert ids (or NULL). */
+ef_status ef_ep_dispatch(const ef_moe_cfg* cfg, int n_ranks, const void* x, int T, const void* gate_w,
+                         const float* e_bias, void* send_rows, int32_t* send_expert, int32_t* send_counts,
+                         int32_t* inv_out, float* wts_out, int32_t* inds_out, void* workspace,
+                         size_t workspace_bytes, void* stream);
+/* y[t] = sum_j wts[t, j] * back_rows[inv[t, j]] (+ back_rows[T*k + t] when
+ * with_shared), in j order; back_rows fp32 [T*k (+T), H]. */
+ef_status ef_ep_combine(const ef_moe_cfg* cfg, const float* back_rows, const int32_t* inv, const float* wts, int T,
+                        int with_shared, void* y, void* stream);
+
 /* ---- expert residency: cache policy and HBM slot pool ------------------------------ */
 /* Eviction policies.  EF_POLICY_FREQ is the reference's FrequencyWeightedCache
  * (ef_engine.py:48-104): a hit adds 1 to the key's score, a put inserts with
