@@ -325,16 +325,19 @@ def section_prefill(name, spec, T, args, pg, dev, rank, ws, peaks):
     steps = max(3, min(args.steps, 10))
     ms, ub, recs, xs = _time_layers(L, T, steps, args.warmup, pg, dev, trace=True)
     by = _by_kernel(recs)
+    n_traced = min(steps, 2 * L.n)
+    # per step: every launch of the kernel (routed and, expert-parallel, the
+    # separate shared-expert launch) against all rows of the step
     rows = T * (spec.top_k + spec.n_shared)
     fl = {"qgemm_gate_up": 4.0 * spec.hidden * spec.inter * rows, "qgemm_down": 2.0 * spec.hidden * spec.inter * rows}
     kern = {}
     for k, f in fl.items():
         if k in by:
-            t = statistics.mean(by[k])
+            t = sum(by[k]) / n_traced
             tf = f / (t * 1e-3) / 1e12
-            kern[k] = {"ms": round(t, 4), "tflops": round(tf, 1), "frac_sustained": round(tf / peaks["bf16_sustained"], 4),
-                       "frac_burst": round(tf / peaks["bf16"], 4)}
-    gemm_ms = sum(statistics.mean(by[k]) for k in fl if k in by)
+            kern[k] = {"ms": round(t, 4), "launches_per_step": len(by[k]) // n_traced, "tflops": round(tf, 1),
+                       "frac_sustained": round(tf / peaks["bf16_sustained"], 4), "frac_burst": round(tf / peaks["bf16"], 4)}
+    gemm_ms = sum(sum(by[k]) / n_traced for k in fl if k in by)
     gemm_tf = sum(fl.values()) / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
     routed_tflop = 6.0 * spec.hidden * spec.inter * T * spec.top_k / 1e12
     out = {"workload": name, "bound": "tensor", "tokens": T, "tokens_per_s": round(ws * T / (ms * 1e-3), 1),
