@@ -213,10 +213,11 @@ class _EpLayers:
             self.layers.append(ExpertParallelMoE(spec, ops))
 
 
-def _time_layers(L, T, steps, warmup, pg, dev, trace=False, x_seed=7):
+def _time_layers(L, T, steps, warmup, pg, dev, trace=False, x_seed=7, graphs=False):
     """CUDA-event time of `steps` forwards (max over ranks), the distinct
     experts per step (from the routing indices) and, with trace, the per-launch
-    kernel times of a separate pass."""
+    kernel times of a separate (eager) pass.  graphs: each layer copy's forward
+    is captured in a CUDA graph (MoELayer.capture) and replayed."""
     import torch
     from expertflow_b200 import synthetic, _lib
 
@@ -227,8 +228,14 @@ def _time_layers(L, T, steps, warmup, pg, dev, trace=False, x_seed=7):
         inds = torch.empty((T, spec.top_k), dtype=torch.int32, device=dev)
         m(xs[i], inds_out=inds)
         uniq.append(int(torch.unique(inds).numel()))
+    fwd = [(lambda m=m, x=x: m(x)) for m, x in zip(L.layers, xs)]
+    if graphs:
+        cfs = [m.capture(T, x.dtype) for m, x in zip(L.layers, xs)]
+        for cf, x in zip(cfs, xs):
+            cf.x.copy_(x)
+        fwd = [cf.graph.replay for cf in cfs]
     for s in range(warmup):
-        L.layers[s % L.n](xs[s % L.n])
+        fwd[s % L.n]()
     torch.cuda.synchronize()
     if pg:
         pg.barrier()
@@ -236,7 +243,7 @@ def _time_layers(L, T, steps, warmup, pg, dev, trace=False, x_seed=7):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
     for s in range(steps):
-        L.layers[s % L.n](xs[s % L.n])
+        fwd[s % L.n]()
     e1.record(st)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
@@ -447,8 +454,9 @@ def bench_ours(args):
     L = _Layers(spec, dev, rank)
     T = args.tokens
     with ClockSampler(local) as clk:
-        ms, ub, _, _ = _time_layers(L, T, args.steps, args.warmup, pg, dev)
+        ms, ub, _, _ = _time_layers(L, T, args.steps, args.warmup, pg, dev, graphs=True)
     clocks = clk.summary()
+    ms_eager, _, _, _ = _time_layers(L, T, args.steps, args.warmup, pg, dev)
     ms_tr, ub_tr, recs, _ = _time_layers(L, T, args.steps, 1, pg, dev, trace=True)
     n_u = statistics.mean(ub)
     ab = algorithmic_bytes(spec, n_u, T)
@@ -471,7 +479,7 @@ def bench_ours(args):
     # ---- sweep (same run)
     sweep = []
     for t_s in args.sweep:
-        m_s, u_s, _, _ = _time_layers(L, t_s, args.steps, args.warmup, pg, dev)
+        m_s, u_s, _, _ = _time_layers(L, t_s, args.steps, args.warmup, pg, dev, graphs=True)
         ab_s = algorithmic_bytes(spec, statistics.mean(u_s), t_s)
         gbs = ab_s["total"] / (m_s * 1e-3) / 1e9
         sweep.append({"tokens": t_s, "tokens_per_s": round(ws * t_s / (m_s * 1e-3), 1), "ms_per_step": round(m_s, 4),
@@ -479,20 +487,21 @@ def bench_ours(args):
                       "layer_frac": round(gbs / hbm_peak, 4)})
 
     # ---- e2e through the public API with host buffers (pinned), copies inside the timed region
+    # the public API's captured forward (MoELayer.capture): pinned x -> device
+    # input buffer, replay, device output -> pinned y, every step
     xh = [synthetic.make_x_torch(spec, T, seed=7 + i, device=dev).cpu().pin_memory() for i in range(L.n)]
     yh = torch.empty((T, spec.hidden), dtype=xh[0].dtype).pin_memory()
+    cfs = [m.capture(T, xh[0].dtype) for m in L.layers]
     st = torch.cuda.current_stream()
     for s in range(args.warmup):
-        xd = xh[s % L.n].to(dev, non_blocking=True)
-        yh.copy_(moe.streaming_moe_forward(L.layers[s % L.n], xd[None])[0], non_blocking=True)
+        yh.copy_(cfs[s % L.n](xh[s % L.n]), non_blocking=True)
     torch.cuda.synchronize()
     if pg:
         pg.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
     for s in range(args.steps):
-        xd = xh[s % L.n].to(dev, non_blocking=True)
-        yh.copy_(moe.streaming_moe_forward(L.layers[s % L.n], xd[None])[0], non_blocking=True)
+        yh.copy_(cfs[s % L.n](xh[s % L.n]), non_blocking=True)
     e1.record(st)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
@@ -536,6 +545,7 @@ def bench_ours(args):
         "config": {"workload": args.workload, "tokens": T,
                    "hidden": spec.hidden, "experts": spec.n_experts, "top_k": spec.top_k, "inter": spec.inter,
                    "bits": spec.bits, "group": spec.group_size, "parallelism": "replicas" if ws > 1 else "single",
+                   "launch": "CUDA graph per layer copy (MoELayer.capture)",
                    "layer_copies": n_copies, "l2": f"rotating {n_copies} layer copies of {layer_bytes/1e6:.0f} MB",
                    "unique_experts_per_step": round(n_u, 2)},
         "layer_gbs": round(ab["total"] / (ms * 1e-3) / 1e9, 1),
@@ -548,7 +558,8 @@ def bench_ours(args):
         "cpu_baseline": cpu,
         "e2e": {"value": round(ws * T / (e2e_ms * 1e-3), 1), "unit": UNIT, "ms_per_step": round(e2e_ms, 5),
                 "h2d_bytes_per_step": T * spec.hidden * 2, "d2h_bytes_per_step": T * spec.hidden * 2,
-                "api": "streaming_moe_forward (C ABI ef_moe_forward), pinned host x/y"},
+                "api": "MoELayer.capture (C ABI ef_moe_forward in a CUDA graph), pinned host x/y"},
+        "eager_ms_per_step": round(ms_eager, 5),
         "gpu_launches": launches,
         "sweep": sweep,
         "clocks": clocks,

@@ -238,8 +238,10 @@ class MoELayer(torch.nn.Module):
         return c
 
     def forward(self, x: torch.Tensor, inds_out: Optional[torch.Tensor] = None,
-                wts_out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
-        """y = MoE(x) in x's dtype, or fp32 (the un-rounded combine) with out_dtype=torch.float32."""
+                wts_out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                workspace_buf: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y = MoE(x) in x's dtype, or fp32 (the un-rounded combine) with out_dtype=torch.float32.
+        workspace_buf: caller-owned scratch (uint8, >= workspace_bytes(T)) instead of the shared one."""
         H = self.switch_mlp.gate_proj.input_dims
         xf = x.reshape(-1, H).contiguous()
         _need_cuda(xf)
@@ -252,7 +254,12 @@ class MoELayer(torch.nn.Module):
         cfg = self.cfg(_act_dt(xf))
         cfg.out_f32 = int(y.dtype == torch.float32)
         n = L.lib().ef_moe_workspace_size(ctypes.byref(cfg), T)
-        ws = workspace(n, xf.device)
+        if workspace_buf is not None:
+            if workspace_buf.numel() < n or workspace_buf.device != xf.device:
+                raise ValueError(f"workspace_buf needs {n} bytes on {xf.device}")
+            ws = workspace_buf
+        else:
+            ws = workspace(n, xf.device)
         sp = self.switch_mlp
         sh = self.shared_experts
         sq = [ctypes.byref(p.qweight()) for p in (sh.gate_proj, sh.up_proj, sh.down_proj)] if sh else [None] * 3
@@ -265,6 +272,15 @@ class MoELayer(torch.nn.Module):
             wts_out.data_ptr() if wts_out is not None else None, ws.data_ptr(), ws.numel(),
             _stream_ptr(xf.device)))
         return y.reshape(x.shape)
+
+    def workspace_bytes(self, T: int, act_dtype: torch.dtype = torch.bfloat16) -> int:
+        cfg = self.cfg(L.EF_DT_BF16 if act_dtype == torch.bfloat16 else L.EF_DT_F16)
+        return int(L.lib().ef_moe_workspace_size(ctypes.byref(cfg), T))
+
+    def capture(self, T: int, dtype: torch.dtype = torch.bfloat16,
+                out_dtype: Optional[torch.dtype] = None) -> "CapturedForward":
+        """This layer's forward for T tokens captured in a CUDA graph."""
+        return CapturedForward(self, T, dtype, out_dtype)
 
     # -- construction helpers -------------------------------------------------
     @staticmethod
@@ -295,6 +311,37 @@ class MoELayer(torch.nn.Module):
             sg, su, sd = layer["shared"]
             shared = QuantizedMLP(qlin(sg), qlin(su), qlin(sd))
         return MoELayer(gate, mlp, shared, path)
+
+
+class CapturedForward:
+    """One MoELayer forward for a fixed token count captured in a CUDA graph:
+    the layer's kernel launches (router, permute, gather, experts, combine)
+    replay with one host call.  Write the input into ``.x`` (or pass it to
+    ``__call__``), replay, read ``.y``.  The graph owns its input, output and
+    workspace buffers, and keeps the layer's weight tensors alive."""
+
+    def __init__(self, layer: MoELayer, T: int, dtype: torch.dtype = torch.bfloat16,
+                 out_dtype: Optional[torch.dtype] = None):
+        dev = layer.gate.weight.device
+        H = layer.switch_mlp.gate_proj.input_dims
+        self.layer = layer
+        self.x = torch.zeros((T, H), dtype=dtype, device=dev)
+        self.ws = torch.empty(max(layer.workspace_bytes(T, dtype), 1), dtype=torch.uint8, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):  # eager warm-up: sets kernel attributes outside the capture
+            for _ in range(2):
+                layer(self.x, out_dtype=out_dtype, workspace_buf=self.ws)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.y = layer(self.x, out_dtype=out_dtype, workspace_buf=self.ws)
+
+    def __call__(self, x: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x is not None:
+            self.x.copy_(x.reshape(self.x.shape), non_blocking=True)
+        self.graph.replay()
+        return self.y
 
 
 def streaming_moe_forward(moe_module: MoELayer, x: torch.Tensor, expert_cache=None) -> torch.Tensor:

@@ -321,3 +321,26 @@ def test_prefill_deepseek_v3_8bit_sampled():
     assert_ffn_close(y.cpu().numpy()[tokens], y_ref, what="prefill 8-bit")
     del m, layer
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("spec_name,T", [("qwen3-30b-a3b-moe", 1), ("qwen3-30b-a3b-moe", 64),
+                                         ("mixtral-small-h1024-e16", 300)])
+def test_captured_forward_equals_eager(spec_name, T):
+    """The CUDA-graph-captured layer forward replays exactly the eager forward
+    (decode GEMV and grouped-GEMM paths), with new inputs written into .x."""
+    moe = _moe()
+    from expertflow_b200 import _lib as L
+    from expertflow_b200.spec import WORKLOADS
+
+    spec = WORKLOADS[spec_name]
+    layer = _torch_layer(spec, seed=8)
+    m = moe.MoELayer.from_arrays(spec, layer, path=L.EF_PATH_GEMM if T >= 256 else L.EF_PATH_AUTO)
+    dt = torch.bfloat16 if spec.act_dtype == "bfloat16" else torch.float16
+    cf = m.capture(T, dt, out_dtype=torch.float32)
+    for seed in (1, 2):
+        x = synthetic.make_x_torch(spec, T, seed=seed)
+        y_graph = cf(x).clone()
+        y_eager = m(x, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        assert torch.equal(y_graph, y_eager)
+    assert moe.device_error() == 0
