@@ -385,16 +385,13 @@ def section_stream(name, spec, args, dev):
     xs = [synthetic.make_x_torch(spec, 1, seed=5000 + t, device=dev) for t in range(steps)]
 
     def run(pl, lookahead, n):
+        """n decode steps through all layers, in the library (ef_pool_decode_step)."""
+        rs = [xs[t % steps].float().contiguous() for t in range(n)]
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for t in range(n):
-            r = xs[t % steps].float()
-            for layer in range(NL):  # the MoE input is the normalised residual, as after a pre-MoE norm
-                x = (r * torch.rsqrt(r.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
-                y = pl.forward(layer, x, gates[layer], gates[layer + 1] if (lookahead and layer + 1 < NL) else None)
-                r = r + y.float()
-            pl.end_token()
+            pl.decode_step(rs[t], gates, lookahead=lookahead)
         e1.record()
         torch.cuda.synchronize()
         return e0.elapsed_time(e1)
@@ -407,6 +404,7 @@ def section_stream(name, spec, args, dev):
     del res
     torch.cuda.empty_cache()
     out = {"workload": name, "layers": NL, "steps": steps, "slots_per_layer": budget + spec.top_k,
+           "loop": "ef_pool_decode_step (per layer: residual add + RMS norm, routed MoE on HBM slots)",
            "budget_per_layer": budget, "policy": "FrequencyWeightedCache (decay 0.95)",
            "resident_tokens_per_s": round(steps / (ms_res * 1e-3), 2)}
     for la in (False, True):

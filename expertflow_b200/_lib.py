@@ -122,6 +122,8 @@ SIGNATURES = {
     "ef_pool_workspace_size": (_SZ, [_P, _I]),
     "ef_pool_moe_forward": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ, _P]),
     "ef_pool_end_token": (_I, [_P]),
+    "ef_pool_decode_workspace_size": (_SZ, [_P, _I]),
+    "ef_pool_decode_step": (_I, [_P, _P, _I, _P, _P, _I, ctypes.c_float, _P, _SZ, _P]),
     "ef_pool_resident": (_I, [_P, _I, _P, _I, ctypes.POINTER(_I)]),
     "ef_pool_get_stats": (_I, [_P, ctypes.POINTER(PoolStats)]),
     "ef_pool_reset_stats": (_I, [_P]),

@@ -144,9 +144,9 @@ struct LayerSlots {
   std::vector<int> expert_slot;            // -1: not in HBM
   std::vector<char> staged;                // copied by the lookahead, not yet in the policy
   CachePolicy policy;
-  cudaEvent_t ready = nullptr;             // copy stream: after the last copy into this layer
-  cudaEvent_t last_use = nullptr;          // compute stream: after this layer's last expert kernels
-  bool has_ready = false, has_use = false;
+  cudaEvent_t ready[2] = {nullptr, nullptr};  // per copy lane: after its last copy into this layer
+  cudaEvent_t last_use = nullptr;             // compute stream: after this layer's last expert kernels
+  bool has_ready[2] = {false, false}, has_use = false;
   explicit LayerSlots(int kind, int budget, double decay) : policy(kind, budget, decay) {}
 };
 
@@ -182,6 +182,39 @@ __global__ void pool_scatter_kernel(const __grid_constant__ ScatterParams p) {
   }
 }
 
+// r[t] += y[t] (when y), then x[t] = r[t] / sqrt(mean(r[t]^2) + eps) in the
+// activation dtype (when x): the residual stream and pre-MoE norm between the
+// stacked layers of a decode step.  One CTA per token, fixed reduction order.
+constexpr int kNormThreads = 256;
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __restrict__ r, const float* __restrict__ y,
+                                                                   int H, float eps, int act_bf16,
+                                                                   uint16_t* __restrict__ x) {
+  const size_t base = (size_t)blockIdx.x * H;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < H; i += kNormThreads) {
+    float v = r[base + i];
+    if (y) {
+      v += y[base + i];
+      r[base + i] = v;
+    }
+    ss = fmaf(v, v, ss);
+  }
+  if (!x) return;
+  __shared__ float part[kNormThreads / 32];
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) tot += part[w];
+  const float inv = rsqrtf(tot / (float)H + eps);
+  for (int i = threadIdx.x; i < H; i += kNormThreads) {
+    const float v = r[base + i] * inv;
+    x[base + i] = act_bf16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v)) : __half_as_ushort(__float2half_rn(v));
+  }
+}
+
 }  // namespace ef
 
 struct ef_slot_pool {
@@ -195,12 +228,17 @@ struct ef_slot_pool {
   size_t blob_bytes = 0;                   // one expert, 9 arrays
   size_t blob_off[10] = {0};               // array offsets within a blob
   uint8_t* host_blobs = nullptr;           // pinned [n_layers][E] blobs
-  uint8_t* stage = nullptr;                // device staging ring, kScatterMax blobs
-  int n_staged = 0;
-  ef::ScatterParams scat{};
+  // copy lanes: 0 = the step's own misses, 1 = lookahead prefetch; each has its
+  // stream, staging ring and scatter batch, so neither waits behind the other
+  struct Lane {
+    cudaStream_t stream = nullptr;
+    uint8_t* stage = nullptr;  // device staging ring, kScatterMax blobs
+    int n_staged = 0;
+    ef::ScatterParams scat{};
+  } lane[2];
+  ef::ScatterParams scat{};                // blob layout, copied into each lane's batch
   std::vector<ef::LayerSlots> layers;
   uint8_t* dev_mem = nullptr;
-  cudaStream_t copy = nullptr;
   int32_t* h_inds = nullptr;               // pinned staging: routed ids, predicted ids, slot ids
   int32_t* h_pred = nullptr;
   int32_t* h_slot = nullptr;
@@ -253,7 +291,7 @@ void fold_timers(ef_slot_pool* P, bool all) {
   P->timers.erase(P->timers.begin(), P->timers.begin() + keep_from);
 }
 
-CopyTimer timer_begin(ef_slot_pool* P) {
+CopyTimer timer_begin(ef_slot_pool* P, cudaStream_t cs) {
   if (P->timers.size() > 256) fold_timers(P, false);
   CopyTimer t;
   if (!P->spare.empty()) {
@@ -263,42 +301,44 @@ CopyTimer timer_begin(ef_slot_pool* P) {
     cudaEventCreate(&t.a);
     cudaEventCreate(&t.b);
   }
-  cudaEventRecord(t.a, P->copy);
+  cudaEventRecord(t.a, cs);
   return t;
 }
 
 // Scatter the staged blobs into their slots (one kernel on the copy stream).
-ef_status flush_stage(ef_slot_pool* P) {
-  if (P->n_staged == 0) return EF_OK;
-  P->scat.n = P->n_staged;
-  dim3 grid(64, P->n_staged);
-  ef::pool_scatter_kernel<<<grid, 256, 0, P->copy>>>(P->scat);
-  P->n_staged = 0;
+ef_status flush_stage(ef_slot_pool* P, int ln) {
+  auto& C = P->lane[ln];
+  if (C.n_staged == 0) return EF_OK;
+  C.scat.n = C.n_staged;
+  dim3 grid(64, C.n_staged);
+  ef::pool_scatter_kernel<<<grid, 256, 0, C.stream>>>(C.scat);
+  C.n_staged = 0;
   if (cudaGetLastError() != cudaSuccess) return fail(EF_ERR_CUDA, "slot scatter launch failed");
   return EF_OK;
 }
 
 // Copy expert e of layer l into slot s: one blob copy into the staging ring
 // (the scatter into the slot arrays follows in flush_stage).
-ef_status copy_expert(ef_slot_pool* P, int l, int e, int s) {
+ef_status copy_expert(ef_slot_pool* P, int ln, int l, int e, int s) {
   LayerSlots& L = P->layers[l];
-  if (P->n_staged == ef::kScatterMax) {
-    ef_status st = flush_stage(P);
+  auto& C = P->lane[ln];
+  if (C.n_staged == ef::kScatterMax) {
+    ef_status st = flush_stage(P, ln);
     if (st) return st;
   }
-  if (P->n_staged == 0) {  // the ring now holds this layer's blobs
+  if (C.n_staged == 0) {  // the ring now holds this layer's blobs
     const SlotView v = slot_arrays(P, L);
     for (int j = 0; j < 3; ++j) {
-      P->scat.dst[3 * j] = v.w[j];
-      P->scat.dst[3 * j + 1] = v.s[j];
-      P->scat.dst[3 * j + 2] = v.b[j];
+      C.scat.dst[3 * j] = v.w[j];
+      C.scat.dst[3 * j + 1] = v.s[j];
+      C.scat.dst[3 * j + 2] = v.b[j];
     }
   }
   const uint8_t* src = P->host_blobs + ((size_t)l * P->cfg.n_experts + e) * P->blob_bytes;
-  if (cudaMemcpyAsync(P->stage + (size_t)P->n_staged * P->blob_bytes, src, P->blob_bytes, cudaMemcpyHostToDevice,
-                      P->copy) != cudaSuccess)
+  if (cudaMemcpyAsync(C.stage + (size_t)C.n_staged * P->blob_bytes, src, P->blob_bytes, cudaMemcpyHostToDevice,
+                      C.stream) != cudaSuccess)
     return fail(EF_ERR_CUDA, "expert copy failed: %s", cudaGetErrorString(cudaGetLastError()));
-  P->scat.slot[P->n_staged++] = s;
+  C.scat.slot[C.n_staged++] = s;
   L.slot_expert[s] = e;
   L.expert_slot[e] = s;
   P->st.h2d_bytes += (double)P->expert_bytes;
@@ -323,9 +363,9 @@ int take_slot(ef_slot_pool* P, int l, const std::vector<char>& keep) {
   return -1;
 }
 
-void copies_begin(ef_slot_pool* P, LayerSlots& L) {
+void copies_begin(ef_slot_pool* P, int ln, LayerSlots& L) {
   // a slot may still be read by the layer's previous expert kernels
-  if (L.has_use) cudaStreamWaitEvent(P->copy, L.last_use, 0);
+  if (L.has_use) cudaStreamWaitEvent(P->lane[ln].stream, L.last_use, 0);
 }
 
 std::vector<int> distinct_sorted(const int32_t* ids, int n, int E) {
@@ -361,15 +401,20 @@ size_t pool_ws(const ef_slot_pool* P, int T, Carver& c, PoolWs& w) {
   return c.off;
 }
 
+// Routes x through gate gw (and, when gw2, the next layer's gate gw2 in the same
+// two launches: that routing is the lookahead prediction).
 ef_status pool_route(const ef_moe_cfg& cfg, const void* x, int T, const void* gw, const float* eb, float* logits, int* inds,
-                float* wts, cudaStream_t st) {
+                     float* wts, const void* gw2, const float* eb2, float* logits2, int* inds2, float* wts2,
+                     cudaStream_t st) {
   const bool bf = cfg.act_dtype == EF_DT_BF16;
   EF_LAUNCH("router_logits", launch_router_logits(static_cast<const uint16_t*>(x), bf, static_cast<const uint16_t*>(gw),
-                                                  cfg.gate_dtype == EF_DT_BF16, T, cfg.n_experts, cfg.hidden, logits, st));
+                                                  cfg.gate_dtype == EF_DT_BF16, T, cfg.n_experts, cfg.hidden, logits, st,
+                                                  static_cast<const uint16_t*>(gw2), gw2 ? logits2 : nullptr));
   EF_LAUNCH("router_select",
             launch_router_select(logits, eb, T, cfg.n_experts, cfg.top_k, cfg.router_mode, cfg.norm_topk,
                                  cfg.router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg.n_group : 1, cfg.topk_group,
-                                 cfg.router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg.routed_scaling : 1.0f, inds, wts, st));
+                                 cfg.router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg.routed_scaling : 1.0f, inds, wts, st,
+                                 gw2 ? logits2 : nullptr, eb2, inds2, wts2));
   return EF_OK;
 }
 
@@ -464,9 +509,11 @@ ef_status ef_pool_create(const ef_moe_cfg* cfg, const ef_pool_cfg* pc, const ef_
                                                  (j == 0 ? host_gate : j == 1 ? host_up : host_down) + pc->n_layers);
   const size_t per_layer = (size_t)n_slots * P->expert_bytes;
   if (cudaMalloc(&P->dev_mem, per_layer * pc->n_layers) != cudaSuccess ||
-      cudaMalloc(&P->stage, (size_t)ef::kScatterMax * P->blob_bytes) != cudaSuccess) {
+      cudaMalloc(&P->lane[0].stage, (size_t)ef::kScatterMax * P->blob_bytes) != cudaSuccess ||
+      cudaMalloc(&P->lane[1].stage, (size_t)ef::kScatterMax * P->blob_bytes) != cudaSuccess) {
     cudaGetLastError();
     if (P->dev_mem) cudaFree(P->dev_mem);
+    if (P->lane[0].stage) cudaFree(P->lane[0].stage);
     delete P;
     return fail(EF_ERR_CUDA, "slot pool: cannot allocate %zu bytes of HBM", per_layer * pc->n_layers);
   }
@@ -474,7 +521,8 @@ ef_status ef_pool_create(const ef_moe_cfg* cfg, const ef_pool_cfg* pc, const ef_
   if (cudaMallocHost(&P->host_blobs, host_bytes) != cudaSuccess) {
     cudaGetLastError();
     cudaFree(P->dev_mem);
-    cudaFree(P->stage);
+    cudaFree(P->lane[0].stage);
+    cudaFree(P->lane[1].stage);
     delete P;
     return fail(EF_ERR_CUDA, "slot pool: cannot pin %zu bytes of host memory", host_bytes);
   }
@@ -499,10 +547,17 @@ ef_status ef_pool_create(const ef_moe_cfg* cfg, const ef_pool_cfg* pc, const ef_
     }
     for (auto& x : th) x.join();
   }
-  P->scat.stage = P->stage;
+  for (int ln = 0; ln < 2; ++ln) {
+    P->lane[ln].scat = P->scat;
+    P->lane[ln].scat.stage = P->lane[ln].stage;
+  }
   for (int j = 0; j < 3; ++j) P->host[j].clear();  // the caller's arrays are not read again
-  if (cudaStreamCreateWithFlags(&P->copy, cudaStreamNonBlocking) != cudaSuccess) {
+  if (cudaStreamCreateWithFlags(&P->lane[0].stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&P->lane[1].stream, cudaStreamNonBlocking) != cudaSuccess) {
     cudaFree(P->dev_mem);
+    cudaFree(P->lane[0].stage);
+    cudaFree(P->lane[1].stage);
+    cudaFreeHost(P->host_blobs);
     delete P;
     return fail(EF_ERR_CUDA, "slot pool: stream creation failed");
   }
@@ -514,7 +569,8 @@ ef_status ef_pool_create(const ef_moe_cfg* cfg, const ef_pool_cfg* pc, const ef_
     L.slot_expert.assign(n_slots, -1);
     L.expert_slot.assign(E, -1);
     L.staged.assign(E, 0);
-    cudaEventCreateWithFlags(&L.ready, cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&L.ready[0], cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&L.ready[1], cudaEventDisableTiming);
     cudaEventCreateWithFlags(&L.last_use, cudaEventDisableTiming);
   }
   *out = P;
@@ -553,8 +609,9 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
   int* inds = inds_out ? inds_out : w.inds;
   float* wts = wts_out ? wts_out : w.wts;
   // 1. route this layer, and predict the next layer's experts from the same input
-  if ((s = pool_route(cfg, x, T, gate_w, e_bias, w.logits, inds, wts, st))) return s;
-  if (next_gate_w && (s = pool_route(cfg, x, T, next_gate_w, next_e_bias, w.plogits, w.pinds, w.pwts, st))) return s;
+  if ((s = pool_route(cfg, x, T, gate_w, e_bias, w.logits, inds, wts, next_gate_w, next_e_bias, w.plogits, w.pinds,
+                      w.pwts, st)))
+    return s;
   if (n > P->h_cap) {
     if (P->h_inds) cudaFreeHost(P->h_inds);
     P->h_cap = std::max(n, 256);
@@ -586,20 +643,20 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
       const int sl = take_slot(P, nl, nkeep);
       if (sl < 0) break;  // no free slot: the prediction is only a hint
       if (!any) {
-        copies_begin(P, N);
-        t = timer_begin(P);
+        copies_begin(P, 1, N);
+        t = timer_begin(P, P->lane[1].stream);
         any = true;
       }
-      if ((s = copy_expert(P, nl, e, sl))) return s;
+      if ((s = copy_expert(P, 1, nl, e, sl))) return s;
       N.staged[e] = 1;
       P->st.copies_prefetch++;
     }
     if (any) {
-      if ((s = flush_stage(P))) return s;
-      cudaEventRecord(t.b, P->copy);
+      if ((s = flush_stage(P, 1))) return s;
+      cudaEventRecord(t.b, P->lane[1].stream);
       P->timers.push_back(t);
-      cudaEventRecord(N.ready, P->copy);
-      N.has_ready = true;
+      cudaEventRecord(N.ready[1], P->lane[1].stream);
+      N.has_ready[1] = true;
     }
   }
   // 3. resolve this layer's experts (ef_engine.py:650-675): policy get, put on a miss
@@ -631,21 +688,23 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
       P->st.evictions++;
     }
     if (!any) {
-      copies_begin(P, L);
-      t = timer_begin(P);
+      copies_begin(P, 0, L);
+      t = timer_begin(P, P->lane[0].stream);
       any = true;
     }
-    if ((s = copy_expert(P, layer, e, sl))) return s;
+    if ((s = copy_expert(P, 0, layer, e, sl))) return s;
     P->st.copies_sync++;
   }
   if (any) {
-    if ((s = flush_stage(P))) return s;
-    cudaEventRecord(t.b, P->copy);
+    if ((s = flush_stage(P, 0))) return s;
+    cudaEventRecord(t.b, P->lane[0].stream);
     P->timers.push_back(t);
-    cudaEventRecord(L.ready, P->copy);
-    L.has_ready = true;
+    cudaEventRecord(L.ready[0], P->lane[0].stream);
+    L.has_ready[0] = true;
   }
-  if (L.has_ready) cudaStreamWaitEvent(st, L.ready, 0);
+  // this layer's experts wait for both lanes' copies into its slots
+  for (int ln = 0; ln < 2; ++ln)
+    if (L.has_ready[ln]) cudaStreamWaitEvent(st, L.ready[ln], 0);
   // 4. experts on slot ids
   // slot ids stay in pinned memory: the permute kernel reads them over the
   // link (n ints) instead of a copy that would queue behind the expert copies
@@ -661,6 +720,43 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
   cudaEventRecord(L.last_use, st);
   L.has_use = true;
   return EF_OK;
+}
+
+size_t ef_pool_decode_workspace_size(const ef_slot_pool* P, int T) {
+  if (!P || T < 0) return 0;
+  const size_t H = P->cfg.hidden;
+  return ((size_t)T * H * 2 + 255) / 256 * 256 + ((size_t)T * H * 4 + 255) / 256 * 256 + ef_pool_workspace_size(P, T) +
+         256;
+}
+
+ef_status ef_pool_decode_step(ef_slot_pool* P, float* r, int T, const void* const* gate_w,
+                              const float* const* e_bias, int lookahead, float eps, void* workspace, size_t ws_bytes,
+                              void* stream) {
+  if (!P) return fail(EF_ERR_INVALID, "pool is NULL");
+  if (T < 0) return fail(EF_ERR_INVALID, "T < 0");
+  if (T == 0) return EF_OK;
+  if (!r || !gate_w) return fail(EF_ERR_INVALID, "null pointer");
+  if (ws_bytes < ef_pool_decode_workspace_size(P, T) || !workspace) return fail(EF_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int H = P->cfg.hidden, L = P->pc.n_layers;
+  const int bf = P->cfg.act_dtype == EF_DT_BF16;
+  Carver c{static_cast<uint8_t*>(workspace)};
+  uint16_t* x = c.take<uint16_t>((size_t)T * H);
+  float* y = c.take<float>((size_t)T * H);
+  void* fws = c.take<uint8_t>(ef_pool_workspace_size(P, T));
+  const size_t fws_bytes = ef_pool_workspace_size(P, T);
+  ef_status s;
+  for (int l = 0; l < L; ++l) {
+    EF_LAUNCH("add_rmsnorm", (ef::add_rmsnorm_kernel<<<T, ef::kNormThreads, 0, st>>>(r, l ? y : nullptr, H, eps, bf, x),
+                              cudaGetLastError()));
+    const bool la = lookahead && l + 1 < L;
+    if ((s = ef_pool_moe_forward(P, l, x, T, gate_w[l], e_bias ? e_bias[l] : nullptr, la ? gate_w[l + 1] : nullptr,
+                                 la && e_bias ? e_bias[l + 1] : nullptr, y, 1, nullptr, nullptr, fws, fws_bytes, st)))
+      return s;
+  }
+  EF_LAUNCH("add_rmsnorm", (ef::add_rmsnorm_kernel<<<T, ef::kNormThreads, 0, st>>>(r, y, H, eps, bf, nullptr),
+                            cudaGetLastError()));
+  return ef_pool_end_token(P);
 }
 
 ef_status ef_pool_end_token(ef_slot_pool* P) {
@@ -688,7 +784,7 @@ ef_status ef_pool_resident(const ef_slot_pool* P, int layer, int32_t* experts, i
 
 ef_status ef_pool_get_stats(ef_slot_pool* P, ef_pool_stats* out) {
   if (!P || !out) return fail(EF_ERR_INVALID, "null pointer");
-  cudaStreamSynchronize(P->copy);
+  for (auto& C : P->lane) cudaStreamSynchronize(C.stream);
   fold_timers(P, true);
   *out = P->st;
   return EF_OK;
@@ -696,7 +792,7 @@ ef_status ef_pool_get_stats(ef_slot_pool* P, ef_pool_stats* out) {
 
 ef_status ef_pool_reset_stats(ef_slot_pool* P) {
   if (!P) return fail(EF_ERR_INVALID, "pool is NULL");
-  cudaStreamSynchronize(P->copy);
+  for (auto& C : P->lane) cudaStreamSynchronize(C.stream);
   fold_timers(P, true);
   P->st = ef_pool_stats{};
   return EF_OK;
@@ -704,19 +800,22 @@ ef_status ef_pool_reset_stats(ef_slot_pool* P) {
 
 ef_status ef_pool_destroy(ef_slot_pool* P) {
   if (!P) return EF_OK;
-  cudaStreamSynchronize(P->copy);
+  for (auto& C : P->lane) cudaStreamSynchronize(C.stream);
   fold_timers(P, true);
   for (auto& t : P->spare) {
     cudaEventDestroy(t.a);
     cudaEventDestroy(t.b);
   }
   for (auto& L : P->layers) {
-    cudaEventDestroy(L.ready);
+    cudaEventDestroy(L.ready[0]);
+    cudaEventDestroy(L.ready[1]);
     cudaEventDestroy(L.last_use);
   }
-  cudaStreamDestroy(P->copy);
+  for (auto& C : P->lane) {
+    cudaStreamDestroy(C.stream);
+    cudaFree(C.stage);
+  }
   cudaFree(P->dev_mem);
-  cudaFree(P->stage);
   if (P->host_blobs) cudaFreeHost(P->host_blobs);
   if (P->h_inds) cudaFreeHost(P->h_inds);
   delete P;

@@ -68,11 +68,19 @@ EF_DEV void cvt8(const uint4& v, int is_bf16, float (&f)[8]) {
   }
 }
 
-// CTA = 4 warps computes logits for TT tokens x TE experts.
+// CTA = 4 warps computes logits for TT tokens x TE experts.  blockIdx.z = 1
+// takes a second gate (wg2 -> logits2) over the same tokens, so a layer's
+// routing and the next layer's prediction share one launch.
 template <int TT, int TE>
 __global__ void __launch_bounds__(128) router_logits_kernel(const uint16_t* __restrict__ x, int x_bf16,
                                                             const uint16_t* __restrict__ wg, int w_bf16,
-                                                            int T, int E, int H, float* __restrict__ logits) {
+                                                            int T, int E, int H, float* __restrict__ logits,
+                                                            const uint16_t* __restrict__ wg2,
+                                                            float* __restrict__ logits2) {
+  if (blockIdx.z) {
+    wg = wg2;
+    logits = logits2;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * TT, e0 = blockIdx.y * TE;
   const int nch = H >> 3;
@@ -103,7 +111,7 @@ __global__ void __launch_bounds__(128) router_logits_kernel(const uint16_t* __re
 #pragma unroll
       for (int b = 0; b < TE; ++b)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(xf[a][i], wf[b][i]));
+        for (int i = 0; i < 8; ++i) acc[a][b] = __fmaf_rn(xf[a][i], wf[b][i], acc[a][b]);  // exact product: one rounding either way
   }
   __shared__ float part[4][TT][TE];
 #pragma unroll
@@ -147,11 +155,22 @@ EF_DEV void warp_argmax(float& v, int& i) {
 constexpr int kMaxE = 512;
 constexpr int kSelWarps = 4;
 
-// One warp per token.  Scores live in shared memory (E <= 512).
+// One warp per token.  Scores live in shared memory (E <= 512).  blockIdx.y = 1
+// selects the second gate's logits / bias / outputs (see router_logits_kernel).
 __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const float* __restrict__ logits,
                                                                        const float* __restrict__ e_bias, int T,
                                                                        SelCfg cfg, int* __restrict__ inds,
-                                                                       float* __restrict__ wts) {
+                                                                       float* __restrict__ wts,
+                                                                       const float* __restrict__ logits2,
+                                                                       const float* __restrict__ e_bias2,
+                                                                       int* __restrict__ inds2,
+                                                                       float* __restrict__ wts2) {
+  if (blockIdx.y) {
+    logits = logits2;
+    e_bias = e_bias2;
+    inds = inds2;
+    wts = wts2;
+  }
   __shared__ float s_score[kSelWarps][kMaxE];  // selection score
   __shared__ float s_keep[kSelWarps][kMaxE];   // sigmoid value / logit for weights
   __shared__ float s_gs[kSelWarps][32];
@@ -253,31 +272,35 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const flo
 }
 
 // ---------------------------------------------------------------- launchers
+// wg2 / logits2 (optional): a second gate routed in the same launch.
 cudaError_t launch_router_logits(const uint16_t* x, int x_bf16, const uint16_t* wg, int w_bf16, int T, int E,
-                                 int H, float* logits, cudaStream_t st) {
+                                 int H, float* logits, cudaStream_t st, const uint16_t* wg2, float* logits2) {
+  const int nz = wg2 ? 2 : 1;
   if (T >= 64) {
-    dim3 grid((T + 7) / 8, (E + 7) / 8);
-    router_logits_kernel<8, 8><<<grid, 128, 0, st>>>(x, x_bf16, wg, w_bf16, T, E, H, logits);
+    dim3 grid((T + 7) / 8, (E + 7) / 8, nz);
+    router_logits_kernel<8, 8><<<grid, 128, 0, st>>>(x, x_bf16, wg, w_bf16, T, E, H, logits, wg2, logits2);
   } else if (T >= 4) {
-    dim3 grid((T + 3) / 4, (E + 3) / 4);
-    router_logits_kernel<4, 4><<<grid, 128, 0, st>>>(x, x_bf16, wg, w_bf16, T, E, H, logits);
+    dim3 grid((T + 3) / 4, (E + 3) / 4, nz);
+    router_logits_kernel<4, 4><<<grid, 128, 0, st>>>(x, x_bf16, wg, w_bf16, T, E, H, logits, wg2, logits2);
   } else {
     int te = (E >= 256) ? 2 : 1;
-    dim3 grid(T, (E + te - 1) / te);
+    dim3 grid(T, (E + te - 1) / te, nz);
     if (te == 2)
-      router_logits_kernel<1, 2><<<grid, 128, 0, st>>>(x, x_bf16, wg, w_bf16, T, E, H, logits);
+      router_logits_kernel<1, 2><<<grid, 128, 0, st>>>(x, x_bf16, wg, w_bf16, T, E, H, logits, wg2, logits2);
     else
-      router_logits_kernel<1, 1><<<grid, 128, 0, st>>>(x, x_bf16, wg, w_bf16, T, E, H, logits);
+      router_logits_kernel<1, 1><<<grid, 128, 0, st>>>(x, x_bf16, wg, w_bf16, T, E, H, logits, wg2, logits2);
   }
   return cudaGetLastError();
 }
 
 cudaError_t launch_router_select(const float* logits, const float* e_bias, int T, int E, int k, int mode,
                                  int norm_topk, int n_group, int topk_group, float scaling, int* inds, float* wts,
-                                 cudaStream_t st) {
+                                 cudaStream_t st, const float* logits2, const float* e_bias2, int* inds2,
+                                 float* wts2) {
   SelCfg c{E, k, mode, norm_topk, n_group, topk_group, scaling};
-  dim3 grid((T + kSelWarps - 1) / kSelWarps);
-  router_select_kernel<<<grid, kSelWarps * 32, 0, st>>>(logits, e_bias, T, c, inds, wts);
+  dim3 grid((T + kSelWarps - 1) / kSelWarps, logits2 ? 2 : 1);
+  router_select_kernel<<<grid, kSelWarps * 32, 0, st>>>(logits, e_bias, T, c, inds, wts, logits2, e_bias2, inds2,
+                                                          wts2);
   return cudaGetLastError();
 }
 

@@ -170,6 +170,29 @@ class ExpertSlotPool:
             wts_out.data_ptr() if wts_out is not None else None, ws.data_ptr(), ws.numel(), _stream_ptr(xf.device)))
         return y.reshape(x.shape)
 
+    def decode_step(self, r: torch.Tensor, gates: Sequence[MoEGate], lookahead: bool = True,
+                    eps: float = 1e-6) -> torch.Tensor:
+        """One decode step through all layers in the library (ef_pool_decode_step):
+        per layer r += y, x = rmsnorm(r), y = MoE_layer(x); then r += y and the
+        per-token trim.  r: fp32 [T, H] residual stream, updated in place."""
+        if r.dtype != torch.float32 or not r.is_cuda or not r.is_contiguous():
+            raise ValueError("r must be a contiguous fp32 CUDA tensor")
+        if len(gates) != self.n_layers:
+            raise ValueError("one gate per layer")
+        T = r.reshape(-1, self.spec.hidden).shape[0]
+        key = tuple(g.weight.data_ptr() for g in gates)
+        if getattr(self, "_gate_key", None) != key:
+            self._gate_ptrs = (ctypes.c_void_p * self.n_layers)(*[g.weight.data_ptr() for g in gates])
+            self._bias_ptrs = (ctypes.c_void_p * self.n_layers)(
+                *[g.e_score_correction_bias.data_ptr() if g.e_score_correction_bias is not None else None
+                  for g in gates])
+            self._gate_key = key
+        n = L.lib().ef_pool_decode_workspace_size(self._h, T)
+        ws = workspace(n, r.device)
+        L.check(L.lib().ef_pool_decode_step(self._h, r.data_ptr(), T, self._gate_ptrs, self._bias_ptrs, int(lookahead),
+                                            eps, ws.data_ptr(), ws.numel(), _stream_ptr(r.device)))
+        return r
+
     def end_token(self) -> None:
         L.check(L.lib().ef_pool_end_token(self._h))
 

@@ -264,6 +264,16 @@ ef_status ef_pool_moe_forward(ef_slot_pool* pool, int layer, const void* x, int 
                               int out_f32, int32_t* inds_out, float* wts_out, void* workspace,
                               size_t workspace_bytes, void* stream);
 ef_status ef_pool_end_token(ef_slot_pool* pool); /* trim + decay every layer (once per token) */
+/* One decode step through all n_layers pooled layers: for each layer,
+ * r += y (from the previous layer), x = r / sqrt(mean(r^2) + eps) in the
+ * activation dtype (the pre-MoE norm), y = ef_pool_moe_forward(layer, x) with
+ * the next layer's gate as lookahead when `lookahead`; finally r += y and
+ * ef_pool_end_token.  r [T, H] fp32 (the residual stream) is updated in place;
+ * gate_w / e_bias: n_layers device pointers (e_bias may be NULL, or hold NULLs). */
+size_t ef_pool_decode_workspace_size(const ef_slot_pool* pool, int T);
+ef_status ef_pool_decode_step(ef_slot_pool* pool, float* r, int T, const void* const* gate_w,
+                              const float* const* e_bias, int lookahead, float eps, void* workspace,
+                              size_t workspace_bytes, void* stream);
 ef_status ef_pool_resident(const ef_slot_pool* pool, int layer, int32_t* experts, int cap, int* n);
 ef_status ef_pool_get_stats(ef_slot_pool* pool, ef_pool_stats* out);
 ef_status ef_pool_reset_stats(ef_slot_pool* pool);

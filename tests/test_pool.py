@@ -154,3 +154,40 @@ def test_pool_rejects_device_arrays(P):
     host[0]["gate"] = tuple(a.cuda() for a in host[0]["gate"])
     with pytest.raises(ValueError):
         P.ExpertSlotPool(spec, host, budget=4)
+
+
+@pytest.mark.gpu
+def test_pool_decode_step_independent_of_residency(P):
+    """The in-library multi-layer decode step: a pool with 6 of 32 experts per
+    layer in HBM and one holding every expert produce bit-identical residual
+    streams (residency changes where weights come from, never the result)."""
+    import torch
+    from expertflow_b200 import moe, synthetic
+
+    spec = _small_spec()
+    n_layers, steps = 4, 6
+    dev = torch.device("cuda")
+    host = P.make_host_layers(spec, n_layers, seed=200)
+    bias = torch.from_numpy(P.zipf_layer_bias(n_layers, spec.n_experts, 1.1, seed=9)).to(dev)
+    gates = []
+    for layer in range(n_layers):
+        g = torch.Generator(device=dev)
+        g.manual_seed(700 + layer)
+        gw = (torch.randn((spec.n_experts, spec.hidden), generator=g, device=dev) * 0.02).to(torch.float16)
+        gates.append(moe.MoEGate(gw, spec.top_k, "softmax", True, e_score_correction_bias=bias[layer].contiguous()))
+    out = []
+    for budget, la in ((6, True), (spec.n_experts, False)):
+        pl = P.ExpertSlotPool(spec, host, budget=budget, headroom=spec.top_k)
+        rs = []
+        for t in range(steps):
+            r = synthetic.make_x_torch(spec, 2, seed=40 + t).float().contiguous()
+            pl.decode_step(r, gates, lookahead=la)
+            rs.append(r.clone())
+        torch.cuda.synchronize()
+        out.append((torch.stack(rs), pl.stats()))
+        pl.close()
+    (ra, sa), (rb, sb) = out
+    assert torch.isfinite(ra).all() and torch.equal(ra, rb)
+    assert sa["tokens"] == steps and sa["copies_prefetch"] > 0
+    assert sb["copies_sync"] <= spec.n_experts * n_layers
+    assert moe.device_error() == 0
