@@ -110,16 +110,37 @@ struct QmvSmem {
   uint64_t* sync;      // [2] epilogue staging
 };
 
-// Dot products of one 64-column group for rows rA, rB of matrix m and the
-// segment's 8 tokens; folds the group's affine scale into y.
-template <int BITS, int MODE>
-EF_DEV void qmv_group(const uint8_t* cm, const uint4 (&blk)[2], int G, int rA, int rB, int t, float sA, float sB,
-                      float bA, float bB, float x0, float x1, float (&y)[4]) {
-  float D[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+// The code words of one 64-column group for rows rA, rB (8 bytes of each row at
+// 4 bits, 16 at 8 bits), read from a 128-byte-swizzled stage tile.
+template <int BITS>
+struct GroupCodes {
+  uint4 a, b;  // 4 bits: .x/.y used
+};
+template <int BITS>
+EF_DEV GroupCodes<BITS> load_group_codes(const uint8_t* cm, int G, int rA, int rB, int t) {
+  GroupCodes<BITS> c;
   if constexpr (BITS == 4) {
     const int chunk = 2 * G + (t >> 1);
     const uint2 va = *reinterpret_cast<const uint2*>(cm + rA * 128 + ((chunk ^ (rA & 7)) << 4) + 8 * (t & 1));
     const uint2 vb = *reinterpret_cast<const uint2*>(cm + rB * 128 + ((chunk ^ (rB & 7)) << 4) + 8 * (t & 1));
+    c.a = make_uint4(va.x, va.y, 0u, 0u);
+    c.b = make_uint4(vb.x, vb.y, 0u, 0u);
+  } else {
+    const int chunk = 4 * G + t;
+    c.a = *reinterpret_cast<const uint4*>(cm + rA * 128 + ((chunk ^ (rA & 7)) << 4));
+    c.b = *reinterpret_cast<const uint4*>(cm + rB * 128 + ((chunk ^ (rB & 7)) << 4));
+  }
+  return c;
+}
+
+// Dot products of one 64-column group for rows rA, rB of matrix m and the
+// segment's 8 tokens; folds the group's affine scale into y.
+template <int BITS, int MODE>
+EF_DEV void qmv_group_regs(const GroupCodes<BITS>& cw, const uint4 (&blk)[2], float sA, float sB, float bA, float bB,
+                           float x0, float x1, float (&y)[4]) {
+  float D[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  if constexpr (BITS == 4) {
+    const uint2 va = make_uint2(cw.a.x, cw.a.y), vb = make_uint2(cw.b.x, cw.b.y);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t wa = h ? va.y : va.x, wb = h ? vb.y : vb.x;
@@ -132,9 +153,7 @@ EF_DEV void qmv_group(const uint8_t* cm, const uint4 (&blk)[2], int G, int rA, i
       mma_16816(D[1], a1, blk[h].z, blk[h].w);
     }
   } else {
-    const int chunk = 4 * G + t;
-    const uint4 va = *reinterpret_cast<const uint4*>(cm + rA * 128 + ((chunk ^ (rA & 7)) << 4));
-    const uint4 vb = *reinterpret_cast<const uint4*>(cm + rB * 128 + ((chunk ^ (rB & 7)) << 4));
+    const uint4 va = cw.a, vb = cw.b;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t wa0 = h ? va.z : va.x, wa1 = h ? va.w : va.y;  // row A: cols 0-3, 4-7 of block h
@@ -152,6 +171,12 @@ EF_DEV void qmv_group(const uint8_t* cm, const uint4 (&blk)[2], int G, int rA, i
   y[1] = fmaf(sA, D[0][1] + D[1][1], fmaf(bA, x1, y[1]));
   y[2] = fmaf(sB, D[0][2] + D[1][2], fmaf(bB, x0, y[2]));
   y[3] = fmaf(sB, D[0][3] + D[1][3], fmaf(bB, x1, y[3]));
+}
+
+template <int BITS, int MODE>
+EF_DEV void qmv_group(const uint8_t* cm, const uint4 (&blk)[2], int G, int rA, int rB, int t, float sA, float sB,
+                      float bA, float bB, float x0, float x1, float (&y)[4]) {
+  qmv_group_regs<BITS, MODE>(load_group_codes<BITS>(cm, G, rA, rB, t), blk, sA, sB, bA, bB, x0, x1, y);
 }
 
 // One work item for one compute warp.  Returns false after a failed wait.
@@ -205,6 +230,14 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
         blk[G][0] = *reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t) ^ g) << 4));
         blk[G][1] = *reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t + 1) ^ g) << 4));
       }
+      // every code word of the stage up front: the shared-memory latencies
+      // overlap instead of serialising group by group
+      GroupCodes<BITS> cw[S::NMAT][S::GPS];
+#pragma unroll
+      for (int m = 0; m < S::NMAT; ++m)
+#pragma unroll
+        for (int G = 0; G < S::GPS; ++G)
+          cw[m][G] = load_group_codes<BITS>(codes + (size_t)m * kRowTile * S::ROWB, G, rA, rB, t);
 #pragma unroll
       for (int m = 0; m < S::NMAT; ++m) {
         const uint16_t* ms = s_sb + (size_t)m * 2 * kRowTile * sp;
@@ -236,12 +269,11 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
             hbB[G] = (uint16_t)(d >> (16 * G));
           }
         }
-        const uint8_t* cm = codes + (size_t)m * kRowTile * S::ROWB;
 #pragma unroll
         for (int G = 0; G < S::GPS; ++G) {
           const float sA = h16_to_f32(hsA[G]) * kQ, sB = h16_to_f32(hsB[G]) * kQ;
-          qmv_group<BITS, MODE>(cm, blk[G], G, rA, rB, t, sA, sB, h16_to_f32(hbA[G]) - sA,
-                                h16_to_f32(hbB[G]) - sB, xa[G], xb[G], y[m]);
+          qmv_group_regs<BITS, MODE>(cw[m][G], blk[G], sA, sB, h16_to_f32(hbA[G]) - sA, h16_to_f32(hbB[G]) - sB,
+                                     xa[G], xb[G], y[m]);
         }
       }
     } else {
