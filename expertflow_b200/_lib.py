@@ -24,7 +24,7 @@ STATUS = {
 }
 EF_DT_BF16, EF_DT_F16, EF_DT_F32 = 0, 1, 2
 EF_ROUTER_SOFTMAX, EF_ROUTER_SIGMOID_GROUP = 0, 1
-EF_PATH_AUTO, EF_PATH_GEMV, EF_PATH_GEMM = 0, 1, 2
+EF_PATH_AUTO, EF_PATH_GEMV, EF_PATH_GEMM, EF_PATH_GEMM_PAIR = 0, 1, 2, 3
 
 
 class EfmoeUnavailable(RuntimeError):

@@ -32,6 +32,7 @@ cudaError_t launch_combine(const float* rows, const int* inv, const float* wts, 
 cudaError_t launch_qmv(int bits, int mode, const QmvParams& p, int n_sm, cudaStream_t st);
 size_t qmv_smem_required(int bits, int mode, int K);
 cudaError_t launch_qgemm(int bits, int mode, const GemmParams& p, int n_sm, cudaStream_t st);
+cudaError_t launch_qgemm2(int bits, int mode, const GemmParams& p, int n_sm, cudaStream_t st);
 size_t qgemm_smem_required(int bits);
 cudaError_t launch_dequantize(const uint32_t* w, const uint16_t* s, const uint16_t* b, int rows, int cols, int bits,
                               void* out, int out_dtype, cudaStream_t st);
@@ -170,13 +171,13 @@ ef_status encode_gemm_codes_map(CUtensorMap* m, const uint32_t* w, long long row
   return EF_OK;
 }
 
-// Activation rows for the grouped GEMM: box 64 columns x 32 rows, 128-B swizzle.
-ef_status encode_gemm_act_map(CUtensorMap* m, const uint16_t* act, long long rows, int K) {
+// Activation rows for the grouped GEMM: box 64 columns x box_rows rows, 128-B swizzle.
+ef_status encode_gemm_act_map(CUtensorMap* m, const uint16_t* act, long long rows, int K, int box_rows = 32) {
   PFN_encodeTiled_t enc = get_encoder();
   if (!enc) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {64, 32};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(act), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -332,39 +333,46 @@ ef_status run_experts_gemm(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, co
                            const ef_qweight* sd, cudaStream_t st) {
   const int H = c->hidden, I = c->inter, E = c->n_experts, bits = c->bits;
   const int nsm = sm_count();
+  // single-SM kernel unless the SM-pair kernel (cta_group::2) is requested:
+  // both tile 256 weight rows x <= 192 token rows per tile, so the pair loads
+  // the same activation bytes and dequantises the same codes per FLOP, and its
+  // cross-SM handshakes made it slower on B200 (4.5 ms vs 3.2 ms for the
+  // 4096-token DeepSeek-V3-shaped gate_up)
+  const bool pairs = c->path == EF_PATH_GEMM_PAIR && nsm >= 2;
+  const int cb0 = pairs ? 64 : 128, cb1 = 128, ab = pairs ? 16 : 32;
   ef_status s;
   GemmParams g0;
   memset(&g0, 0, sizeof(g0));
-  if ((s = encode_gemm_codes_map(&g0.tm_c0, gate.w, (long long)E * I, H * bits / 32, bits, 128))) return s;
-  if ((s = encode_gemm_codes_map(&g0.tm_c1, up.w, (long long)E * I, H * bits / 32, bits, 128))) return s;
+  if ((s = encode_gemm_codes_map(&g0.tm_c0, gate.w, (long long)E * I, H * bits / 32, bits, cb0))) return s;
+  if ((s = encode_gemm_codes_map(&g0.tm_c1, up.w, (long long)E * I, H * bits / 32, bits, cb0))) return s;
   if (sg) {
-    if ((s = encode_gemm_codes_map(&g0.tm_sc0, sg->w, I, H * bits / 32, bits, 128))) return s;
-    if ((s = encode_gemm_codes_map(&g0.tm_sc1, su->w, I, H * bits / 32, bits, 128))) return s;
+    if ((s = encode_gemm_codes_map(&g0.tm_sc0, sg->w, I, H * bits / 32, bits, cb0))) return s;
+    if ((s = encode_gemm_codes_map(&g0.tm_sc1, su->w, I, H * bits / 32, bits, cb0))) return s;
     g0.ss0 = sg->scales; g0.sb0 = sg->biases; g0.ss1 = su->scales; g0.sb1 = su->biases;
   } else {
     g0.tm_sc0 = g0.tm_c0; g0.tm_sc1 = g0.tm_c1;
     g0.ss0 = gate.scales; g0.sb0 = gate.biases; g0.ss1 = up.scales; g0.sb1 = up.biases;
   }
   g0.s0 = gate.scales; g0.b0 = gate.biases; g0.s1 = up.scales; g0.b1 = up.biases;
-  if ((s = encode_gemm_act_map(&g0.tm_act, f.x16, n_rows, H))) return s;
+  if ((s = encode_gemm_act_map(&g0.tm_act, f.x16, n_rows, H, ab))) return s;
   g0.seg_expert = f.pb.seg_expert; g0.seg_row0 = f.pb.seg_row0; g0.seg_nrows = f.pb.seg_nrows; g0.n_seg = f.pb.n_seg;
   g0.K = H; g0.R = I; g0.n_experts = E; g0.h_out = f.h16;
-  EF_LAUNCH("qgemm_gate_up", launch_qgemm(bits, 0, g0, nsm, st));
+  EF_LAUNCH("qgemm_gate_up", pairs ? launch_qgemm2(bits, 0, g0, nsm, st) : launch_qgemm(bits, 0, g0, nsm, st));
   GemmParams g1;
   memset(&g1, 0, sizeof(g1));
-  if ((s = encode_gemm_codes_map(&g1.tm_c0, down.w, (long long)E * H, I * bits / 32, bits, 128))) return s;
+  if ((s = encode_gemm_codes_map(&g1.tm_c0, down.w, (long long)E * H, I * bits / 32, bits, cb1))) return s;
   if (sd) {
-    if ((s = encode_gemm_codes_map(&g1.tm_sc0, sd->w, H, I * bits / 32, bits, 128))) return s;
+    if ((s = encode_gemm_codes_map(&g1.tm_sc0, sd->w, H, I * bits / 32, bits, cb1))) return s;
     g1.ss0 = sd->scales; g1.sb0 = sd->biases;
   } else {
     g1.tm_sc0 = g1.tm_c0; g1.ss0 = down.scales; g1.sb0 = down.biases;
   }
   g1.tm_c1 = g1.tm_c0; g1.tm_sc1 = g1.tm_sc0;
   g1.s0 = down.scales; g1.b0 = down.biases;
-  if ((s = encode_gemm_act_map(&g1.tm_act, f.h16, n_rows, I))) return s;
+  if ((s = encode_gemm_act_map(&g1.tm_act, f.h16, n_rows, I, ab))) return s;
   g1.seg_expert = f.pb.seg_expert; g1.seg_row0 = f.pb.seg_row0; g1.seg_nrows = f.pb.seg_nrows; g1.n_seg = f.pb.n_seg;
   g1.K = I; g1.R = H; g1.n_experts = E; g1.y_out = f.yrows;
-  EF_LAUNCH("qgemm_down", launch_qgemm(bits, 1, g1, nsm, st));
+  EF_LAUNCH("qgemm_down", pairs ? launch_qgemm2(bits, 1, g1, nsm, st) : launch_qgemm(bits, 1, g1, nsm, st));
   return EF_OK;
 }
 
@@ -372,7 +380,7 @@ ef_status run_experts_gemm(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, co
 bool use_gemm(const ef_moe_cfg* c, int n_rows, int n_ent) {
   // code boxes are 128 rows tall: both projections need at least that many rows
   if (n_rows < 128 || c->inter < 128 || c->hidden < 128) return false;
-  if (c->path == EF_PATH_GEMM) return true;
+  if (c->path == EF_PATH_GEMM || c->path == EF_PATH_GEMM_PAIR) return true;
   if (c->path == EF_PATH_GEMV) return false;
   return (long long)n_ent >= 32LL * c->n_experts;  // >= 32 routed rows per expert on average
 }

@@ -5,6 +5,7 @@
 #include "ef_dequant.cu"
 #include "ef_qmv.cu"
 #include "ef_qgemm.cu"
+#include "ef_qgemm2.cu"
 #include "ef_api.cu"
 #include "ef_pool.cu"
 #include "ef_ep.cu"

@@ -52,7 +52,7 @@ typedef int ef_status;
 
 enum { EF_DT_BF16 = 0, EF_DT_F16 = 1, EF_DT_F32 = 2 };
 enum { EF_ROUTER_SOFTMAX = 0, EF_ROUTER_SIGMOID_GROUP = 1 };
-enum { EF_PATH_AUTO = 0, EF_PATH_GEMV = 1, EF_PATH_GEMM = 2 };
+enum { EF_PATH_AUTO = 0, EF_PATH_GEMV = 1, EF_PATH_GEMM = 2, EF_PATH_GEMM_PAIR = 3 };
 
 /* One stack of quantised projections (see layout above). */
 typedef struct {
@@ -80,7 +80,8 @@ typedef struct {
   int shared_inter;   /* I of the shared expert */
   int act_dtype;      /* EF_DT_BF16 or EF_DT_F16 (x and y) */
   int gate_dtype;     /* EF_DT_F16 or EF_DT_BF16 (router weight) */
-  int path;           /* EF_PATH_AUTO / GEMV (decode kernels) / GEMM (tcgen05 grouped GEMM) */
+  int path;           /* EF_PATH_AUTO / GEMV (decode kernels) / GEMM (tcgen05 grouped GEMM, one SM per tile) /
+                         GEMM_PAIR (the same contraction on SM pairs, cta_group::2) */
   int out_f32;        /* 1: y is fp32 (the combine's accumulator); 0: y has act_dtype */
 } ef_moe_cfg;
 

@@ -285,7 +285,7 @@ def test_gemm_path_matches_oracle(bits, shared, T, H, I):
     xb = synthetic.make_x_np(spec, T, 7)
     x = _x_tensor(xb, spec)
     out = {}
-    for path in (L.EF_PATH_GEMM, L.EF_PATH_GEMV):
+    for path in (L.EF_PATH_GEMM, L.EF_PATH_GEMM_PAIR, L.EF_PATH_GEMV):
         m = moe.MoELayer.from_arrays(spec, layer, path=path)
         inds = torch.empty((T, spec.top_k), dtype=torch.int32, device="cuda")
         out[path] = (m(x, inds_out=inds, out_dtype=torch.float32), inds)
@@ -296,6 +296,8 @@ def test_gemm_path_matches_oracle(bits, shared, T, H, I):
     for path, (y, inds) in out.items():
         np.testing.assert_array_equal(inds.cpu().numpy(), i_ref)
         assert_ffn_close(y.cpu().numpy(), y_ref, what=f"path {path}")
+    # the SM-pair kernel accumulates the same products in the same k order
+    assert torch.equal(out[L.EF_PATH_GEMM][0], out[L.EF_PATH_GEMM_PAIR][0])
 
 
 def test_prefill_deepseek_v3_8bit_sampled():
