@@ -125,63 +125,117 @@ PFN_encodeTiled_t get_encoder() {
   return fn;
 }
 
+// A tensor map depends only on (base, shape, box, swizzle), which repeat call
+// after call for a layer's weights and workspaces, while an encode costs
+// microseconds of host time: a small per-thread cache of encoded 2-D maps keeps
+// the encodes off the launch path.
+static CUresult encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, const cuuint64_t* dims,
+                          const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw,
+                          CUtensorMapL2promotion l2) {
+  struct Entry {
+    CUtensorMap map;
+    const void* base;
+    cuuint64_t d0, d1, s0;
+    cuuint32_t b0, b1;
+    int dt, sw, l2;
+    bool valid;
+  };
+  static thread_local Entry cache[256];
+  uint64_t h = reinterpret_cast<uintptr_t>(base) * 0x9E3779B97F4A7C15ull;
+  h ^= (dims[0] * 0x100000001B3ull) ^ (dims[1] * 0xC2B2AE3D27D4EB4Full) ^ ((uint64_t)box[1] << 40) ^
+       ((uint64_t)box[0] << 48) ^ ((uint64_t)dt << 56) ^ ((uint64_t)sw << 60);
+  Entry& e = cache[(h ^ (h >> 29)) & 255];
+  if (e.valid && e.base == base && e.d0 == dims[0] && e.d1 == dims[1] && e.s0 == strides[0] && e.b0 == box[0] &&
+      e.b1 == box[1] && e.dt == (int)dt && e.sw == (int)sw && e.l2 == (int)l2) {
+    *m = e.map;
+    return CUDA_SUCCESS;
+  }
+  PFN_encodeTiled_t enc = get_encoder();
+  if (!enc) return CUDA_ERROR_NOT_INITIALIZED;
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         sw, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_SUCCESS) {
+    e.map = *m;
+    e.base = base;
+    e.d0 = dims[0]; e.d1 = dims[1]; e.s0 = strides[0];
+    e.b0 = box[0]; e.b1 = box[1];
+    e.dt = (int)dt; e.sw = (int)sw; e.l2 = (int)l2;
+    e.valid = true;
+  }
+  return r;
+}
+
 // 2-D map over packed codes [rows, words], box = 32 words x 64 rows, 128-B swizzle.
 ef_status encode_codes_map(CUtensorMap* m, const uint32_t* w, long long rows, int words) {
-  PFN_encodeTiled_t enc = get_encoder();
-  if (!enc) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
+  if (!get_encoder()) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)words, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)words * 4};
   cuuint32_t box[2] = {32, (cuuint32_t)kRowTile};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(w), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (r != CUDA_SUCCESS) return fail(EF_ERR_INVALID, "tensor map encode failed (%d)", (int)r);
   return EF_OK;
 }
 
 // 2-D map over fp16 activation rows [rows, K]: box 64 columns x 8 rows, 128-B swizzle.
 ef_status encode_act_map(CUtensorMap* m, const uint16_t* act, long long rows, int K) {
-  PFN_encodeTiled_t enc = get_encoder();
-  if (!enc) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
+  if (!get_encoder()) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)(rows > 0 ? rows : 1)};
   cuuint64_t strides[1] = {(cuuint64_t)K * 2};
   cuuint32_t box[2] = {64, (cuuint32_t)kTokChunk};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(act), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, act, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
   if (r != CUDA_SUCCESS) return fail(EF_ERR_INVALID, "activation tensor map encode failed (%d)", (int)r);
   return EF_OK;
+}
+
+// fp16 scales or biases [rows, ng] for the decode GEMV's scale chunks: box 32
+// groups x 64 rows, 64-byte swizzle.  Needs 16-byte rows (ng % 8 == 0) and a
+// 16-byte-aligned base; false (nothing recorded) when the map cannot be made.
+static bool encode_scales_map(CUtensorMap* m, const uint16_t* a, long long rows, int ng) {
+  if (!get_encoder() || !a || ng % 8 || !aligned16(a) || rows < kRowTile) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)ng, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ng * 2};
+  cuuint32_t box[2] = {32, (cuuint32_t)kRowTile};
+  return encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B) == CUDA_SUCCESS;
+}
+
+// Chunked scale streaming for a GEMV launch whose scale pointers are set:
+// maps over the routed arrays (rows = E * R) and the shared expert's (rows =
+// shared_rows); whole-item scale slots when any map cannot be made.
+static void set_scale_maps(QmvParams& p, long long rows, long long shared_rows) {
+  p.sb_chunked = 0;
+  const uint16_t* arr[8] = {p.s0, p.b0, p.s1 ? p.s1 : p.s0, p.b1 ? p.b1 : p.b0,
+                            p.ss0, p.sb0, p.ss1 ? p.ss1 : p.ss0, p.sb1 ? p.sb1 : p.sb0};
+  for (int i = 0; i < 8; ++i)
+    if (!encode_scales_map(&p.tm_sc[i], arr[i], i < 4 ? rows : shared_rows, p.K / 64)) return;
+  p.sb_chunked = 1;
 }
 
 // Code tiles for the grouped GEMM: box (chunk of 64 columns) x box_rows rows,
 // swizzle matching the 64-byte (8-bit) / 32-byte (4-bit) row chunk.
 ef_status encode_gemm_codes_map(CUtensorMap* m, const uint32_t* w, long long rows, int words, int bits, int box_rows) {
-  PFN_encodeTiled_t enc = get_encoder();
-  if (!enc) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
+  if (!get_encoder()) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)words, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)words * 4};
   cuuint32_t box[2] = {(cuuint32_t)(64 * bits / 32), (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(w), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, bits == 8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, dims, strides, box,
+                         bits == 8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (r != CUDA_SUCCESS) return fail(EF_ERR_INVALID, "GEMM code tensor map encode failed (%d)", (int)r);
   return EF_OK;
 }
 
 // Activation rows for the grouped GEMM: box 64 columns x box_rows rows, 128-B swizzle.
 ef_status encode_gemm_act_map(CUtensorMap* m, const uint16_t* act, long long rows, int K, int box_rows = 32) {
-  PFN_encodeTiled_t enc = get_encoder();
-  if (!enc) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
+  if (!get_encoder()) return fail(EF_ERR_NOT_READY, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)K * 2};
   cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(act), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, act, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (r != CUDA_SUCCESS) return fail(EF_ERR_INVALID, "GEMM activation tensor map encode failed (%d)", (int)r);
   return EF_OK;
 }
@@ -304,6 +358,7 @@ ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, const e
   p0.act_sum = f.xsum;
   p0.seg_expert = f.pb.seg_expert; p0.seg_row0 = f.pb.seg_row0; p0.seg_nrows = f.pb.seg_nrows; p0.n_seg = f.pb.n_seg;
   p0.K = H; p0.R = I; p0.n_experts = E;
+  set_scale_maps(p0, (long long)E * I, sg ? I : (long long)E * I);
   p0.h_out = f.h16; p0.hsum_out = f.hsum; p0.y_out = nullptr;
   EF_LAUNCH("qmv_gate_up", launch_qmv(bits, 0, p0, nsm, st));
   // mode 1: K = I, R = H
@@ -322,6 +377,7 @@ ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, const e
   p1.act_sum = f.hsum;
   p1.seg_expert = f.pb.seg_expert; p1.seg_row0 = f.pb.seg_row0; p1.seg_nrows = f.pb.seg_nrows; p1.n_seg = f.pb.n_seg;
   p1.K = I; p1.R = H; p1.n_experts = E;
+  set_scale_maps(p1, (long long)E * H, sd ? H : (long long)E * H);
   p1.y_out = f.yrows;
   EF_LAUNCH("qmv_down", launch_qmv(bits, 1, p1, nsm, st));
   return EF_OK;
@@ -648,6 +704,7 @@ static ef_status run_single_matrix(const ef_qweight& w, int n_exp, int out_dim, 
   p.act_sum = f.xsum;
   p.seg_expert = f.pb.seg_expert; p.seg_row0 = f.pb.seg_row0; p.seg_nrows = f.pb.seg_nrows; p.n_seg = f.pb.n_seg;
   p.K = in_dim; p.R = out_dim; p.n_experts = n_exp;
+  set_scale_maps(p, (long long)n_exp * out_dim, (long long)n_exp * out_dim);
   p.y_out = f.yrows;
   EF_LAUNCH("qmv_down", launch_qmv(bits, 1, p, sm_count(), st));
   return EF_OK;

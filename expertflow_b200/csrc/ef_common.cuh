@@ -67,6 +67,12 @@ EF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int32_t c0, int32_t c
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
       : "memory");
 }
+// Prefetch the box of a 2-D tensor map at (c0, c1) into L2.
+EF_DEV void prefetch_tile_l2(const CUtensorMap* map, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
 // 1-D bulk copy global -> shared; dst/src 16-byte aligned, bytes % 16 == 0.
 EF_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

@@ -155,11 +155,6 @@ EF_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
 }
 EF_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 EF_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-EF_DEV void prefetch_tile_l2(const CUtensorMap* map, int32_t c0, int32_t c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1)
-               : "memory");
-}
 
 struct GemmItem {
   int expert, row0_seg, nrows, rt;

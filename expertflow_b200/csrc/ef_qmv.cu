@@ -6,24 +6,31 @@
 //
 // Work item = (segment of <= 8 rows routed to one expert) x (64 weight rows).
 // A CTA has 4 compute warps (16 rows each), a TMA producer warp and a scale
-// producer warp, and loops over work items (persistent; two CTAs per SM when
-// shared memory allows).  The TMA warp streams, per 256-column (4-bit) /
-// 128-column (8-bit) stage, the 64-row code tile of each matrix with a 2-D TMA
-// load (128-byte swizzle) and the segment's activation rows with 1-D bulk
-// copies into an mbarrier ring.  The scale warp bulk-loads, per work item, the
-// tile's fp16 scales/biases (row pitch padded against bank conflicts when the
-// row length allows) and the rows' group sums into one of two slots, so the
-// next item's loads overlap this item's math.
+// producer warp, and loops over work items (persistent; two CTAs per SM).
+//  * The TMA warp streams, per 256-column (4-bit) / 128-column (8-bit) stage,
+//    the 64-row code tile of each matrix (2-D TMA, 128-byte swizzle) and the
+//    segment's activation rows into an mbarrier ring.
+//  * The scale warp streams the tile's fp16 scales and biases in chunks of 32
+//    groups (2-D TMA boxes of 32 groups x 64 rows, 64-byte swizzle, so that a
+//    chunk slot is 16 KB whatever K is and the compute warps' reads are free
+//    of bank conflicts) together with the rows' group sums, into a ring of
+//    slots a chunk or more ahead of the compute warps.  When the row length
+//    is not a multiple of 8 groups (16 bytes) the slot holds a whole item's
+//    scales instead, copied as contiguous blocks.  In mode 0 the same warp
+//    also copies each finished item's h tile from shared memory to h_out, so
+//    the compute warps go straight on to the next item.
 //
 // Dot products run on the tensor cores with exact operands: a code q becomes
-// the fp16 value 1 + q/1024 by masking it into the low mantissa bits (one LOP3
-// per pair of codes plus one shift per nibble/byte position); activations are
-// fp16; products accumulate in fp32 per 64-column group in two independent MMA
-// chains per matrix:
-//     D_g = sum_i x_i (1 + q_i / 1024)
-//     y  += (1024 s_g) D_g + (b_g - 1024 s_g) sum_i x_i    (= sum_i x_i (s_g q_i + b_g))
+// the fp16 value 1024 + q by masking it into the low mantissa bits under the
+// exponent of 1024 (one LOP3 per pair of codes plus one shift per nibble/byte
+// position); activations are fp16; products accumulate in fp32 per 64-column
+// group in one MMA chain per matrix:
+//     D_g = sum_i x_i (1024 + q_i)
+//     y  += s_g D_g + (b_g - 1024 s_g) sum_i x_i    (= sum_i x_i (s_g q_i + b_g))
 // The k order inside mma.m16n8k16 is permuted consistently for codes and
-// activations (see act_pos), which leaves every dot product unchanged.
+// activations (see act_pos), which leaves every dot product unchanged.  The
+// 16 weight rows of an MMA block are taken in the order row_of_lane(), so that
+// the swizzled code words and scales a warp loads fall in distinct banks.
 //
 // mode 0: gate and up tiles together, epilogue h = silu(g) * u stored as fp16
 //         rows in the activation layout + group sums (input of mode 1).
@@ -48,35 +55,93 @@ struct QmvShape {
 };
 constexpr float kQ = 1024.0f;
 
-// Group sums and scales/biases are copied as contiguous blocks (one copy per
-// array per item): their shared-memory row pitch is the global one.
-__host__ __device__ inline int xs_pitch(int K) { return sum_ld(K); }
-__host__ __device__ inline int sb_pitch(int K) { return K / 64; }
-
-template <int BITS, int MODE>
-__host__ __device__ inline size_t qmv_sb_bytes(int K) {  // scales + biases of one item
-  return (size_t)QmvShape<BITS, MODE>::NMAT * 2 * kRowTile * sb_pitch(K) * 2;
-}
-__host__ __device__ inline size_t qmv_xs_bytes(int K) { return (size_t)kTokChunk * xs_pitch(K) * 4; }
-template <int BITS, int MODE>
-__host__ __device__ inline size_t qmv_slot_bytes(int K) {
-  return (qmv_sb_bytes<BITS, MODE>(K) + 127) / 128 * 128 + (qmv_xs_bytes(K) + 127) / 128 * 128;
+// Weight row (within a 16-row MMA block, first half) held by the lanes of group
+// g = lane / 4.  The code tile's 16-byte units are swizzled by row % 8; with
+// 8-byte code loads a half-warp (g = 0..3) then reads rows 0, 2, 4, 6 and
+// covers all 32 banks, with 16-byte loads each 8-lane phase reads rows r and
+// r + 4.
+template <int BITS>
+__host__ __device__ constexpr int row_of_lane(int g) {
+  return BITS == 4 ? 2 * (g & 3) + (g >> 2) : (g >> 1) + 4 * (g & 1);
 }
 
-// Shared memory: `ns` pipeline stages, two per-item slots (scales/biases and
-// group sums), the h staging tile and the barriers.
+// ---- scale slots
+// Chunked: [2 * NMAT arrays][64 rows][32 groups] fp16 in the TMA's 64-byte
+// swizzle (a 4 KB box per array), then the group sums [8 tokens][36] fp32
+// (pitch padded against bank conflicts).  Whole item: [2 * NMAT][64][K / 64]
+// fp16 and [8][sum_ld(K)] fp32, both as contiguous copies.
+constexpr int kSbChunk = 32;                          // groups per chunk
+constexpr int kSbBox = kRowTile * kSbChunk * 2;       // bytes of one array's box
+constexpr int kXsPitchChunk = kSbChunk + 4;           // floats
+__host__ __device__ inline bool sb_chunkable(int K) { return ((K / 64) & 7) == 0; }
+
 template <int BITS, int MODE>
-__host__ __device__ inline size_t qmv_smem_bytes(int K, int ns) {
+__host__ __device__ inline size_t qmv_slot_bytes(int K, bool chunked) {
+  constexpr int NM = QmvShape<BITS, MODE>::NMAT;
+  size_t sb, xs;
+  if (chunked) {
+    sb = (size_t)2 * NM * kSbBox;
+    xs = (size_t)kTokChunk * kXsPitchChunk * 4;
+  } else {
+    sb = (size_t)2 * NM * kRowTile * (K / 64) * 2;
+    xs = (size_t)kTokChunk * sum_ld(K) * 4;
+  }
+  const size_t b = (sb + 127) / 128 * 128 + (xs + 127) / 128 * 128;
+  return (b + 1023) / 1024 * 1024;  // slots stay 1024-byte aligned (swizzle atoms)
+}
+
+// Shared memory: `ns` pipeline stages, `nq` scale slots, the double-buffered
+// h staging tile and its per-warp sums, and the barriers.
+template <int BITS, int MODE>
+__host__ __device__ inline size_t qmv_smem_bytes(int K, int ns, int nq, bool chunked) {
   using S = QmvShape<BITS, MODE>;
   size_t b = 1024;  // alignment slack
   b += (size_t)ns * S::STAGE_BYTES;
-  b += 2 * qmv_slot_bytes<BITS, MODE>(K);
-  b += (size_t)kTokChunk * kRowTile * 2;  // h staging (mode 0)
-  b += 256;                               // barriers
+  b += (size_t)nq * qmv_slot_bytes<BITS, MODE>(K, chunked);
+  b += (size_t)2 * kTokChunk * kRowTile * 2;       // h staging (mode 0)
+  b += (size_t)2 * kComputeWarps * kTokChunk * 4;  // h sums
+  b += 256;                                        // barriers: 2 ns + 2 nq + 4
   return b;
 }
 
-EF_DEV uint32_t mag(uint32_t v, uint32_t mask) { return lop3_and_or(v, mask, 0x3C003C00u); }
+// Index (in fp16 words, within one array of a slot) of row r, slot-relative
+// group gc.  Chunked slots follow the 64-byte TMA swizzle: 16-byte unit u of
+// the 64-byte row r sits at unit u ^ ((r >> 1) & 3).
+EF_DEV int sb_word(bool chunked, int r, int gc, int row_len) {
+  if (!chunked) return r * row_len + gc;
+  return r * kSbChunk + ((((gc >> 3) ^ ((r >> 1) & 3)) << 3) | (gc & 7));
+}
+
+// (v & mask) | 1024.0h in both halves: the fp16 pair (1024 + q_lo, 1024 + q_hi)
+EF_DEV uint32_t mag(uint32_t v, uint32_t mask) { return lop3_and_or(v, mask, 0x64006400u); }
+
+// N consecutive floats / fp16 words from shared memory (N * size aligned).
+template <int N>
+EF_DEV void load_f32s(const float* p, float (&v)[N]) {
+  if constexpr (N == 4) {
+    const float4 u = *reinterpret_cast<const float4*>(p);
+    v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w;
+  } else if constexpr (N == 2) {
+    const float2 u = *reinterpret_cast<const float2*>(p);
+    v[0] = u.x; v[1] = u.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = p[i];
+  }
+}
+template <int N>
+EF_DEV void load_h16s(const uint16_t* p, uint16_t (&h)[N]) {
+  if constexpr (N == 4) {
+    const uint2 a = *reinterpret_cast<const uint2*>(p);
+    h[0] = (uint16_t)a.x; h[1] = (uint16_t)(a.x >> 16); h[2] = (uint16_t)a.y; h[3] = (uint16_t)(a.y >> 16);
+  } else if constexpr (N == 2) {
+    const uint32_t a = *reinterpret_cast<const uint32_t*>(p);
+    h[0] = (uint16_t)a; h[1] = (uint16_t)(a >> 16);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) h[i] = p[i];
+  }
+}
 
 struct WorkItem {
   int expert, row0_seg, nrows, rt;
@@ -92,22 +157,17 @@ EF_DEV WorkItem decode_work(const QmvParams& p, int w, int n_rt) {
   return it;
 }
 
-// Bounded barrier among the compute warps built from an mbarrier.
-EF_DEV bool warps_sync(uint64_t* bar, uint32_t parity) {
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
-  return mbar_wait(bar, parity, kDevErrTimeoutFull);
-}
-
 struct QmvSmem {
   uint8_t* stage_base;
   uint8_t* slot_base;
-  uint16_t* s_h;
+  uint16_t* s_h;       // [2][8][64] h staging (mode 0)
+  float* hsum;         // [2][kComputeWarps][8] per-warp h sums (mode 0)
   uint64_t* full;
   uint64_t* empty;
-  uint64_t* sb_full;   // [2]
-  uint64_t* sb_empty;  // [2]
-  uint64_t* sync;      // [2] epilogue staging
+  uint64_t* sb_full;   // [n_slots]
+  uint64_t* sb_empty;  // [n_slots]
+  uint64_t* h_ready;   // [2] mode 0: h tile staged (compute warps)
+  uint64_t* h_free;    // [2] mode 0: h tile copied out (scale warp)
 };
 
 // The code words of one 64-column group for rows rA, rB (8 bytes of each row at
@@ -134,23 +194,24 @@ EF_DEV GroupCodes<BITS> load_group_codes(const uint8_t* cm, int G, int rA, int r
 }
 
 // Dot products of one 64-column group for rows rA, rB of matrix m and the
-// segment's 8 tokens; folds the group's affine scale into y.
+// segment's 8 tokens; folds the group's affine scale into y (sA, sB: scales;
+// bA, bB: bias - 1024 * scale; x0, x1: the group sums of tokens 2t, 2t + 1).
 template <int BITS, int MODE>
 EF_DEV void qmv_group_regs(const GroupCodes<BITS>& cw, const uint4 (&blk)[2], float sA, float sB, float bA, float bB,
                            float x0, float x1, float (&y)[4]) {
-  float D[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  float D[4] = {0.f, 0.f, 0.f, 0.f};
   if constexpr (BITS == 4) {
     const uint2 va = make_uint2(cw.a.x, cw.a.y), vb = make_uint2(cw.b.x, cw.b.y);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t wa = h ? va.y : va.x, wb = h ? vb.y : vb.x;
-      // nibble pairs (s, s+4): P_s = ((w >> 4s) & 0x000F000F) | 1.0h
+      // nibble pairs (s, s+4): P_s = ((w >> 4s) & 0x000F000F) | 1024.0h
       const uint32_t a0[4] = {mag(wa, 0x000F000Fu), mag(wb, 0x000F000Fu), mag(wa >> 4, 0x000F000Fu),
                               mag(wb >> 4, 0x000F000Fu)};
       const uint32_t a1[4] = {mag(wa >> 8, 0x000F000Fu), mag(wb >> 8, 0x000F000Fu), mag(wa >> 12, 0x000F000Fu),
                               mag(wb >> 12, 0x000F000Fu)};
-      mma_16816(D[0], a0, blk[h].x, blk[h].y);
-      mma_16816(D[1], a1, blk[h].z, blk[h].w);
+      mma_16816(D, a0, blk[h].x, blk[h].y);
+      mma_16816(D, a1, blk[h].z, blk[h].w);
     }
   } else {
     const uint4 va = cw.a, vb = cw.b;
@@ -158,42 +219,86 @@ EF_DEV void qmv_group_regs(const GroupCodes<BITS>& cw, const uint4 (&blk)[2], fl
     for (int h = 0; h < 2; ++h) {
       const uint32_t wa0 = h ? va.z : va.x, wa1 = h ? va.w : va.y;  // row A: cols 0-3, 4-7 of block h
       const uint32_t wb0 = h ? vb.z : vb.x, wb1 = h ? vb.w : vb.y;
-      // bytes (0,2) and (1,3) of a word: ((w >> 8k) & 0x00FF00FF) | 1.0h
+      // bytes (0,2) and (1,3) of a word: ((w >> 8k) & 0x00FF00FF) | 1024.0h
       const uint32_t a0[4] = {mag(wa0, 0x00FF00FFu), mag(wb0, 0x00FF00FFu), mag(wa1, 0x00FF00FFu),
                               mag(wb1, 0x00FF00FFu)};
       const uint32_t a1[4] = {mag(wa0 >> 8, 0x00FF00FFu), mag(wb0 >> 8, 0x00FF00FFu), mag(wa1 >> 8, 0x00FF00FFu),
                               mag(wb1 >> 8, 0x00FF00FFu)};
-      mma_16816(D[0], a0, blk[h].x, blk[h].y);
-      mma_16816(D[1], a1, blk[h].z, blk[h].w);
+      mma_16816(D, a0, blk[h].x, blk[h].y);
+      mma_16816(D, a1, blk[h].z, blk[h].w);
     }
   }
-  y[0] = fmaf(sA, D[0][0] + D[1][0], fmaf(bA, x0, y[0]));
-  y[1] = fmaf(sA, D[0][1] + D[1][1], fmaf(bA, x1, y[1]));
-  y[2] = fmaf(sB, D[0][2] + D[1][2], fmaf(bB, x0, y[2]));
-  y[3] = fmaf(sB, D[0][3] + D[1][3], fmaf(bB, x1, y[3]));
+  y[0] = fmaf(sA, D[0], fmaf(bA, x0, y[0]));
+  y[1] = fmaf(sA, D[1], fmaf(bA, x1, y[1]));
+  y[2] = fmaf(sB, D[2], fmaf(bB, x0, y[2]));
+  y[3] = fmaf(sB, D[3], fmaf(bB, x1, y[3]));
 }
 
+// Scale warp, mode 0: copy item e's staged h tile to h_out and its per-token
+// sums (over the compute warps, in warp order) to hsum_out, then free the
+// staging buffer.  Returns false after a failed wait.
 template <int BITS, int MODE>
-EF_DEV void qmv_group(const uint8_t* cm, const uint4 (&blk)[2], int G, int rA, int rB, int t, float sA, float sB,
-                      float bA, float bB, float x0, float x1, float (&y)[4]) {
-  qmv_group_regs<BITS, MODE>(load_group_codes<BITS>(cm, G, rA, rB, t), blk, sA, sB, bA, bB, x0, x1, y);
+EF_DEV bool qmv_h_out(const QmvParams& p, const QmvSmem& sm, const WorkItem& it, uint32_t e) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t b = e & 1u;
+  bool ok = true;
+  if (lane == 0) ok = mbar_wait(&sm.h_ready[b], (e >> 1) & 1u, kDevErrTimeoutFull);
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok) return false;
+  const uint16_t* s_h = sm.s_h + (size_t)b * kTokChunk * kRowTile;
+  const float* s_hs = sm.hsum + (size_t)b * kComputeWarps * kTokChunk;
+  const int R = p.R, row0 = it.rt * kRowTile;
+  for (int c = lane; c < it.nrows * 8; c += 32) {
+    const int tok = c >> 3, part = c & 7;
+    const uint4 v = reinterpret_cast<const uint4*>(s_h + tok * kRowTile)[part];
+    reinterpret_cast<uint4*>(p.h_out + (size_t)(it.row0_seg + tok) * R + row0)[part] = v;
+  }
+  if (lane < it.nrows) {
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kComputeWarps; ++w) s += s_hs[w * kTokChunk + lane];
+    p.hsum_out[(size_t)(it.row0_seg + lane) * sum_ld(R) + it.rt] = s;
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&sm.h_free[b]);
+  return true;
 }
 
-// One work item for one compute warp.  Returns false after a failed wait.
+// Scale-slot bookkeeping shared by the producer and the compute warps.
+struct SbGeom {
+  bool chunked;
+  int spc;      // stages per scale chunk
+  int row_len;  // groups per slot row
+  int xp;       // floats per token row of the slot's group sums
+};
 template <int BITS, int MODE>
-EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, int q, uint32_t item,
-                     uint32_t fill_base, int ns) {
+EF_DEV SbGeom sb_geom(const QmvParams& p, int nstages) {
+  SbGeom g;
+  g.chunked = p.sb_chunked != 0;
+  g.spc = g.chunked ? kSbChunk / QmvShape<BITS, MODE>::GPS : nstages;
+  g.row_len = g.chunked ? kSbChunk : p.K / 64;
+  g.xp = g.chunked ? kXsPitchChunk : sum_ld(p.K);
+  return g;
+}
+
+// One work item for one compute warp; `cc` counts the scale chunks consumed.
+// Returns false after a failed wait.
+template <int BITS, int MODE>
+EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, uint32_t item, uint32_t fill_base,
+                     uint32_t& cc, int ns, int nq) {
   using S = QmvShape<BITS, MODE>;
+  constexpr int GPS = S::GPS;
   const int lane = threadIdx.x & 31, cw = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int ng = p.K / 64;
-  const int xp = xs_pitch(p.K), sp = sb_pitch(p.K);
   const int nstages = (p.K + S::KT - 1) / S::KT;
-  const int rA = cw * 16 + g, rB = rA + 8;
-  const uint8_t* slot = sm.slot_base + (size_t)q * qmv_slot_bytes<BITS, MODE>(p.K);
-  const uint16_t* s_sb = reinterpret_cast<const uint16_t*>(slot);
-  const float* s_xs = reinterpret_cast<const float*>(slot + (qmv_sb_bytes<BITS, MODE>(p.K) + 127) / 128 * 128);
-  const bool vec_ok = (ng & 3) == 0;  // stage groups 8-byte aligned in the scale rows
+  const SbGeom geo = sb_geom<BITS, MODE>(p, nstages);
+  const size_t slot_bytes = qmv_slot_bytes<BITS, MODE>(p.K, geo.chunked);
+  const size_t arr_words = geo.chunked ? (size_t)kRowTile * kSbChunk : (size_t)kRowTile * ng;
+  const size_t xs_off =
+      geo.chunked ? (size_t)2 * S::NMAT * kSbBox : ((size_t)2 * S::NMAT * arr_words * 2 + 127) / 128 * 128;
+  const int rA = cw * 16 + row_of_lane<BITS>(g), rB = rA + 8;
+  const bool vec_ok = geo.chunked || (ng & 3) == 0;  // a stage's groups aligned in the scale rows
 
   float y[S::NMAT][4];
 #pragma unroll
@@ -201,133 +306,133 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
 #pragma unroll
     for (int i = 0; i < 4; ++i) y[m][i] = 0.0f;
 
+  const uint16_t* s_sb = nullptr;
+  const float* s_xs = nullptr;
+  int q = 0, sc = 0, cg0 = 0;  // slot, stage within the chunk, first group of the chunk
+  int slot_i = (int)(fill_base % (uint32_t)ns);
+  uint32_t phase = (fill_base / (uint32_t)ns) & 1u;
   for (int st = 0; st < nstages; ++st) {
-    const uint32_t f = fill_base + st;
-    const int slot_i = f % ns;
-    if (!mbar_wait(&sm.full[slot_i], (f / ns) & 1u, kDevErrTimeoutFull)) return false;
+    if (sc == 0) {  // a new scale chunk
+      q = (int)(cc % (uint32_t)nq);
+      if (!mbar_wait(&sm.sb_full[q], (cc / (uint32_t)nq) & 1u, kDevErrTimeoutScales)) return false;
+      const uint8_t* slot = sm.slot_base + (size_t)q * slot_bytes;
+      s_sb = reinterpret_cast<const uint16_t*>(slot);
+      s_xs = reinterpret_cast<const float*>(slot + xs_off);
+      cg0 = st * GPS;
+    }
+    if (!mbar_wait(&sm.full[slot_i], phase, kDevErrTimeoutFull)) return false;
     const uint8_t* codes = sm.stage_base + (size_t)slot_i * S::STAGE_BYTES;
     // activation box of group G: [8 rows][128 B], 16-byte chunk c of row r at chunk c ^ r
     const uint8_t* act = codes + S::CODE_BYTES + (size_t)g * 128;
-    const int gvalid = min(S::GPS, ng - st * S::GPS);  // last stage may be partial
-    const int g0 = st * S::GPS;
-    if (gvalid == S::GPS && vec_ok) {
+    const int gvalid = min(GPS, ng - st * GPS);  // last stage may be partial
+    const int gc = st * GPS - cg0;               // slot-relative first group of the stage
+    if (gvalid == GPS && vec_ok) {
       // ---- full stage: all loads of the stage issued up front, groups unguarded
-      float xa[S::GPS], xb[S::GPS];
-      if constexpr (S::GPS == 4) {
-        const float4 u = *reinterpret_cast<const float4*>(s_xs + (2 * t) * xp + g0);
-        const float4 v = *reinterpret_cast<const float4*>(s_xs + (2 * t + 1) * xp + g0);
-        xa[0] = u.x; xa[1] = u.y; xa[2] = u.z; xa[3] = u.w;
-        xb[0] = v.x; xb[1] = v.y; xb[2] = v.z; xb[3] = v.w;
-      } else {
-        const float2 u = *reinterpret_cast<const float2*>(s_xs + (2 * t) * xp + g0);
-        const float2 v = *reinterpret_cast<const float2*>(s_xs + (2 * t + 1) * xp + g0);
-        xa[0] = u.x; xa[1] = u.y;
-        xb[0] = v.x; xb[1] = v.y;
-      }
-      uint4 blk[S::GPS][2];
+      float xa[GPS], xb[GPS];
+      load_f32s<GPS>(s_xs + (2 * t) * geo.xp + gc, xa);
+      load_f32s<GPS>(s_xs + (2 * t + 1) * geo.xp + gc, xb);
+      uint4 blk[GPS][2];
 #pragma unroll
-      for (int G = 0; G < S::GPS; ++G) {
+      for (int G = 0; G < GPS; ++G) {
         blk[G][0] = *reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t) ^ g) << 4));
         blk[G][1] = *reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t + 1) ^ g) << 4));
       }
       // every code word of the stage up front: the shared-memory latencies
       // overlap instead of serialising group by group
-      GroupCodes<BITS> cw[S::NMAT][S::GPS];
+      GroupCodes<BITS> cwd[S::NMAT][GPS];
 #pragma unroll
       for (int m = 0; m < S::NMAT; ++m)
 #pragma unroll
-        for (int G = 0; G < S::GPS; ++G)
-          cw[m][G] = load_group_codes<BITS>(codes + (size_t)m * kRowTile * S::ROWB, G, rA, rB, t);
+        for (int G = 0; G < GPS; ++G)
+          cwd[m][G] = load_group_codes<BITS>(codes + (size_t)m * kRowTile * S::ROWB, G, rA, rB, t);
+      const int wA = sb_word(geo.chunked, rA, gc, geo.row_len), wB = sb_word(geo.chunked, rB, gc, geo.row_len);
 #pragma unroll
       for (int m = 0; m < S::NMAT; ++m) {
-        const uint16_t* ms = s_sb + (size_t)m * 2 * kRowTile * sp;
-        const uint16_t* mb = ms + (size_t)kRowTile * sp;
-        uint16_t hsA[S::GPS], hsB[S::GPS], hbA[S::GPS], hbB[S::GPS];
-        if constexpr (S::GPS == 4) {
-          const uint2 a = *reinterpret_cast<const uint2*>(ms + rA * sp + g0);
-          const uint2 b = *reinterpret_cast<const uint2*>(ms + rB * sp + g0);
-          const uint2 c = *reinterpret_cast<const uint2*>(mb + rA * sp + g0);
-          const uint2 d = *reinterpret_cast<const uint2*>(mb + rB * sp + g0);
-          const uint32_t wa[2] = {a.x, a.y}, wb[2] = {b.x, b.y}, wc[2] = {c.x, c.y}, wd[2] = {d.x, d.y};
+        const uint16_t* ms = s_sb + (size_t)m * 2 * arr_words;
+        const uint16_t* mb = ms + arr_words;
+        uint16_t hsA[GPS], hsB[GPS], hbA[GPS], hbB[GPS];
+        load_h16s<GPS>(ms + wA, hsA);
+        load_h16s<GPS>(ms + wB, hsB);
+        load_h16s<GPS>(mb + wA, hbA);
+        load_h16s<GPS>(mb + wB, hbB);
 #pragma unroll
-          for (int G = 0; G < 4; ++G) {
-            hsA[G] = (uint16_t)(wa[G >> 1] >> (16 * (G & 1)));
-            hsB[G] = (uint16_t)(wb[G >> 1] >> (16 * (G & 1)));
-            hbA[G] = (uint16_t)(wc[G >> 1] >> (16 * (G & 1)));
-            hbB[G] = (uint16_t)(wd[G >> 1] >> (16 * (G & 1)));
-          }
-        } else {
-          const uint32_t a = *reinterpret_cast<const uint32_t*>(ms + rA * sp + g0);
-          const uint32_t b = *reinterpret_cast<const uint32_t*>(ms + rB * sp + g0);
-          const uint32_t c = *reinterpret_cast<const uint32_t*>(mb + rA * sp + g0);
-          const uint32_t d = *reinterpret_cast<const uint32_t*>(mb + rB * sp + g0);
-#pragma unroll
-          for (int G = 0; G < 2; ++G) {
-            hsA[G] = (uint16_t)(a >> (16 * G));
-            hsB[G] = (uint16_t)(b >> (16 * G));
-            hbA[G] = (uint16_t)(c >> (16 * G));
-            hbB[G] = (uint16_t)(d >> (16 * G));
-          }
-        }
-#pragma unroll
-        for (int G = 0; G < S::GPS; ++G) {
-          const float sA = h16_to_f32(hsA[G]) * kQ, sB = h16_to_f32(hsB[G]) * kQ;
-          qmv_group_regs<BITS, MODE>(cw[m][G], blk[G], sA, sB, h16_to_f32(hbA[G]) - sA, h16_to_f32(hbB[G]) - sB,
-                                     xa[G], xb[G], y[m]);
+        for (int G = 0; G < GPS; ++G) {
+          const float sA = h16_to_f32(hsA[G]), sB = h16_to_f32(hsB[G]);
+          qmv_group_regs<BITS, MODE>(cwd[m][G], blk[G], sA, sB, fmaf(-kQ, sA, h16_to_f32(hbA[G])),
+                                     fmaf(-kQ, sB, h16_to_f32(hbB[G])), xa[G], xb[G], y[m]);
         }
       }
     } else {
 #pragma unroll
-      for (int G = 0; G < S::GPS; ++G) {
+      for (int G = 0; G < GPS; ++G) {
         if (G < gvalid) {
-          const int Gabs = g0 + G;
           const uint4 blk[2] = {*reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t) ^ g) << 4)),
                                 *reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t + 1) ^ g) << 4))};
-          const float x0 = s_xs[(2 * t) * xp + Gabs], x1 = s_xs[(2 * t + 1) * xp + Gabs];
+          const float x0 = s_xs[(2 * t) * geo.xp + gc + G], x1 = s_xs[(2 * t + 1) * geo.xp + gc + G];
+          const int wA = sb_word(geo.chunked, rA, gc + G, geo.row_len);
+          const int wB = sb_word(geo.chunked, rB, gc + G, geo.row_len);
 #pragma unroll
           for (int m = 0; m < S::NMAT; ++m) {
-            const uint16_t* ms = s_sb + (size_t)m * 2 * kRowTile * sp;
-            const uint16_t* mb = ms + (size_t)kRowTile * sp;
-            const float sA = h16_to_f32(ms[rA * sp + Gabs]) * kQ, sB = h16_to_f32(ms[rB * sp + Gabs]) * kQ;
-            const float bA = h16_to_f32(mb[rA * sp + Gabs]) - sA, bB = h16_to_f32(mb[rB * sp + Gabs]) - sB;
-            qmv_group<BITS, MODE>(codes + (size_t)m * kRowTile * S::ROWB, blk, G, rA, rB, t, sA, sB, bA, bB, x0,
-                                  x1, y[m]);
+            const uint16_t* ms = s_sb + (size_t)m * 2 * arr_words;
+            const uint16_t* mb = ms + arr_words;
+            const float sA = h16_to_f32(ms[wA]), sB = h16_to_f32(ms[wB]);
+            const float bA = fmaf(-kQ, sA, h16_to_f32(mb[wA])), bB = fmaf(-kQ, sB, h16_to_f32(mb[wB]));
+            qmv_group_regs<BITS, MODE>(load_group_codes<BITS>(codes + (size_t)m * kRowTile * S::ROWB, G, rA, rB, t),
+                                       blk, sA, sB, bA, bB, x0, x1, y[m]);
           }
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[slot_i]);
+    if (++slot_i == ns) {
+      slot_i = 0;
+      phase ^= 1u;
+    }
+    if (++sc == geo.spc || st == nstages - 1) {  // chunk done: its slot may be reloaded
+      if (lane == 0) mbar_arrive(&sm.sb_empty[q]);
+      sc = 0;
+      ++cc;
+    }
   }
-  __syncwarp();
-  if (lane == 0) mbar_arrive(&sm.sb_empty[q]);  // slot may be reloaded
 
   const int row0 = it.rt * kRowTile;
-  const int R = p.R;
   if constexpr (MODE == 0) {
-    // h = silu(g) * u -> fp16 staging [8][64] in the activation layout
+    // h = silu(g) * u -> fp16 staging [8][64] in the activation layout, and
+    // each token's sum of the 64 rounded h values (the group sum the down
+    // projection folds its biases with): per thread over rows rA, rB, over the
+    // 8 lane groups by shuffles, over the warps by the scale warp, which also
+    // copies the tile out.  Staging and sums are double-buffered by item
+    // parity; a buffer is rewritten (item + 2) only after its copy-out.
+    const uint32_t hb_i = item & 1u;
+    uint16_t* s_h = sm.s_h + (size_t)hb_i * kTokChunk * kRowTile;
+    float* s_hs = sm.hsum + (size_t)hb_i * kComputeWarps * kTokChunk;
+    if (item >= 2 && !mbar_wait(&sm.h_free[hb_i], ((item >> 1) - 1) & 1u, kDevErrTimeoutFull)) return false;
+    float part[2] = {0.0f, 0.0f};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int r = (i < 2) ? rA : rB;
       const int tok = 2 * t + (i & 1);
       const float gv = y[0][i], uv = y[1][i];
-      const float h = gv / (1.0f + expf(-gv)) * uv;
-      sm.s_h[tok * kRowTile + (r & ~7) + act_pos(r & 7, BITS)] = f32_to_h16_sat(h);
+      const float h = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
+      const uint16_t hb = f32_to_h16_sat(h);
+      s_h[tok * kRowTile + (r & ~7) + act_pos(r & 7, BITS)] = hb;
+      part[i & 1] += h16_to_f32(hb);
     }
-    if (!warps_sync(&sm.sync[0], item & 1u)) return false;
-    for (int c = threadIdx.x; c < it.nrows * 8; c += kComputeWarps * 32) {
-      const int tok = c >> 3, part = c & 7;
-      const uint4 v = reinterpret_cast<const uint4*>(sm.s_h + tok * kRowTile)[part];
-      reinterpret_cast<uint4*>(p.h_out + (size_t)(it.row0_seg + tok) * R + row0)[part] = v;
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
+      part[1] += __shfl_xor_sync(0xffffffffu, part[1], o);
     }
-    if ((int)threadIdx.x < it.nrows) {
-      const int tok = threadIdx.x;
-      float s = 0.0f;
-      for (int c = 0; c < kRowTile; ++c) s += h16_to_f32(sm.s_h[tok * kRowTile + c]);
-      p.hsum_out[(size_t)(it.row0_seg + tok) * sum_ld(R) + it.rt] = s;
+    if (g == 0) {
+      s_hs[cw * kTokChunk + 2 * t] = part[0];
+      s_hs[cw * kTokChunk + 2 * t + 1] = part[1];
     }
-    if (!warps_sync(&sm.sync[1], item & 1u)) return false;  // staging free for the next item
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.h_ready[hb_i]);
+    (void)row0;
   } else {
+    const int R = p.R;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int r = (i < 2) ? rA : rB;
@@ -343,18 +448,23 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
   using S = QmvShape<BITS, MODE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int ns = p.n_stages;
+  const int ns = p.n_stages, nq = p.n_slots;
   const int ng = p.K / 64;
+  const int nstages = (p.K + S::KT - 1) / S::KT;
+  const SbGeom geo = sb_geom<BITS, MODE>(p, nstages);
+  const size_t slot_bytes = qmv_slot_bytes<BITS, MODE>(p.K, geo.chunked);
   QmvSmem sm;
   sm.stage_base = smem;
   sm.slot_base = sm.stage_base + (size_t)ns * S::STAGE_BYTES;
-  sm.s_h = reinterpret_cast<uint16_t*>(sm.slot_base + 2 * qmv_slot_bytes<BITS, MODE>(p.K));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm.s_h + (size_t)kTokChunk * kRowTile);
+  sm.s_h = reinterpret_cast<uint16_t*>(sm.slot_base + (size_t)nq * slot_bytes);
+  sm.hsum = reinterpret_cast<float*>(sm.s_h + (size_t)2 * kTokChunk * kRowTile);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm.hsum + (size_t)2 * kComputeWarps * kTokChunk);
   sm.full = bars;
   sm.empty = bars + ns;
   sm.sb_full = bars + 2 * ns;
-  sm.sb_empty = sm.sb_full + 2;
-  sm.sync = sm.sb_full + 4;
+  sm.sb_empty = sm.sb_full + nq;
+  sm.h_ready = sm.sb_empty + nq;
+  sm.h_free = sm.h_ready + 2;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -362,10 +472,13 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], kComputeWarps);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < nq; ++i) {
       mbar_init(&sm.sb_full[i], 1);
       mbar_init(&sm.sb_empty[i], kComputeWarps);
-      mbar_init(&sm.sync[i], kComputeWarps);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.h_ready[i], kComputeWarps);
+      mbar_init(&sm.h_free[i], 1);
     }
     mbar_fence_init();
   }
@@ -373,7 +486,6 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
 
   const int n_rt = p.R / kRowTile;
   const int n_work = (*p.n_seg) * n_rt;
-  const int nstages = (p.K + S::KT - 1) / S::KT;
 
   if (warp == kTmaWarp) {
     if (lane != 0) return;
@@ -416,61 +528,97 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
     return;
   }
   if (warp == kScaleWarp) {
-    if (lane != 0) return;
-    // ---------------------------------------------------- per-item scales/biases and group sums
-    const int xs_ld = sum_ld(p.K), sp = sb_pitch(p.K);
-    uint32_t item = 0;
+    // ---------------------------------------------------- scale chunks (lane 0); mode 0: h copy-out (warp)
+    const int xs_ld = sum_ld(p.K);
+    const int nck = geo.chunked ? (ng + kSbChunk - 1) / kSbChunk : 1;
+    const size_t arr_bytes = geo.chunked ? (size_t)kSbBox : (size_t)kRowTile * ng * 2;
+    const size_t xs_off =
+        geo.chunked ? (size_t)2 * S::NMAT * kSbBox : ((size_t)2 * S::NMAT * arr_bytes + 127) / 128 * 128;
+    if (lane == 0 && geo.chunked)
+      for (int a = 0; a < 2 * S::NMAT; ++a) prefetch_tmap(&p.tm_sc[a]);
+    uint32_t item = 0, cc = 0;
+    bool ok = true;
     int w = blockIdx.x;
     WorkItem nxt = w < n_work ? decode_work(p, w, n_rt) : WorkItem{0, 0, 0, 0};
-    for (; w < n_work; w += gridDim.x, ++item) {
+    for (; w < n_work && ok; w += gridDim.x, ++item) {
       const WorkItem it = nxt;
       if (w + (int)gridDim.x < n_work) nxt = decode_work(p, w + gridDim.x, n_rt);
       const bool shared = it.expert >= p.n_experts;
       const size_t rowg = (size_t)(shared ? 0 : it.expert) * p.R + (size_t)it.rt * kRowTile;
-      const int q = item & 1;
-      if (item >= 2 && !mbar_wait(&sm.sb_empty[q], ((item >> 1) - 1) & 1u, kDevErrTimeoutScales)) break;
-      uint8_t* slot = sm.slot_base + (size_t)q * qmv_slot_bytes<BITS, MODE>(p.K);
-      uint16_t* s_sb = reinterpret_cast<uint16_t*>(slot);
-      float* s_xs = reinterpret_cast<float*>(slot + (qmv_sb_bytes<BITS, MODE>(p.K) + 127) / 128 * 128);
-      const uint32_t row_bytes = (uint32_t)(ng * 2);
-      const uint32_t xs_bytes = (uint32_t)(it.nrows * xs_ld * 4);
-      mbar_arrive_expect_tx(&sm.sb_full[q], S::NMAT * 2 * kRowTile * row_bytes + xs_bytes);
-      const uint16_t* srcs[4] = {shared ? p.ss0 : p.s0, shared ? p.sb0 : p.b0, shared ? p.ss1 : p.s1,
-                                 shared ? p.sb1 : p.b1};
+      for (int ck = 0; ck < nck && ok; ++ck, ++cc) {
+        const int q = (int)(cc % (uint32_t)nq);
+        if (lane == 0)
+          ok = cc < (uint32_t)nq || mbar_wait(&sm.sb_empty[q], ((cc / nq) - 1) & 1u, kDevErrTimeoutScales);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        // item - 2 has left its stages (the freed slot held a later chunk)
+        if (MODE == 0 && ck == 0 && item >= 2) {
+          ok = qmv_h_out<BITS, MODE>(p, sm, decode_work(p, w - 2 * (int)gridDim.x, n_rt), item - 2);
+          if (!ok) break;
+        }
+        if (lane != 0) continue;
+        uint8_t* slot = sm.slot_base + (size_t)q * slot_bytes;
+        float* s_xs = reinterpret_cast<float*>(slot + xs_off);
+        if (geo.chunked) {
+          const int g0 = ck * kSbChunk;
+          const int xs_n = min(kSbChunk, xs_ld - g0);  // multiple of 4
+          mbar_arrive_expect_tx(&sm.sb_full[q], (uint32_t)(2 * S::NMAT * kSbBox + it.nrows * xs_n * 4));
 #pragma unroll
-      for (int a = 0; a < 2 * S::NMAT; ++a) {
-        const uint16_t* gsrc = srcs[a] + rowg * ng;
-        uint16_t* dst = s_sb + (size_t)a * kRowTile * sp;
-        bulk_load(dst, gsrc, kRowTile * row_bytes, &sm.sb_full[q]);
+          for (int a = 0; a < 2 * S::NMAT; ++a)
+            tma_load_2d(slot + (size_t)a * kSbBox, &p.tm_sc[(shared ? 4 : 0) + a], g0, (int)rowg, &sm.sb_full[q]);
+          for (int tok = 0; tok < it.nrows; ++tok)
+            bulk_load(s_xs + tok * kXsPitchChunk, p.act_sum + (size_t)(it.row0_seg + tok) * xs_ld + g0,
+                      (uint32_t)xs_n * 4, &sm.sb_full[q]);
+        } else {
+          const uint32_t row_bytes = (uint32_t)(ng * 2);
+          const uint32_t xs_bytes = (uint32_t)(it.nrows * xs_ld * 4);
+          mbar_arrive_expect_tx(&sm.sb_full[q], S::NMAT * 2 * kRowTile * row_bytes + xs_bytes);
+          const uint16_t* srcs[4] = {shared ? p.ss0 : p.s0, shared ? p.sb0 : p.b0, shared ? p.ss1 : p.s1,
+                                     shared ? p.sb1 : p.b1};
+#pragma unroll
+          for (int a = 0; a < 2 * S::NMAT; ++a)
+            bulk_load(slot + (size_t)a * arr_bytes, srcs[a] + rowg * ng, kRowTile * row_bytes, &sm.sb_full[q]);
+          bulk_load(s_xs, p.act_sum + (size_t)it.row0_seg * xs_ld, xs_bytes, &sm.sb_full[q]);
+        }
       }
-      bulk_load(s_xs, p.act_sum + (size_t)it.row0_seg * xs_ld, xs_bytes, &sm.sb_full[q]);
     }
-    if (item > 0) mbar_wait(&sm.sb_full[(item - 1) & 1], ((item - 1) >> 1) & 1u, kDevErrTimeoutScales);
+    // the last items' h tiles
+    if (MODE == 0)
+      for (uint32_t e = item > 2u ? item - 2 : 0; e < item && ok; ++e)
+        ok = qmv_h_out<BITS, MODE>(p, sm, decode_work(p, blockIdx.x + (int)e * (int)gridDim.x, n_rt), e);
+    if (lane == 0 && cc > 0) mbar_wait(&sm.sb_full[(cc - 1) % nq], ((cc - 1) / nq) & 1u, kDevErrTimeoutScales);
     return;
   }
   // -------------------------------------------------------------- compute warps
-  uint32_t fill_base = 0, item = 0;
+  uint32_t fill_base = 0, item = 0, cc = 0;
   int w = blockIdx.x;
   WorkItem nxt = w < n_work ? decode_work(p, w, n_rt) : WorkItem{0, 0, 0, 0};
   for (; w < n_work; w += gridDim.x, ++item) {
     const WorkItem it = nxt;
     if (w + (int)gridDim.x < n_work) nxt = decode_work(p, w + gridDim.x, n_rt);
-    const int q = item & 1;
-    if (!mbar_wait(&sm.sb_full[q], (item >> 1) & 1u, kDevErrTimeoutScales)) return;
-    if (!qmv_item<BITS, MODE>(p, it, sm, q, item, fill_base, ns)) return;
+    if (!qmv_item<BITS, MODE>(p, it, sm, item, fill_base, cc, ns, nq)) return;
     fill_base += nstages;
   }
 }
 
-// Ring depth and CTAs per SM: two CTAs per SM with >= 3 stages each when they
-// fit in half of the shared memory, else one CTA with the deepest ring.
+// Ring depth, scale slots and CTAs per SM: two CTAs per SM with >= 3 stages
+// each when they fit in half of the shared memory, else one CTA with the
+// deepest ring.  Scale chunks of few stages get four slots, so that a chunk's
+// scales are requested several chunks before its first stage.
 template <int BITS, int MODE>
-static int qmv_pick(int K, int* ctas_per_sm) {
+static int qmv_pick(int K, bool chunked, int* ctas_per_sm, int* n_slots) {
   if (K > 16384) return 0;
-  for (int ns = 6; ns >= 3; --ns)
-    if (qmv_smem_bytes<BITS, MODE>(K, ns) <= 113 * 1024) { *ctas_per_sm = 2; return ns; }
-  for (int ns = 6; ns >= 2; --ns)
-    if (qmv_smem_bytes<BITS, MODE>(K, ns) <= 227 * 1024) { *ctas_per_sm = 1; return ns; }
+  const int nstages = (K + QmvShape<BITS, MODE>::KT - 1) / QmvShape<BITS, MODE>::KT;
+  const int spc = chunked ? kSbChunk / QmvShape<BITS, MODE>::GPS : nstages;
+  const int nq = spc <= 4 ? 4 : 2;
+  for (int q = nq; q >= 2; q -= 2) {
+    *n_slots = q;
+    for (int ns = 6; ns >= 3; --ns)
+      if (qmv_smem_bytes<BITS, MODE>(K, ns, q, chunked) <= 113 * 1024) { *ctas_per_sm = 2; return ns; }
+  }
+  *n_slots = 2;
+  for (int ns = 12; ns >= 2; --ns)
+    if (qmv_smem_bytes<BITS, MODE>(K, ns, 2, chunked) <= 227 * 1024) { *ctas_per_sm = 1; return ns; }
   return 0;
 }
 
@@ -478,9 +626,10 @@ template <int BITS, int MODE>
 static cudaError_t launch_qmv_t(const QmvParams& p_in, int n_sm, cudaStream_t st) {
   QmvParams p = p_in;
   int per_sm = 1;
-  p.n_stages = qmv_pick<BITS, MODE>(p.K, &per_sm);
+  const bool chunked = p.sb_chunked != 0;
+  p.n_stages = qmv_pick<BITS, MODE>(p.K, chunked, &per_sm, &p.n_slots);
   if (p.n_stages == 0) return cudaErrorInvalidValue;
-  const size_t smem = qmv_smem_bytes<BITS, MODE>(p.K, p.n_stages);
+  const size_t smem = qmv_smem_bytes<BITS, MODE>(p.K, p.n_stages, p.n_slots, chunked);
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -494,17 +643,18 @@ static cudaError_t launch_qmv_t(const QmvParams& p_in, int n_sm, cudaStream_t st
   return cudaGetLastError();
 }
 
-// SIZE_MAX when the decode kernel cannot hold a K-wide item in shared memory.
+// SIZE_MAX when the decode kernel cannot hold a K-wide item in shared memory
+// (whole-item scale slots: the larger of the two layouts).
 size_t qmv_smem_required(int bits, int mode, int K) {
-  int per = 1, ns;
+  int per = 1, nq = 2, ns;
   if (bits == 4) {
-    ns = mode == 0 ? qmv_pick<4, 0>(K, &per) : qmv_pick<4, 1>(K, &per);
+    ns = mode == 0 ? qmv_pick<4, 0>(K, false, &per, &nq) : qmv_pick<4, 1>(K, false, &per, &nq);
     if (!ns) return ~size_t(0);
-    return mode == 0 ? qmv_smem_bytes<4, 0>(K, ns) : qmv_smem_bytes<4, 1>(K, ns);
+    return mode == 0 ? qmv_smem_bytes<4, 0>(K, ns, nq, false) : qmv_smem_bytes<4, 1>(K, ns, nq, false);
   }
-  ns = mode == 0 ? qmv_pick<8, 0>(K, &per) : qmv_pick<8, 1>(K, &per);
+  ns = mode == 0 ? qmv_pick<8, 0>(K, false, &per, &nq) : qmv_pick<8, 1>(K, false, &per, &nq);
   if (!ns) return ~size_t(0);
-  return mode == 0 ? qmv_smem_bytes<8, 0>(K, ns) : qmv_smem_bytes<8, 1>(K, ns);
+  return mode == 0 ? qmv_smem_bytes<8, 0>(K, ns, nq, false) : qmv_smem_bytes<8, 1>(K, ns, nq, false);
 }
 
 cudaError_t launch_qmv(int bits, int mode, const QmvParams& p, int n_sm, cudaStream_t st) {

@@ -69,7 +69,11 @@ struct QmvParams {
   uint16_t* h_out;          // mode 0: fp16 pair-ordered [n_rows, R]
   float* hsum_out;          // mode 0: [n_rows, R/64]
   float* y_out;             // mode 1: fp32 [n_rows, R]
+  CUtensorMap tm_sc[8];     // scales/biases as [rows, K/64] fp16, box 32 groups x 64 rows, 64-byte swizzle:
+                            // s0, b0, s1, b1, then the shared expert's ss0, sb0, ss1, sb1 (valid if sb_chunked)
+  int sb_chunked;           // 1: scales streamed in 32-group chunks through tm_sc (K / 64 a multiple of 8)
   int n_stages;             // TMA ring depth (set by the launcher)
+  int n_slots;              // scale slots (set by the launcher)
 };
 
 }  // namespace ef
