@@ -29,7 +29,7 @@ cudaError_t launch_prep_act(const uint16_t* act, const int* row_src, int is_bf16
                             uint16_t* out, float* sums, cudaStream_t st);
 cudaError_t launch_combine(const float* rows, const int* inv, const float* wts, int T, int k, int H, int sh_base,
                            void* out, int out_dtype, cudaStream_t st);
-cudaError_t launch_qmv(int bits, int mode, const QmvParams& p, int n_sm, cudaStream_t st);
+cudaError_t launch_qmv(int bits, int mode, const QmvParams& p, int n_sm, cudaStream_t st, int min_segments = 0);
 size_t qmv_smem_required(int bits, int mode, int K);
 cudaError_t launch_qgemm(int bits, int mode, const GemmParams& p, int n_sm, cudaStream_t st);
 cudaError_t launch_qgemm2(int bits, int mode, const GemmParams& p, int n_sm, cudaStream_t st);
@@ -379,7 +379,9 @@ ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, const e
   p1.K = I; p1.R = H; p1.n_experts = E;
   set_scale_maps(p1, (long long)E * H, sd ? H : (long long)E * H);
   p1.y_out = f.yrows;
-  EF_LAUNCH("qmv_down", launch_qmv(bits, 1, p1, nsm, st));
+  // each expert with rows makes at least one segment
+  const int min_segs = std::min(n_rows, E + (sd ? 1 : 0));
+  EF_LAUNCH("qmv_down", launch_qmv(bits, 1, p1, nsm, st, min_segs));
   return EF_OK;
 }
 
@@ -706,7 +708,7 @@ static ef_status run_single_matrix(const ef_qweight& w, int n_exp, int out_dim, 
   p.K = in_dim; p.R = out_dim; p.n_experts = n_exp;
   set_scale_maps(p, (long long)n_exp * out_dim, (long long)n_exp * out_dim);
   p.y_out = f.yrows;
-  EF_LAUNCH("qmv_down", launch_qmv(bits, 1, p, sm_count(), st));
+  EF_LAUNCH("qmv_down", launch_qmv(bits, 1, p, sm_count(), st, std::min(n_rows, n_exp)));
   return EF_OK;
 }
 

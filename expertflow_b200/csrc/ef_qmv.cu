@@ -21,10 +21,10 @@
 //    the compute warps go straight on to the next item.
 //
 // Dot products run on the tensor cores with exact operands: a code q becomes
-// the fp16 value 1024 + q by masking it into the low mantissa bits under the
-// exponent of 1024 (one LOP3 per pair of codes plus one shift per nibble/byte
-// position); activations are fp16; products accumulate in fp32 per 64-column
-// group in one MMA chain per matrix:
+// the fp16 value 1024 + q, placed in the low mantissa bits under the exponent
+// of 1024 (4-bit: one LOP3 per pair of codes plus one shift per nibble
+// position; 8-bit: one byte permute per pair); activations are fp16; products
+// accumulate in fp32 per 64-column group in one MMA chain per matrix:
 //     D_g = sum_i x_i (1024 + q_i)
 //     y  += s_g D_g + (b_g - 1024 s_g) sum_i x_i    (= sum_i x_i (s_g q_i + b_g))
 // The k order inside mma.m16n8k16 is permuted consistently for codes and
@@ -35,6 +35,9 @@
 // mode 0: gate and up tiles together, epilogue h = silu(g) * u stored as fp16
 //         rows in the activation layout + group sums (input of mode 1).
 // mode 1: down projection, fp32 rows for the combine.
+// mode 2: mode 1 with 128-row items, taken as two 64-row tiles of the same
+//         matrix in the two-matrix path of mode 0 (twice the work per stage
+//         and per item, one activation tile for both).
 #include "ef_common.cuh"
 
 namespace ef {
@@ -47,7 +50,8 @@ struct QmvShape {
   static constexpr int KT = BITS == 4 ? 256 : 128;   // columns per stage
   static constexpr int GPS = KT / 64;                 // groups per stage
   static constexpr int ROWB = KT * BITS / 8;          // bytes per code row per stage (128)
-  static constexpr int NMAT = MODE == 0 ? 2 : 1;
+  static constexpr int NMAT = MODE == 1 ? 1 : 2;
+  static constexpr int ITEM_ROWS = MODE == 2 ? 2 * kRowTile : kRowTile;  // weight rows per work item
   static constexpr int CODE_BYTES = NMAT * kRowTile * ROWB;
   static constexpr int ACT_BOX = kTokChunk * 128;     // one 64-column group of 8 activation rows
   static constexpr int ACT_BYTES = GPS * ACT_BOX;
@@ -114,6 +118,9 @@ EF_DEV int sb_word(bool chunked, int r, int gc, int row_len) {
 
 // (v & mask) | 1024.0h in both halves: the fp16 pair (1024 + q_lo, 1024 + q_hi)
 EF_DEV uint32_t mag(uint32_t v, uint32_t mask) { return lop3_and_or(v, mask, 0x64006400u); }
+// Bytes of v picked by `sel` (0x4240: bytes 0, 2; 0x4341: bytes 1, 3) as the low
+// bytes of two fp16 halves whose high byte is 0x64: the pair (1024 + b, 1024 + b').
+EF_DEV uint32_t mag8(uint32_t v, uint32_t sel) { return prmt(v, 0x64646464u, sel); }
 
 // N consecutive floats / fp16 words from shared memory (N * size aligned).
 template <int N>
@@ -219,11 +226,10 @@ EF_DEV void qmv_group_regs(const GroupCodes<BITS>& cw, const uint4 (&blk)[2], fl
     for (int h = 0; h < 2; ++h) {
       const uint32_t wa0 = h ? va.z : va.x, wa1 = h ? va.w : va.y;  // row A: cols 0-3, 4-7 of block h
       const uint32_t wb0 = h ? vb.z : vb.x, wb1 = h ? vb.w : vb.y;
-      // bytes (0,2) and (1,3) of a word: ((w >> 8k) & 0x00FF00FF) | 1024.0h
-      const uint32_t a0[4] = {mag(wa0, 0x00FF00FFu), mag(wb0, 0x00FF00FFu), mag(wa1, 0x00FF00FFu),
-                              mag(wb1, 0x00FF00FFu)};
-      const uint32_t a1[4] = {mag(wa0 >> 8, 0x00FF00FFu), mag(wb0 >> 8, 0x00FF00FFu), mag(wa1 >> 8, 0x00FF00FFu),
-                              mag(wb1 >> 8, 0x00FF00FFu)};
+      // bytes (0,2) and (1,3) of a word under the high byte 0x64 of 1024.0h,
+      // one byte permute per pair
+      const uint32_t a0[4] = {mag8(wa0, 0x4240u), mag8(wb0, 0x4240u), mag8(wa1, 0x4240u), mag8(wb1, 0x4240u)};
+      const uint32_t a1[4] = {mag8(wa0, 0x4341u), mag8(wb0, 0x4341u), mag8(wa1, 0x4341u), mag8(wb1, 0x4341u)};
       mma_16816(D, a0, blk[h].x, blk[h].y);
       mma_16816(D, a1, blk[h].z, blk[h].w);
     }
@@ -396,8 +402,8 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
     }
   }
 
-  const int row0 = it.rt * kRowTile;
   if constexpr (MODE == 0) {
+    const int row0 = it.rt * kRowTile;
     // h = silu(g) * u -> fp16 staging [8][64] in the activation layout, and
     // each token's sum of the 64 rounded h values (the group sum the down
     // projection folds its biases with): per thread over rows rA, rB, over the
@@ -434,11 +440,14 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
   } else {
     const int R = p.R;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = (i < 2) ? rA : rB;
-      const int tok = 2 * t + (i & 1);
-      if (tok < it.nrows) p.y_out[(size_t)(it.row0_seg + tok) * R + row0 + r] = y[0][i];
-    }
+    for (int m = 0; m < S::NMAT; ++m)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = (i < 2) ? rA : rB;
+        const int tok = 2 * t + (i & 1);
+        const int row = it.rt * S::ITEM_ROWS + m * kRowTile + r;
+        if (tok < it.nrows) p.y_out[(size_t)(it.row0_seg + tok) * R + row] = y[m][i];
+      }
   }
   return true;
 }
@@ -484,7 +493,7 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
   }
   __syncthreads();
 
-  const int n_rt = p.R / kRowTile;
+  const int n_rt = p.R / S::ITEM_ROWS;
   const int n_work = (*p.n_seg) * n_rt;
 
   if (warp == kTmaWarp) {
@@ -501,9 +510,11 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
       const WorkItem it = nxt;
       if (w + (int)gridDim.x < n_work) nxt = decode_work(p, w + gridDim.x, n_rt);
       const bool shared = it.expert >= p.n_experts;
-      const int rowg = (shared ? 0 : it.expert) * p.R + it.rt * kRowTile;
+      const int rowg = (shared ? 0 : it.expert) * p.R + it.rt * S::ITEM_ROWS;
       const CUtensorMap* m0 = shared ? &p.tm_sw0 : &p.tm_w0;
-      const CUtensorMap* m1 = shared ? &p.tm_sw1 : &p.tm_w1;
+      // second tile: up (mode 0), or the next 64 rows of the same matrix (mode 2)
+      const CUtensorMap* m1 = MODE == 2 ? m0 : (shared ? &p.tm_sw1 : &p.tm_w1);
+      const int rowg1 = MODE == 2 ? rowg + kRowTile : rowg;
       for (int st = 0; st < nstages; ++st, ++fill_it) {
         const int slot = fill_it % ns;
         if (fill_it >= (uint32_t)ns && !mbar_wait(&sm.empty[slot], ((fill_it / ns) - 1) & 1u, kDevErrTimeoutEmpty)) {
@@ -516,7 +527,7 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
         mbar_arrive_expect_tx(&sm.full[slot], S::CODE_BYTES + gv * S::ACT_BOX);
         const int kw = st * (S::KT * BITS / 32);
         tma_load_2d(dst, m0, kw, rowg, &sm.full[slot]);
-        if (MODE == 0) tma_load_2d(dst + kRowTile * S::ROWB, m1, kw, rowg, &sm.full[slot]);
+        if (S::NMAT == 2) tma_load_2d(dst + kRowTile * S::ROWB, m1, kw, rowg1, &sm.full[slot]);
         uint8_t* adst = dst + S::CODE_BYTES;
         for (int G = 0; G < gv; ++G)
           tma_load_2d(adst + G * S::ACT_BOX, &p.tm_act, st * S::KT + 64 * G, it.row0_seg, &sm.full[slot]);
@@ -544,7 +555,7 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
       const WorkItem it = nxt;
       if (w + (int)gridDim.x < n_work) nxt = decode_work(p, w + gridDim.x, n_rt);
       const bool shared = it.expert >= p.n_experts;
-      const size_t rowg = (size_t)(shared ? 0 : it.expert) * p.R + (size_t)it.rt * kRowTile;
+      const size_t rowg = (size_t)(shared ? 0 : it.expert) * p.R + (size_t)it.rt * S::ITEM_ROWS;
       for (int ck = 0; ck < nck && ok; ++ck, ++cc) {
         const int q = (int)(cc % (uint32_t)nq);
         if (lane == 0)
@@ -563,9 +574,11 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
           const int g0 = ck * kSbChunk;
           const int xs_n = min(kSbChunk, xs_ld - g0);  // multiple of 4
           mbar_arrive_expect_tx(&sm.sb_full[q], (uint32_t)(2 * S::NMAT * kSbBox + it.nrows * xs_n * 4));
+          // arrays s, b of tile 0, then of tile 1 (mode 0: up; mode 2: the next 64 rows)
 #pragma unroll
           for (int a = 0; a < 2 * S::NMAT; ++a)
-            tma_load_2d(slot + (size_t)a * kSbBox, &p.tm_sc[(shared ? 4 : 0) + a], g0, (int)rowg, &sm.sb_full[q]);
+            tma_load_2d(slot + (size_t)a * kSbBox, &p.tm_sc[(shared ? 4 : 0) + (MODE == 2 ? (a & 1) : a)], g0,
+                        (int)rowg + (MODE == 2 ? (a >> 1) * kRowTile : 0), &sm.sb_full[q]);
           for (int tok = 0; tok < it.nrows; ++tok)
             bulk_load(s_xs + tok * kXsPitchChunk, p.act_sum + (size_t)(it.row0_seg + tok) * xs_ld + g0,
                       (uint32_t)xs_n * 4, &sm.sb_full[q]);
@@ -573,8 +586,10 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
           const uint32_t row_bytes = (uint32_t)(ng * 2);
           const uint32_t xs_bytes = (uint32_t)(it.nrows * xs_ld * 4);
           mbar_arrive_expect_tx(&sm.sb_full[q], S::NMAT * 2 * kRowTile * row_bytes + xs_bytes);
-          const uint16_t* srcs[4] = {shared ? p.ss0 : p.s0, shared ? p.sb0 : p.b0, shared ? p.ss1 : p.s1,
-                                     shared ? p.sb1 : p.b1};
+          const uint16_t* s0 = shared ? p.ss0 : p.s0;
+          const uint16_t* b0 = shared ? p.sb0 : p.b0;
+          const uint16_t* srcs[4] = {s0, b0, MODE == 2 ? s0 + (size_t)kRowTile * ng : (shared ? p.ss1 : p.s1),
+                                     MODE == 2 ? b0 + (size_t)kRowTile * ng : (shared ? p.sb1 : p.b1)};
 #pragma unroll
           for (int a = 0; a < 2 * S::NMAT; ++a)
             bulk_load(slot + (size_t)a * arr_bytes, srcs[a] + rowg * ng, kRowTile * row_bytes, &sm.sb_full[q]);
@@ -657,9 +672,17 @@ size_t qmv_smem_required(int bits, int mode, int K) {
   return mode == 0 ? qmv_smem_bytes<8, 0>(K, ns, nq, false) : qmv_smem_bytes<8, 1>(K, ns, nq, false);
 }
 
-cudaError_t launch_qmv(int bits, int mode, const QmvParams& p, int n_sm, cudaStream_t st) {
-  if (bits == 4) return mode == 0 ? launch_qmv_t<4, 0>(p, n_sm, st) : launch_qmv_t<4, 1>(p, n_sm, st);
-  return mode == 0 ? launch_qmv_t<8, 0>(p, n_sm, st) : launch_qmv_t<8, 1>(p, n_sm, st);
+// mode 1 runs as mode 2 (128-row items) when the output rows allow it and
+// the segments (at least min_segments of them) give every CTA an item.
+cudaError_t launch_qmv(int bits, int mode, const QmvParams& p, int n_sm, cudaStream_t st, int min_segments) {
+  if (mode == 1 && p.R % (2 * kRowTile) == 0 && (long long)min_segments * (p.R / (2 * kRowTile)) >= 2LL * n_sm)
+    mode = 2;
+  if (bits == 4) {
+    if (mode == 0) return launch_qmv_t<4, 0>(p, n_sm, st);
+    return mode == 2 ? launch_qmv_t<4, 2>(p, n_sm, st) : launch_qmv_t<4, 1>(p, n_sm, st);
+  }
+  if (mode == 0) return launch_qmv_t<8, 0>(p, n_sm, st);
+  return mode == 2 ? launch_qmv_t<8, 2>(p, n_sm, st) : launch_qmv_t<8, 1>(p, n_sm, st);
 }
 
 }  // namespace ef

@@ -67,7 +67,7 @@ struct QmvParams {
   int R;                    // output rows per expert
   int n_experts;            // expert id == n_experts selects the shared expert
   uint16_t* h_out;          // mode 0: fp16 pair-ordered [n_rows, R]
-  float* hsum_out;          // mode 0: [n_rows, R/64]
+  float* hsum_out;          // mode 0: [n_rows, sum_ld(R)] group sums of h
   float* y_out;             // mode 1: fp32 [n_rows, R]
   CUtensorMap tm_sc[8];     // scales/biases as [rows, K/64] fp16, box 32 groups x 64 rows, 64-byte swizzle:
                             // s0, b0, s1, b1, then the shared expert's ss0, sb0, ss1, sb1 (valid if sb_chunked)
