@@ -8,6 +8,7 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "efmoe_internal.h"
 
@@ -57,6 +58,47 @@ EF_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
   }
   ef_set_error(code);
   return false;
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// The kernels of one forward are launched with programmatic stream
+// serialisation: each waits for its predecessor's completion and memory
+// (pdl_wait) before its first global-memory access, then lets its successor
+// be scheduled (pdl_launch_next), so the stream order of the data is kept
+// while launch latency and prologues overlap the predecessor's tail.  Letting
+// the successor launch only after the wait keeps the early launches to one
+// kernel ahead: a chain of waiting grids would hold the SMs' registers and
+// shared memory.  Kernels followed by a persistent grid (the decode GEMV and
+// the grouped GEMM fill every SM) do not launch it early -- its CTAs would
+// start late on SMs still busy with the predecessor -- it then launches at
+// the predecessor's completion, which still saves the launch gap.  Without a
+// programmatic predecessor both are no-ops.
+EF_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+EF_DEV void pdl_launch_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// EF_PDL=0 in the environment launches without the attribute.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("EF_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
 // ---------------------------------------------------------------- TMA / bulk copies

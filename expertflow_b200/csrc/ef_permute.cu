@@ -51,6 +51,8 @@ __device__ int block_exclusive_scan(int v, int* s_warp, int* total) {
 // n_sh: rows of the shared bin (0 or T), bin index n_exp.
 __global__ void __launch_bounds__(kPermThreads) permute_kernel(const int* __restrict__ entries, int n_ent, int k,
                                                                int n_exp, int n_sh, int seg_chunk, PermBufs pb) {
+  pdl_wait();
+  pdl_launch_next();
   extern __shared__ int s_hist[];  // [kPermWarps][nb]
   __shared__ int s_warp[32];
   __shared__ int s_total;
@@ -143,6 +145,7 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(const int* __rest
 // every segment's rows contiguous for the GEMV kernel's tile loads.
 __global__ void prep_act_kernel(const uint16_t* __restrict__ act, const int* __restrict__ row_src, int is_bf16, int n,
                                 int K, int bits, uint16_t* __restrict__ out, float* __restrict__ sums) {
+  pdl_wait();  // its successor, a persistent GEMV / GEMM, launches at its completion
   const int nblk = K >> 3;
   long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   long long total = (long long)n * nblk;
@@ -191,6 +194,8 @@ __global__ void prep_act_kernel(const uint16_t* __restrict__ act, const int* __r
 __global__ void combine_kernel(const float* __restrict__ rows, const int* __restrict__ inv,
                                const float* __restrict__ wts, int T, int k, int H, int sh_base,
                                void* __restrict__ out, int out_dtype) {
+  pdl_wait();
+  pdl_launch_next();
   const int t = blockIdx.y;
   const int c4 = blockIdx.x * blockDim.x + threadIdx.x;  // index of a 4-column quad
   if (t >= T || c4 * 4 >= H) return;
@@ -233,8 +238,7 @@ cudaError_t launch_permute(const int* entries, int n_ent, int k, int n_exp, int 
     cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
     attr_set = true;
   }
-  permute_kernel<<<1, kPermThreads, smem, st>>>(entries, n_ent, k, n_exp, n_sh, seg_chunk, pb);
-  return cudaGetLastError();
+  return launch_pdl(permute_kernel, 1, kPermThreads, smem, st, entries, n_ent, k, n_exp, n_sh, seg_chunk, pb);
 }
 
 cudaError_t launch_prep_act(const uint16_t* act, const int* row_src, int is_bf16, int n, int K, int bits,
@@ -243,8 +247,7 @@ cudaError_t launch_prep_act(const uint16_t* act, const int* row_src, int is_bf16
   if (total == 0) return cudaSuccess;
   int threads = 256;
   long long blocks = (total + threads - 1) / threads;
-  prep_act_kernel<<<(unsigned)blocks, threads, 0, st>>>(act, row_src, is_bf16, n, K, bits, out, sums);
-  return cudaGetLastError();
+  return launch_pdl(prep_act_kernel, (unsigned)blocks, threads, 0, st, act, row_src, is_bf16, n, K, bits, out, sums);
 }
 
 cudaError_t launch_combine(const float* rows, const int* inv, const float* wts, int T, int k, int H, int sh_base,
@@ -253,8 +256,7 @@ cudaError_t launch_combine(const float* rows, const int* inv, const float* wts, 
   int quads = H / 4;
   int threads = quads < 256 ? ((quads + 31) / 32) * 32 : 256;
   dim3 grid((quads + threads - 1) / threads, T);
-  combine_kernel<<<grid, threads, 0, st>>>(rows, inv, wts, T, k, H, sh_base, out, out_dtype);
-  return cudaGetLastError();
+  return launch_pdl(combine_kernel, grid, threads, 0, st, rows, inv, wts, T, k, H, sh_base, out, out_dtype);
 }
 
 }  // namespace ef

@@ -189,6 +189,8 @@ constexpr int kNormThreads = 256;
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __restrict__ r, const float* __restrict__ y,
                                                                    int H, float eps, int act_bf16,
                                                                    uint16_t* __restrict__ x) {
+  pdl_wait();
+  pdl_launch_next();
   const size_t base = (size_t)blockIdx.x * H;
   float ss = 0.0f;
   for (int i = threadIdx.x; i < H; i += kNormThreads) {
@@ -747,15 +749,15 @@ ef_status ef_pool_decode_step(ef_slot_pool* P, float* r, int T, const void* cons
   const size_t fws_bytes = ef_pool_workspace_size(P, T);
   ef_status s;
   for (int l = 0; l < L; ++l) {
-    EF_LAUNCH("add_rmsnorm", (ef::add_rmsnorm_kernel<<<T, ef::kNormThreads, 0, st>>>(r, l ? y : nullptr, H, eps, bf, x),
-                              cudaGetLastError()));
+    EF_LAUNCH("add_rmsnorm", launch_pdl(ef::add_rmsnorm_kernel, T, ef::kNormThreads, 0, st, r,
+                                            l ? static_cast<const float*>(y) : nullptr, H, eps, bf, x));
     const bool la = lookahead && l + 1 < L;
     if ((s = ef_pool_moe_forward(P, l, x, T, gate_w[l], e_bias ? e_bias[l] : nullptr, la ? gate_w[l + 1] : nullptr,
                                  la && e_bias ? e_bias[l + 1] : nullptr, y, 1, nullptr, nullptr, fws, fws_bytes, st)))
       return s;
   }
-  EF_LAUNCH("add_rmsnorm", (ef::add_rmsnorm_kernel<<<T, ef::kNormThreads, 0, st>>>(r, y, H, eps, bf, nullptr),
-                            cudaGetLastError()));
+  EF_LAUNCH("add_rmsnorm", launch_pdl(ef::add_rmsnorm_kernel, T, ef::kNormThreads, 0, st, r,
+                                          static_cast<const float*>(y), H, eps, bf, static_cast<uint16_t*>(nullptr)));
   return ef_pool_end_token(P);
 }
 

@@ -252,6 +252,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the segments and activations of the previous kernels
+  // (no early launch of the successor: its CTAs would wait on SMs this
+  // persistent grid fills)
 
   const int n_rt = MODE == 0 ? (p.R + kGemmTileM - 1) / kGemmTileM : (p.R + kGemmItemRows - 1) / kGemmItemRows;
   const int n_work = (*p.n_seg) * n_rt;
@@ -558,8 +561,7 @@ static cudaError_t launch_qgemm_t(const GemmParams& p, int n_sm, cudaStream_t st
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  qgemm_kernel<BITS, MODE><<<n_sm, kGemmThreads, smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(qgemm_kernel<BITS, MODE>, n_sm, kGemmThreads, smem, st, p);
 }
 
 cudaError_t launch_qgemm(int bits, int mode, const GemmParams& p, int n_sm, cudaStream_t st) {

@@ -492,6 +492,9 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
     mbar_fence_init();
   }
   __syncthreads();
+  pdl_wait();  // the segments, activations and sums of the previous kernels
+  // (no early launch of the successor: its CTAs would wait on SMs this
+  // persistent grid fills)
 
   const int n_rt = p.R / S::ITEM_ROWS;
   const int n_work = (*p.n_seg) * n_rt;
@@ -654,8 +657,7 @@ static cudaError_t launch_qmv_t(const QmvParams& p_in, int n_sm, cudaStream_t st
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  qmv_kernel<BITS, MODE><<<n_sm * per_sm, kQmvThreads, smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(qmv_kernel<BITS, MODE>, n_sm * per_sm, kQmvThreads, smem, st, p);
 }
 
 // SIZE_MAX when the decode kernel cannot hold a K-wide item in shared memory

@@ -77,6 +77,8 @@ __global__ void __launch_bounds__(128) router_logits_kernel(const uint16_t* __re
                                                             int T, int E, int H, float* __restrict__ logits,
                                                             const uint16_t* __restrict__ wg2,
                                                             float* __restrict__ logits2) {
+  pdl_wait();
+  pdl_launch_next();
   if (blockIdx.z) {
     wg = wg2;
     logits = logits2;
@@ -165,6 +167,8 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const flo
                                                                        const float* __restrict__ e_bias2,
                                                                        int* __restrict__ inds2,
                                                                        float* __restrict__ wts2) {
+  pdl_wait();
+  pdl_launch_next();
   if (blockIdx.y) {
     logits = logits2;
     e_bias = e_bias2;
@@ -278,17 +282,21 @@ cudaError_t launch_router_logits(const uint16_t* x, int x_bf16, const uint16_t* 
   const int nz = wg2 ? 2 : 1;
   if (T >= 64) {
     dim3 grid((T + 7) / 8, (E + 7) / 8, nz);
-    router_logits_kernel<8, 8><<<grid, 128, 0, st>>>(x, x_bf16, wg, w_bf16, T, E, H, logits, wg2, logits2);
+    return launch_pdl(router_logits_kernel<8, 8>, grid, 128, 0, st, x, x_bf16, wg, w_bf16, T, E, H, logits, wg2,
+                      logits2);
   } else if (T >= 4) {
     dim3 grid((T + 3) / 4, (E + 3) / 4, nz);
-    router_logits_kernel<4, 4><<<grid, 128, 0, st>>>(x, x_bf16, wg, w_bf16, T, E, H, logits, wg2, logits2);
+    return launch_pdl(router_logits_kernel<4, 4>, grid, 128, 0, st, x, x_bf16, wg, w_bf16, T, E, H, logits, wg2,
+                      logits2);
   } else {
     int te = (E >= 256) ? 2 : 1;
     dim3 grid(T, (E + te - 1) / te, nz);
     if (te == 2)
-      router_logits_kernel<1, 2><<<grid, 128, 0, st>>>(x, x_bf16, wg, w_bf16, T, E, H, logits, wg2, logits2);
+      return launch_pdl(router_logits_kernel<1, 2>, grid, 128, 0, st, x, x_bf16, wg, w_bf16, T, E, H, logits, wg2,
+                        logits2);
     else
-      router_logits_kernel<1, 1><<<grid, 128, 0, st>>>(x, x_bf16, wg, w_bf16, T, E, H, logits, wg2, logits2);
+      return launch_pdl(router_logits_kernel<1, 1>, grid, 128, 0, st, x, x_bf16, wg, w_bf16, T, E, H, logits, wg2,
+                        logits2);
   }
   return cudaGetLastError();
 }
@@ -299,9 +307,8 @@ cudaError_t launch_router_select(const float* logits, const float* e_bias, int T
                                  float* wts2) {
   SelCfg c{E, k, mode, norm_topk, n_group, topk_group, scaling};
   dim3 grid((T + kSelWarps - 1) / kSelWarps, logits2 ? 2 : 1);
-  router_select_kernel<<<grid, kSelWarps * 32, 0, st>>>(logits, e_bias, T, c, inds, wts, logits2, e_bias2, inds2,
-                                                          wts2);
-  return cudaGetLastError();
+  return launch_pdl(router_select_kernel, grid, kSelWarps * 32, 0, st, logits, e_bias, T, c, inds, wts, logits2, e_bias2,
+                    inds2, wts2);
 }
 
 }  // namespace ef
