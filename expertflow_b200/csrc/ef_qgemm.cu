@@ -19,9 +19,10 @@
 //               swizzle = the UMMA K-major canonical layout) into an act ring
 //   warp 1      TMEM allocation (512 columns); lane 0 issues tcgen05.mma
 //               (M=128, N = segment rows rounded to 16, K=16) and commits
-//   warps 2-9   dequantise one weight row each: codes -> exact fp16 q
-//               (mantissa trick + one fp16 FMA) -> fp16 s*q + b (one fp16 FMA,
-//               single rounding) -> tcgen05.st into the A tile of its lane
+//   warps 2-9   dequantise one weight row each: codes -> fp16 1024 + q under
+//               the exponent of 1024 (8-bit: one byte permute per pair; 4-bit:
+//               LOP3 + shift) -> exact q (one fp16 subtraction) -> fp16 s*q + b
+//               (one fp16 FMA, single rounding) -> tcgen05.st into the A tile
 //   warps 10-17 epilogue (two per TMEM lane quarter, alternate 32-column
 //               blocks): tcgen05.ld of both accumulators; gate/up pass:
 //               h = silu(g) * u -> fp16 rows; down pass: fp32 rows
@@ -197,12 +198,16 @@ EF_DEV uint4 load_group_block(const uint16_t* row, int blk, int ng) {
 }
 
 // fp16 pair (1 + qa/1024, 1 + qb/1024) -> (s qa + b, s qb + b), exact q then one rounding
+// fp16 pair (1024 + q0, 1024 + q1) -> the weights (s q0 + b, s q1 + b): the
+// subtraction is exact, the FMA rounds once.
 EF_DEV uint32_t dq_pair(uint32_t v, __half2 s2, __half2 b2) {
-  const __half2 q = __hfma2(*reinterpret_cast<const __half2*>(&v), __float2half2_rn(1024.0f),
-                            __float2half2_rn(-1024.0f));
+  const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&v), __float2half2_rn(1024.0f));
   const __half2 w = __hfma2(q, s2, b2);
   return *reinterpret_cast<const uint32_t*>(&w);
 }
+// Bytes of v picked by `sel` (0x4240: 0, 2; 0x4341: 1, 3) under the high byte
+// 0x64: the fp16 pair (1024 + b, 1024 + b').
+EF_DEV uint32_t code_pair8(uint32_t v, uint32_t sel) { return prmt(v, 0x64646464u, sel); }
 
 template <int BITS, int MODE>
 __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_constant__ GemmParams p) {
@@ -447,19 +452,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
 #pragma unroll
           for (int b = 0; b < 8; ++b) {  // block b: words (2b, 2b+1) = columns 8b..8b+7
             const uint32_t wa = wv[2 * b], wb = wv[2 * b + 1];
-            a[4 * b + 0] = dq_pair(lop3_and_or(wa, 0x00FF00FFu, 0x3C003C00u), s2, b2);       // (c0, c2)
-            a[4 * b + 1] = dq_pair(lop3_and_or(wb, 0x00FF00FFu, 0x3C003C00u), s2, b2);       // (c4, c6)
-            a[4 * b + 2] = dq_pair(lop3_and_or(wa >> 8, 0x00FF00FFu, 0x3C003C00u), s2, b2);  // (c1, c3)
-            a[4 * b + 3] = dq_pair(lop3_and_or(wb >> 8, 0x00FF00FFu, 0x3C003C00u), s2, b2);  // (c5, c7)
+            a[4 * b + 0] = dq_pair(code_pair8(wa, 0x4240u), s2, b2);  // (c0, c2)
+            a[4 * b + 1] = dq_pair(code_pair8(wb, 0x4240u), s2, b2);  // (c4, c6)
+            a[4 * b + 2] = dq_pair(code_pair8(wa, 0x4341u), s2, b2);  // (c1, c3)
+            a[4 * b + 3] = dq_pair(code_pair8(wb, 0x4341u), s2, b2);  // (c5, c7)
           }
         } else {
 #pragma unroll
           for (int b = 0; b < 8; ++b) {  // block b = word b: nibble pairs (s, s+4)
             const uint32_t wd = wv[b];
-            a[4 * b + 0] = dq_pair(lop3_and_or(wd, 0x000F000Fu, 0x3C003C00u), s2, b2);
-            a[4 * b + 1] = dq_pair(lop3_and_or(wd >> 4, 0x000F000Fu, 0x3C003C00u), s2, b2);
-            a[4 * b + 2] = dq_pair(lop3_and_or(wd >> 8, 0x000F000Fu, 0x3C003C00u), s2, b2);
-            a[4 * b + 3] = dq_pair(lop3_and_or(wd >> 12, 0x000F000Fu, 0x3C003C00u), s2, b2);
+            a[4 * b + 0] = dq_pair(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), s2, b2);
+            a[4 * b + 1] = dq_pair(lop3_and_or(wd >> 4, 0x000F000Fu, 0x64006400u), s2, b2);
+            a[4 * b + 2] = dq_pair(lop3_and_or(wd >> 8, 0x000F000Fu, 0x64006400u), s2, b2);
+            a[4 * b + 3] = dq_pair(lop3_and_or(wd >> 12, 0x000F000Fu, 0x64006400u), s2, b2);
           }
         }
         if (f >= (uint32_t)kGemmABufs &&

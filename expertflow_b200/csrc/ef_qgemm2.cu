@@ -364,10 +364,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kG2Threads, 1)
 #pragma unroll
           for (int b = 0; b < 4; ++b) {
             const uint32_t wa = wv[2 * b], wb = wv[2 * b + 1];
-            a[4 * b + 0] = dq_pair(lop3_and_or(wa, 0x00FF00FFu, 0x3C003C00u), s2, b2);
-            a[4 * b + 1] = dq_pair(lop3_and_or(wb, 0x00FF00FFu, 0x3C003C00u), s2, b2);
-            a[4 * b + 2] = dq_pair(lop3_and_or(wa >> 8, 0x00FF00FFu, 0x3C003C00u), s2, b2);
-            a[4 * b + 3] = dq_pair(lop3_and_or(wb >> 8, 0x00FF00FFu, 0x3C003C00u), s2, b2);
+            a[4 * b + 0] = dq_pair(code_pair8(wa, 0x4240u), s2, b2);
+            a[4 * b + 1] = dq_pair(code_pair8(wb, 0x4240u), s2, b2);
+            a[4 * b + 2] = dq_pair(code_pair8(wa, 0x4341u), s2, b2);
+            a[4 * b + 3] = dq_pair(code_pair8(wb, 0x4341u), s2, b2);
           }
         } else {
           // 32-byte rows, 32-byte swizzle: chunk q at q ^ ((lr >> 2) & 1); this half = chunk khalf
@@ -376,10 +376,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kG2Threads, 1)
 #pragma unroll
           for (int b = 0; b < 4; ++b) {
             const uint32_t wd = wv[b];
-            a[4 * b + 0] = dq_pair(lop3_and_or(wd, 0x000F000Fu, 0x3C003C00u), s2, b2);
-            a[4 * b + 1] = dq_pair(lop3_and_or(wd >> 4, 0x000F000Fu, 0x3C003C00u), s2, b2);
-            a[4 * b + 2] = dq_pair(lop3_and_or(wd >> 8, 0x000F000Fu, 0x3C003C00u), s2, b2);
-            a[4 * b + 3] = dq_pair(lop3_and_or(wd >> 12, 0x000F000Fu, 0x3C003C00u), s2, b2);
+            a[4 * b + 0] = dq_pair(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), s2, b2);
+            a[4 * b + 1] = dq_pair(lop3_and_or(wd >> 4, 0x000F000Fu, 0x64006400u), s2, b2);
+            a[4 * b + 2] = dq_pair(lop3_and_or(wd >> 8, 0x000F000Fu, 0x64006400u), s2, b2);
+            a[4 * b + 3] = dq_pair(lop3_and_or(wd >> 12, 0x000F000Fu, 0x64006400u), s2, b2);
           }
         }
         if (f >= (uint32_t)NA && !mbar_wait_cluster(&afree[ab], ((f / NA) - 1) & 1u, kDevErrTimeoutTc)) {

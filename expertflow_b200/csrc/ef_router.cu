@@ -144,6 +144,21 @@ struct SelCfg {
 
 EF_DEV bool ranks_before(float va, int ia, float vb, int ib) { return (va > vb) || (va == vb && ia < ib); }
 
+// Order-preserving unsigned key of a float (larger float -> larger key; -0
+// and +0 map to the same key, as they compare equal).
+EF_DEV uint32_t order_key(float v) {
+  const uint32_t u = __float_as_uint(__fadd_rn(v, 0.0f));  // -0 + 0 = +0
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Warp-wide arg-max by (value desc, index asc) from each lane's candidate
+// (key 0 and index 0x7fffffff for none): the largest key, then the smallest
+// index among the lanes that hold it -- two warp reductions.
+EF_DEV int warp_argmax_key(uint32_t key, int idx) {
+  const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+  return (int)__reduce_min_sync(0xffffffffu, key == kmax ? (uint32_t)idx : 0x7fffffffu);
+}
+
 // warp-wide arg-max by (value desc, index asc)
 EF_DEV void warp_argmax(float& v, int& i) {
 #pragma unroll
@@ -226,20 +241,29 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const flo
       if (!((keep >> (e / gsz)) & 1u)) sc[e] = 0.0f;
     __syncwarp();
   }
-  // top-k over sc by (value desc, index asc)
+  // top-k over sc by (value desc, index asc); each lane keeps the keys of its
+  // elements e = lane + 32 r, a taken element's key drops to 0
   int sel[16];
-  unsigned taken_lo = 0;  // bit r: this lane's r-th element (e = lane + 32 r) taken
+  constexpr int kPerLane = kMaxE / 32;
+  uint32_t keys[kPerLane];
+#pragma unroll
+  for (int r = 0; r < kPerLane; ++r) keys[r] = lane + 32 * r < E ? order_key(sc[lane + 32 * r]) : 0u;
   for (int j = 0; j < k; ++j) {
-    float bv = -INFINITY;
+    uint32_t bk = 0u;
     int bi = 0x7fffffff;
-    for (int r = 0, e = lane; e < E; ++r, e += 32) {
-      if ((taken_lo >> r) & 1u) continue;
-      float v = sc[e];
-      if (bi == 0x7fffffff || ranks_before(v, e, bv, bi)) { bv = v; bi = e; }
+#pragma unroll
+    for (int r = 0; r < kPerLane; ++r)
+      if (keys[r] > bk) {  // strict: the lane's lower index wins ties
+        bk = keys[r];
+        bi = lane + 32 * r;
+      }
+    const int win = warp_argmax_key(bk, bi);
+    sel[j] = win;
+    if ((win & 31) == lane) {
+#pragma unroll
+      for (int r = 0; r < kPerLane; ++r)
+        if (r == (win >> 5)) keys[r] = 0u;
     }
-    warp_argmax(bv, bi);
-    sel[j] = bi;
-    if ((bi & 31) == lane) taken_lo |= 1u << (bi >> 5);
   }
   // weights (every lane computes the same values; lane 0 writes)
   float w[16];
