@@ -122,18 +122,8 @@ EF_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
-// Prefetch a contiguous global range into L2 (bytes % 16 == 0, 16-byte aligned).
-EF_DEV void prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
-               : "memory");
-}
 EF_DEV void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-// ---------------------------------------------------------------- named barriers
-EF_DEV void named_bar_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // ---------------------------------------------------------------- bit tricks

@@ -77,7 +77,6 @@ __host__ __device__ constexpr int row_of_lane(int g) {
 constexpr int kSbChunk = 32;                          // groups per chunk
 constexpr int kSbBox = kRowTile * kSbChunk * 2;       // bytes of one array's box
 constexpr int kXsPitchChunk = kSbChunk + 4;           // floats
-__host__ __device__ inline bool sb_chunkable(int K) { return ((K / 64) & 7) == 0; }
 
 template <int BITS, int MODE>
 __host__ __device__ inline size_t qmv_slot_bytes(int K, bool chunked) {
