@@ -424,8 +424,79 @@ def section_stream(name, spec, args, dev):
              "copies_prefetch": st["copies_prefetch"], "prefetch_used": st["prefetch_used"],
              "copies_sync": st["copies_sync"]}
         out["lookahead" if la else "no_lookahead"] = d
+    if args.stream_files != "off":
+        out["files"] = stream_from_files(spec, host, gates, run, steps, budget, ms_res, args)
     del host
     return out
+
+
+def stream_from_files(spec, host, gates, run, steps, budget, ms_res, args):
+    """The same decode with the experts in safetensors files on local disk
+    (one shard per 8 layers, mlx_lm tensor names) under a pinned host tier of
+    `--stream-host-frac` of all experts: misses in HBM and the host tier are
+    read from the files by the library's reader threads (O_DIRECT unless the
+    file system refuses it)."""
+    import shutil
+    import tempfile
+
+    import numpy as np
+    from expertflow_b200 import _lib as L, pool as P, weights as W
+
+    NL, E = len(host), spec.n_experts
+    root = tempfile.mkdtemp(prefix="ef_stream_", dir=args.stream_dir or None)
+    try:
+        t0 = time.perf_counter()
+        wm, per = {}, 8
+        for k in range(0, NL, per):
+            fn = f"model-{k // per + 1:05d}-of-{(NL + per - 1) // per:05d}.safetensors"
+            t = {}
+            for layer in range(k, min(NL, k + per)):
+                for m, pn in zip(("gate", "up", "down"), ("gate_proj", "up_proj", "down_proj")):
+                    w, sc, b = (a.numpy() for a in host[layer][m])
+                    pre = f"model.layers.{layer}.mlp.switch_mlp.{pn}"
+                    t[f"{pre}.weight"] = (w.view(np.uint32), "U32")
+                    t[f"{pre}.scales"] = (sc, "F16")
+                    t[f"{pre}.biases"] = (b, "F16")
+            W.write_safetensors(os.path.join(root, fn), t)
+            wm.update({n: fn for n in t})
+        with open(os.path.join(root, "model.safetensors.index.json"), "w") as f:
+            json.dump({"weight_map": wm}, f)
+        write_s = time.perf_counter() - t0
+        direct = args.stream_files == "direct"
+        try:
+            store = P.ExpertStore.from_safetensors(root, spec=spec, direct=direct)
+        except L.EfmoeError as ex:
+            if not direct or ex.status != -9:
+                raise
+            direct = False
+            store = P.ExpertStore.from_safetensors(root, spec=spec)
+        host_blobs = max(2 * spec.top_k, int(args.stream_host_frac * NL * E))
+        pl = P.ExpertSlotPool.from_store(store, budget=budget, host_blobs=host_blobs, headroom=spec.top_k)
+        run(pl, True, min(16, steps))
+        pl.reset_stats()
+        f0 = store.info()["file_bytes"]
+        ms = run(pl, True, steps)
+        st = pl.stats()
+        fb = store.info()["file_bytes"] - f0
+        info = store.info()
+        pl.close()
+        store.close()
+        asked = st["host_hits"] + st["host_reads"]
+        return {"tokens_per_s": round(steps / (ms * 1e-3), 2), "ms_per_token": round(ms / steps, 4),
+                "direct_io": bool(info["direct"]), "readers": info["n_readers"],
+                "host_blobs": host_blobs, "host_frac": args.stream_host_frac,
+                "model_bytes_on_disk": int(sum(os.path.getsize(os.path.join(root, n)) for n in os.listdir(root))),
+                "write_s": round(write_s, 1),
+                "hit_rate": round(st["hit_rate"], 4),
+                "host_hit_rate": round(st["host_hits"] / asked, 4) if asked else None,
+                "host_reads_per_token": round(st["host_reads"] / steps, 3),
+                "host_reads_ahead": st["host_reads_ahead"],
+                "file_bytes_per_token": round(fb / steps),
+                "file_gbs": round(fb / (ms * 1e-3) / 1e9, 2),
+                "read_wait_ms_per_token": round(st["read_wait_ms"] / steps, 4),
+                "exposed_vs_resident_ms_per_token": round(max(0.0, ms - ms_res) / steps, 4)}
+    finally:
+        shutil.rmtree(root, ignore_errors=True)
 
 
 def bench_ours(args):
@@ -626,6 +697,10 @@ def main():
                          "c4 (DeepSeek-V3 8-bit prefill), c3 (48-layer streamed decode)")
     ap.add_argument("--stream-layers", type=int, default=48)
     ap.add_argument("--stream-steps", type=int, default=512)
+    ap.add_argument("--stream-files", default="direct", choices=["direct", "buffered", "off"],
+                    help="c3 again with the experts in safetensors files under a bounded pinned host tier")
+    ap.add_argument("--stream-host-frac", type=float, default=0.25)
+    ap.add_argument("--stream-dir", default=None, help="where the c3 model files go (default: the temp dir)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -21,6 +21,7 @@ STATUS = {
     -6: "EF_ERR_SLOT_MISS",
     -7: "EF_ERR_RANGE",
     -8: "EF_ERR_NOT_READY",
+    -9: "EF_ERR_IO",
 }
 EF_DT_BF16, EF_DT_F16, EF_DT_F32 = 0, 1, 2
 EF_ROUTER_SOFTMAX, EF_ROUTER_SIGMOID_GROUP = 0, 1
@@ -72,13 +73,27 @@ class PoolStats(ctypes.Structure):
     _fields_ = [("accesses", ctypes.c_longlong), ("hits", ctypes.c_longlong), ("misses", ctypes.c_longlong),
                 ("copies_sync", ctypes.c_longlong), ("copies_prefetch", ctypes.c_longlong),
                 ("prefetch_used", ctypes.c_longlong), ("evictions", ctypes.c_longlong),
-                ("tokens", ctypes.c_longlong), ("h2d_bytes", ctypes.c_double), ("copy_ms", ctypes.c_double)]
+                ("tokens", ctypes.c_longlong), ("h2d_bytes", ctypes.c_double), ("copy_ms", ctypes.c_double),
+                ("host_hits", ctypes.c_longlong), ("host_reads", ctypes.c_longlong),
+                ("host_reads_ahead", ctypes.c_longlong), ("host_evictions", ctypes.c_longlong),
+                ("read_wait_ms", ctypes.c_double)]
 
     def as_dict(self) -> dict:
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
 EF_POLICY_FREQ, EF_POLICY_LRU = 0, 1
+
+
+class FileArray(ctypes.Structure):
+    _fields_ = [("file", ctypes.c_int), ("bf16", ctypes.c_int), ("offset", ctypes.c_longlong),
+                ("stride", ctypes.c_longlong)]
+
+
+class StoreInfo(ctypes.Structure):
+    _fields_ = [("blob_bytes", ctypes.c_size_t), ("offsets", ctypes.c_size_t * 10), ("n_layers", ctypes.c_int),
+                ("n_readers", ctypes.c_int), ("direct", ctypes.c_int), ("reads", ctypes.c_longlong),
+                ("file_bytes", ctypes.c_double)]
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -128,6 +143,11 @@ SIGNATURES = {
     "ef_pool_get_stats": (_I, [_P, ctypes.POINTER(PoolStats)]),
     "ef_pool_reset_stats": (_I, [_P]),
     "ef_pool_destroy": (_I, [_P]),
+    "ef_store_open": (_I, [_CFGP, _I, _P, _I, ctypes.POINTER(FileArray), _I, _I, _P]),
+    "ef_store_get_info": (_I, [_P, ctypes.POINTER(StoreInfo)]),
+    "ef_store_read": (_I, [_P, _I, _P, _P, _P]),
+    "ef_store_close": (_I, [_P]),
+    "ef_pool_create_from_store": (_I, [_CFGP, ctypes.POINTER(PoolCfg), _P, _I, _P]),
 }
 
 _lib = None

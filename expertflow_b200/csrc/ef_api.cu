@@ -466,6 +466,7 @@ const char* ef_status_string(ef_status s) {
     case EF_ERR_SLOT_MISS: return "expert not resident";
     case EF_ERR_RANGE: return "value out of range";
     case EF_ERR_NOT_READY: return "not ready";
+    case EF_ERR_IO: return "file read failed";
     default: return "unknown status";
   }
 }

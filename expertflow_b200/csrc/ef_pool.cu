@@ -24,8 +24,18 @@
 //     overlap compute.  trim() runs once per token (ef_pool_end_token), as the
 //     reference trims after each token; the headroom slots hold the token's
 //     misses until then.
+// (3) A pool over an ef_expert_store (ef_pool_create_from_store) keeps only a
+//     bounded number of pinned host blobs, the least recently used replaced;
+//     an expert in neither HBM nor the host tier is read from the model files
+//     by the store's reader threads.  The step starts its own reads first,
+//     then the lookahead starts the reads of the next layer's predicted
+//     experts (they run while this layer computes, and their copies into HBM
+//     follow when that layer runs), then it waits for its own reads.
 #include <algorithm>
+#include <chrono>
 #include <cstring>
+#include <memory>
+#include <set>
 #include <thread>
 #include <unordered_map>
 #include <vector>
@@ -248,6 +258,20 @@ struct ef_slot_pool {
   ef_pool_stats st{};
   std::vector<ef::CopyTimer> timers;       // one per copy batch, folded into st.copy_ms on demand
   std::vector<ef::CopyTimer> spare;
+  // host tier over a store: host_blobs then holds host_n blobs, replaced
+  // least recently used first, instead of every expert of every layer
+  ef_expert_store* store = nullptr;
+  int host_n = 0;
+  std::vector<long long> host_key;             // layer * E + expert, -1: free
+  std::vector<unsigned long long> host_last;   // recency
+  std::vector<unsigned long long> host_pin;    // the step that needs the blob (not replaced during it)
+  std::unique_ptr<ef::ReadTicket[]> host_ticket;
+  std::vector<cudaEvent_t> host_copied;        // after the last copy out of the blob
+  std::vector<char> host_has_copy;
+  std::vector<int> host_free;
+  std::set<std::pair<unsigned long long, int>> host_lru;  // (recency, blob) of the occupied blobs
+  std::unordered_map<long long, int> host_where;
+  unsigned long long host_clock = 0, epoch = 0;
 };
 
 namespace {
@@ -320,8 +344,9 @@ ef_status flush_stage(ef_slot_pool* P, int ln) {
 }
 
 // Copy expert e of layer l into slot s: one blob copy into the staging ring
-// (the scatter into the slot arrays follows in flush_stage).
-ef_status copy_expert(ef_slot_pool* P, int ln, int l, int e, int s) {
+// (the scatter into the slot arrays follows in flush_stage).  h: the expert's
+// host-tier blob in a pool over a store (read complete), else -1.
+ef_status copy_expert(ef_slot_pool* P, int ln, int l, int e, int s, int h) {
   LayerSlots& L = P->layers[l];
   auto& C = P->lane[ln];
   if (C.n_staged == ef::kScatterMax) {
@@ -336,10 +361,14 @@ ef_status copy_expert(ef_slot_pool* P, int ln, int l, int e, int s) {
       C.scat.dst[3 * j + 2] = v.b[j];
     }
   }
-  const uint8_t* src = P->host_blobs + ((size_t)l * P->cfg.n_experts + e) * P->blob_bytes;
+  const uint8_t* src = P->host_blobs + (h >= 0 ? (size_t)h : (size_t)l * P->cfg.n_experts + e) * P->blob_bytes;
   if (cudaMemcpyAsync(C.stage + (size_t)C.n_staged * P->blob_bytes, src, P->blob_bytes, cudaMemcpyHostToDevice,
                       C.stream) != cudaSuccess)
     return fail(EF_ERR_CUDA, "expert copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+  if (h >= 0) {
+    cudaEventRecord(P->host_copied[h], C.stream);
+    P->host_has_copy[h] = 1;
+  }
   C.scat.slot[C.n_staged++] = s;
   L.slot_expert[s] = e;
   L.expert_slot[e] = s;
@@ -363,6 +392,93 @@ int take_slot(ef_slot_pool* P, int l, const std::vector<char>& keep) {
     }
   }
   return -1;
+}
+
+// ---- host tier (pools over a store)
+int host_find(const ef_slot_pool* P, int l, int e) {
+  auto it = P->host_where.find((long long)l * P->cfg.n_experts + e);
+  return it == P->host_where.end() ? -1 : it->second;
+}
+
+void host_touch(ef_slot_pool* P, int h) {
+  P->host_lru.erase({P->host_last[h], h});
+  P->host_last[h] = ++P->host_clock;
+  P->host_lru.insert({P->host_last[h], h});
+  P->host_pin[h] = P->epoch;
+}
+
+void host_drop(ef_slot_pool* P, int h) {
+  P->host_where.erase(P->host_key[h]);
+  P->host_lru.erase({P->host_last[h], h});
+  P->host_key[h] = -1;
+  P->host_free.push_back(h);
+}
+
+// Expert e of layer l in the host tier, pinned for this step: found, or its
+// read from the files started into a free or the least recently used blob
+// that this step does not need.  Returns the blob, or -1 when none can be
+// replaced.
+int host_fetch(ef_slot_pool* P, int l, int e, bool ahead) {
+  int h = host_find(P, l, e);
+  if (h >= 0) {
+    host_touch(P, h);
+    P->st.host_hits++;
+    return h;
+  }
+  if (!P->host_free.empty()) {
+    h = P->host_free.back();
+    P->host_free.pop_back();
+  } else {
+    for (const auto& it : P->host_lru) {
+      const int c = it.second;
+      if (P->host_pin[c] != P->epoch && ef::store_done(&P->host_ticket[c])) {
+        h = c;
+        break;
+      }
+    }
+    if (h < 0 && !ahead) {  // only reads in flight are left to replace: take the oldest once it lands
+      for (const auto& it : P->host_lru) {
+        if (P->host_pin[it.second] != P->epoch) {
+          h = it.second;
+          ef::store_wait(P->store, &P->host_ticket[h], 0, 0);
+          break;
+        }
+      }
+    }
+    if (h < 0) return -1;
+    host_drop(P, h);
+    P->host_free.pop_back();
+    P->st.host_evictions++;
+  }
+  if (P->host_has_copy[h]) {  // a copy out of the blob may still be in flight
+    cudaEventSynchronize(P->host_copied[h]);
+    P->host_has_copy[h] = 0;
+  }
+  const long long key = (long long)l * P->cfg.n_experts + e;
+  P->host_key[h] = key;
+  P->host_where[key] = h;
+  P->host_last[h] = ++P->host_clock;
+  P->host_lru.insert({P->host_last[h], h});
+  P->host_pin[h] = P->epoch;
+  ef::store_submit(P->store, l, e, P->host_blobs + (size_t)h * P->blob_bytes, &P->host_ticket[h]);
+  P->st.host_reads++;
+  if (ahead) P->st.host_reads_ahead++;
+  return h;
+}
+
+// Waits for blob h's read; a failed read leaves the tier (the next request reads again).
+ef_status host_ready(ef_slot_pool* P, int h, int l, int e) {
+  ef::ReadTicket* t = &P->host_ticket[h];
+  ef_status s;
+  if (!ef::store_done(t)) {
+    const auto t0 = std::chrono::steady_clock::now();
+    s = ef::store_wait(P->store, t, l, e);
+    P->st.read_wait_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  } else {
+    s = ef::store_wait(P->store, t, l, e);
+  }
+  if (s) host_drop(P, h);
+  return s;
 }
 
 void copies_begin(ef_slot_pool* P, int ln, LayerSlots& L) {
@@ -420,6 +536,76 @@ ef_status pool_route(const ef_moe_cfg& cfg, const void* x, int T, const void* gw
   return EF_OK;
 }
 
+ef_status check_pool_cfg(const ef_moe_cfg* cfg, const ef_pool_cfg* pc) {
+  ef_status s = check_cfg(cfg);
+  if (s) return s;
+  if (!pc) return fail(EF_ERR_INVALID, "null pointer");
+  if (pc->n_layers <= 0 || pc->budget < 0 || pc->headroom < cfg->top_k)
+    return fail(EF_ERR_INVALID, "need n_layers > 0, budget >= 0, headroom >= top_k");
+  if (pc->policy != EF_POLICY_FREQ && pc->policy != EF_POLICY_LRU) return fail(EF_ERR_INVALID, "unknown policy");
+  if (cfg->n_shared) return fail(EF_ERR_UNSUPPORTED, "the slot pool streams routed experts only (n_shared = 0)");
+  return EF_OK;
+}
+
+// The pool without its host contents: HBM slots, the two copy lanes (stream
+// + staging ring), n_host_blobs pinned host blobs and the per-layer state.
+ef_status pool_alloc(const ef_moe_cfg* cfg, const ef_pool_cfg* pc, size_t n_host_blobs, ef_slot_pool** out) {
+  const int E = cfg->n_experts;
+  const int n_slots = std::min(E, pc->budget + pc->headroom);
+  ef_slot_pool* P = new ef_slot_pool();
+  P->cfg = *cfg;
+  P->pc = *pc;
+  P->n_slots = n_slots;
+  cudaGetDevice(&P->dev);
+  const int H = cfg->hidden, I = cfg->inter, b = cfg->bits;
+  P->geom[0] = {I, H * b / 32, H / 64};
+  P->geom[1] = P->geom[0];
+  P->geom[2] = {H, I * b / 32, I / 64};
+  for (int j = 0; j < 3; ++j) P->expert_bytes += P->geom[j].wbytes() + 2 * P->geom[j].sbytes();
+  const ef::BlobLayout lay = ef::blob_layout(*cfg);
+  for (int a = 0; a < 10; ++a) P->blob_off[a] = P->scat.off[a] = lay.off[a];
+  for (int a = 0; a < 9; ++a) P->scat.size[a] = lay.size[a];
+  P->blob_bytes = P->scat.blob_bytes = lay.bytes;
+  const size_t per_layer = (size_t)n_slots * P->expert_bytes;
+  if (cudaMalloc(&P->dev_mem, per_layer * pc->n_layers) != cudaSuccess ||
+      cudaMalloc(&P->lane[0].stage, (size_t)ef::kScatterMax * P->blob_bytes) != cudaSuccess ||
+      cudaMalloc(&P->lane[1].stage, (size_t)ef::kScatterMax * P->blob_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    ef_pool_destroy(P);
+    return fail(EF_ERR_CUDA, "slot pool: cannot allocate %zu bytes of HBM", per_layer * pc->n_layers);
+  }
+  const size_t host_bytes = n_host_blobs * P->blob_bytes;
+  if (cudaMallocHost(&P->host_blobs, host_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    P->host_blobs = nullptr;
+    ef_pool_destroy(P);
+    return fail(EF_ERR_CUDA, "slot pool: cannot pin %zu bytes of host memory", host_bytes);
+  }
+  for (int ln = 0; ln < 2; ++ln) {
+    P->lane[ln].scat = P->scat;
+    P->lane[ln].scat.stage = P->lane[ln].stage;
+    if (cudaStreamCreateWithFlags(&P->lane[ln].stream, cudaStreamNonBlocking) != cudaSuccess) {
+      cudaGetLastError();
+      ef_pool_destroy(P);
+      return fail(EF_ERR_CUDA, "slot pool: stream creation failed");
+    }
+  }
+  P->layers.reserve(pc->n_layers);
+  for (int l = 0; l < pc->n_layers; ++l) {
+    P->layers.emplace_back(pc->policy, pc->budget, pc->decay);
+    LayerSlots& L = P->layers.back();
+    L.base = P->dev_mem + per_layer * l;
+    L.slot_expert.assign(n_slots, -1);
+    L.expert_slot.assign(E, -1);
+    L.staged.assign(E, 0);
+    cudaEventCreateWithFlags(&L.ready[0], cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&L.ready[1], cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&L.last_use, cudaEventDisableTiming);
+  }
+  *out = P;
+  return EF_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -458,15 +644,10 @@ ef_status ef_pool_create(const ef_moe_cfg* cfg, const ef_pool_cfg* pc, const ef_
                          const ef_qweight* host_up, const ef_qweight* host_down, ef_slot_pool** out) {
   if (!out) return fail(EF_ERR_INVALID, "out is NULL");
   *out = nullptr;
-  ef_status s = check_cfg(cfg);
+  ef_status s = check_pool_cfg(cfg, pc);
   if (s) return s;
-  if (!pc || !host_gate || !host_up || !host_down) return fail(EF_ERR_INVALID, "null pointer");
-  if (pc->n_layers <= 0 || pc->budget < 0 || pc->headroom < cfg->top_k)
-    return fail(EF_ERR_INVALID, "need n_layers > 0, budget >= 0, headroom >= top_k");
-  if (pc->policy != EF_POLICY_FREQ && pc->policy != EF_POLICY_LRU) return fail(EF_ERR_INVALID, "unknown policy");
-  if (cfg->n_shared) return fail(EF_ERR_UNSUPPORTED, "the slot pool streams routed experts only (n_shared = 0)");
+  if (!host_gate || !host_up || !host_down) return fail(EF_ERR_INVALID, "null pointer");
   const int E = cfg->n_experts;
-  const int n_slots = std::min(E, pc->budget + pc->headroom);
   for (int l = 0; l < pc->n_layers; ++l) {
     const ef_qweight* qs[3] = {&host_gate[l], &host_up[l], &host_down[l]};
     for (int j = 0; j < 3; ++j) {
@@ -482,52 +663,10 @@ ef_status ef_pool_create(const ef_moe_cfg* cfg, const ef_pool_cfg* pc, const ef_
       }
     }
   }
-  ef_slot_pool* P = new ef_slot_pool();
-  P->cfg = *cfg;
-  P->pc = *pc;
-  P->n_slots = n_slots;
-  cudaGetDevice(&P->dev);
-  const int H = cfg->hidden, I = cfg->inter, b = cfg->bits;
-  P->geom[0] = {I, H * b / 32, H / 64};
-  P->geom[1] = P->geom[0];
-  P->geom[2] = {H, I * b / 32, I / 64};
-  for (int j = 0; j < 3; ++j) P->expert_bytes += P->geom[j].wbytes() + 2 * P->geom[j].sbytes();
-  {
-    size_t o = 0;
-    for (int j = 0; j < 3; ++j) {
-      const size_t sz[3] = {P->geom[j].wbytes(), P->geom[j].sbytes(), P->geom[j].sbytes()};
-      for (int a = 0; a < 3; ++a) {
-        P->blob_off[3 * j + a] = o;
-        P->scat.size[3 * j + a] = sz[a];
-        o += (sz[a] + 15) & ~size_t(15);
-      }
-    }
-    P->blob_off[9] = o;
-    P->blob_bytes = (o + 255) & ~size_t(255);
-    for (int a = 0; a < 10; ++a) P->scat.off[a] = P->blob_off[a];
-    P->scat.blob_bytes = P->blob_bytes;
-  }
+  ef_slot_pool* P = nullptr;
+  if ((s = pool_alloc(cfg, pc, (size_t)pc->n_layers * E, &P))) return s;
   for (int j = 0; j < 3; ++j) P->host[j].assign((j == 0 ? host_gate : j == 1 ? host_up : host_down),
                                                  (j == 0 ? host_gate : j == 1 ? host_up : host_down) + pc->n_layers);
-  const size_t per_layer = (size_t)n_slots * P->expert_bytes;
-  if (cudaMalloc(&P->dev_mem, per_layer * pc->n_layers) != cudaSuccess ||
-      cudaMalloc(&P->lane[0].stage, (size_t)ef::kScatterMax * P->blob_bytes) != cudaSuccess ||
-      cudaMalloc(&P->lane[1].stage, (size_t)ef::kScatterMax * P->blob_bytes) != cudaSuccess) {
-    cudaGetLastError();
-    if (P->dev_mem) cudaFree(P->dev_mem);
-    if (P->lane[0].stage) cudaFree(P->lane[0].stage);
-    delete P;
-    return fail(EF_ERR_CUDA, "slot pool: cannot allocate %zu bytes of HBM", per_layer * pc->n_layers);
-  }
-  const size_t host_bytes = (size_t)pc->n_layers * E * P->blob_bytes;
-  if (cudaMallocHost(&P->host_blobs, host_bytes) != cudaSuccess) {
-    cudaGetLastError();
-    cudaFree(P->dev_mem);
-    cudaFree(P->lane[0].stage);
-    cudaFree(P->lane[1].stage);
-    delete P;
-    return fail(EF_ERR_CUDA, "slot pool: cannot pin %zu bytes of host memory", host_bytes);
-  }
   {  // repack the stacked arrays into per-expert blobs, layers in parallel
     const int nt = std::max(1, std::min(16, (int)std::thread::hardware_concurrency()));
     std::vector<std::thread> th;
@@ -549,31 +688,42 @@ ef_status ef_pool_create(const ef_moe_cfg* cfg, const ef_pool_cfg* pc, const ef_
     }
     for (auto& x : th) x.join();
   }
-  for (int ln = 0; ln < 2; ++ln) {
-    P->lane[ln].scat = P->scat;
-    P->lane[ln].scat.stage = P->lane[ln].stage;
-  }
   for (int j = 0; j < 3; ++j) P->host[j].clear();  // the caller's arrays are not read again
-  if (cudaStreamCreateWithFlags(&P->lane[0].stream, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaStreamCreateWithFlags(&P->lane[1].stream, cudaStreamNonBlocking) != cudaSuccess) {
-    cudaFree(P->dev_mem);
-    cudaFree(P->lane[0].stage);
-    cudaFree(P->lane[1].stage);
-    cudaFreeHost(P->host_blobs);
-    delete P;
-    return fail(EF_ERR_CUDA, "slot pool: stream creation failed");
-  }
-  P->layers.reserve(pc->n_layers);
-  for (int l = 0; l < pc->n_layers; ++l) {
-    P->layers.emplace_back(pc->policy, pc->budget, pc->decay);
-    LayerSlots& L = P->layers.back();
-    L.base = P->dev_mem + per_layer * l;
-    L.slot_expert.assign(n_slots, -1);
-    L.expert_slot.assign(E, -1);
-    L.staged.assign(E, 0);
-    cudaEventCreateWithFlags(&L.ready[0], cudaEventDisableTiming);
-    cudaEventCreateWithFlags(&L.ready[1], cudaEventDisableTiming);
-    cudaEventCreateWithFlags(&L.last_use, cudaEventDisableTiming);
+  *out = P;
+  return EF_OK;
+}
+
+ef_status ef_pool_create_from_store(const ef_moe_cfg* cfg, const ef_pool_cfg* pc, ef_expert_store* store,
+                                    int host_blobs, ef_slot_pool** out) {
+  if (!out) return fail(EF_ERR_INVALID, "out is NULL");
+  *out = nullptr;
+  ef_status s = check_pool_cfg(cfg, pc);
+  if (s) return s;
+  if (!store) return fail(EF_ERR_INVALID, "store is NULL");
+  const ef_moe_cfg& sc = store->cfg;
+  if (sc.hidden != cfg->hidden || sc.inter != cfg->inter || sc.bits != cfg->bits || sc.n_experts != cfg->n_experts)
+    return fail(EF_ERR_INVALID, "the store's layer shape differs from cfg");
+  if (store->n_layers != pc->n_layers) return fail(EF_ERR_INVALID, "the store holds %d layers, the pool %d",
+                                                   store->n_layers, pc->n_layers);
+  if (host_blobs < 2 * cfg->top_k) return fail(EF_ERR_INVALID, "host_blobs must be >= 2 * top_k");
+  host_blobs = (int)std::min<long long>(host_blobs, (long long)pc->n_layers * cfg->n_experts);
+  ef_slot_pool* P = nullptr;
+  if ((s = pool_alloc(cfg, pc, (size_t)host_blobs, &P))) return s;
+  P->store = store;
+  P->host_n = host_blobs;
+  P->host_key.assign(host_blobs, -1);
+  P->host_last.assign(host_blobs, 0);
+  P->host_pin.assign(host_blobs, 0);
+  P->host_ticket.reset(new ef::ReadTicket[host_blobs]);
+  P->host_copied.assign(host_blobs, nullptr);
+  P->host_has_copy.assign(host_blobs, 0);
+  for (int h = host_blobs - 1; h >= 0; --h) P->host_free.push_back(h);
+  for (int h = 0; h < host_blobs; ++h) {
+    if (cudaEventCreateWithFlags(&P->host_copied[h], cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      ef_pool_destroy(P);
+      return fail(EF_ERR_CUDA, "slot pool: event creation failed");
+    }
   }
   *out = P;
   return EF_OK;
@@ -631,7 +781,17 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
   const std::vector<int> need = distinct_sorted(P->h_inds, n, E);
   std::vector<char> keep(E, 0);
   for (int e : need) keep[e] = 1;
-  // 2. lookahead copies for the next layer (overlap this layer's experts)
+  LayerSlots& L = P->layers[layer];
+  ++P->epoch;
+  if (P->store) {  // start the file reads of this layer's experts missing in HBM and the host tier first
+    for (int e : need)
+      if (L.expert_slot[e] < 0 && host_fetch(P, layer, e, false) < 0)
+        return fail(EF_ERR_SLOT_MISS, "layer %d: the host tier (%d blobs) cannot hold one step's experts", layer,
+                    P->host_n);
+  }
+  // 2. lookahead copies for the next layer (overlap this layer's experts); in
+  //    a pool over a store, an expert not yet in the host tier has its read
+  //    started instead, and is copied when its layer runs
   if (next_gate_w) {
     const int nl = layer + 1;
     LayerSlots& N = P->layers[nl];
@@ -642,6 +802,17 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
     CopyTimer t{};
     for (int e : pred) {
       if (N.expert_slot[e] >= 0) continue;
+      int h = -1;
+      if (P->store) {
+        h = host_find(P, nl, e);
+        if (h < 0) {
+          host_fetch(P, nl, e, true);  // -1 (no blob to replace): the prediction is only a hint
+          continue;
+        }
+        if (!ef::store_done(&P->host_ticket[h]) || P->host_ticket[h].err.load()) continue;
+        host_touch(P, h);
+        P->st.host_hits++;
+      }
       const int sl = take_slot(P, nl, nkeep);
       if (sl < 0) break;  // no free slot: the prediction is only a hint
       if (!any) {
@@ -649,7 +820,7 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
         t = timer_begin(P, P->lane[1].stream);
         any = true;
       }
-      if ((s = copy_expert(P, 1, nl, e, sl))) return s;
+      if ((s = copy_expert(P, 1, nl, e, sl, h))) return s;
       N.staged[e] = 1;
       P->st.copies_prefetch++;
     }
@@ -661,8 +832,17 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
       N.has_ready[1] = true;
     }
   }
+  // this layer's file reads must be complete before its state changes (a
+  // failed read leaves the pool as it was)
+  if (P->store) {
+    for (int e : need) {
+      if (L.expert_slot[e] >= 0) continue;
+      const int h = host_find(P, layer, e);
+      if (h < 0) return fail(EF_ERR_SLOT_MISS, "layer %d expert %d left the host tier", layer, e);
+      if ((s = host_ready(P, h, layer, e))) return s;
+    }
+  }
   // 3. resolve this layer's experts (ef_engine.py:650-675): policy get, put on a miss
-  LayerSlots& L = P->layers[layer];
   bool any = false;
   CopyTimer t{};
   for (int e : need) {
@@ -694,7 +874,7 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
       t = timer_begin(P, P->lane[0].stream);
       any = true;
     }
-    if ((s = copy_expert(P, 0, layer, e, sl))) return s;
+    if ((s = copy_expert(P, 0, layer, e, sl, P->store ? host_find(P, layer, e) : -1))) return s;
     P->st.copies_sync++;
   }
   if (any) {
@@ -802,7 +982,10 @@ ef_status ef_pool_reset_stats(ef_slot_pool* P) {
 
 ef_status ef_pool_destroy(ef_slot_pool* P) {
   if (!P) return EF_OK;
-  for (auto& C : P->lane) cudaStreamSynchronize(C.stream);
+  for (auto& C : P->lane)
+    if (C.stream) cudaStreamSynchronize(C.stream);
+  for (int h = 0; h < P->host_n && P->host_ticket; ++h)  // reads still writing into the host blobs
+    if (!ef::store_done(&P->host_ticket[h])) ef::store_wait(P->store, &P->host_ticket[h], 0, 0);
   fold_timers(P, true);
   for (auto& t : P->spare) {
     cudaEventDestroy(t.a);
@@ -813,11 +996,13 @@ ef_status ef_pool_destroy(ef_slot_pool* P) {
     cudaEventDestroy(L.ready[1]);
     cudaEventDestroy(L.last_use);
   }
+  for (cudaEvent_t ev : P->host_copied)
+    if (ev) cudaEventDestroy(ev);
   for (auto& C : P->lane) {
-    cudaStreamDestroy(C.stream);
-    cudaFree(C.stage);
+    if (C.stream) cudaStreamDestroy(C.stream);
+    if (C.stage) cudaFree(C.stage);
   }
-  cudaFree(P->dev_mem);
+  if (P->dev_mem) cudaFree(P->dev_mem);
   if (P->host_blobs) cudaFreeHost(P->host_blobs);
   if (P->h_inds) cudaFreeHost(P->h_inds);
   delete P;

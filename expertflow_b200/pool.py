@@ -8,12 +8,17 @@
   (ef_engine.py:598, :650-675), and it runs the lookahead prediction of
   experiments/ef_v16_prefetch.py:92-113 (the next layer's gate on the
   current input) so the predicted experts' copies overlap this layer.
+* ``ExpertStore`` -- expert weights read out of the model files by the
+  library's reader threads (``ef_store_*``), the cold tier of a pool made
+  with ``ExpertSlotPool.from_store``.
 * ``zipf_layer_bias`` -- per-layer router logit bias log(p) for a shuffled
   Zipf popularity, the recipe of ef_integrated_engine.py:69-79.
 """
 from __future__ import annotations
 
 import ctypes
+import os
+from dataclasses import replace
 from typing import Optional, Sequence
 
 import numpy as np
@@ -97,6 +102,125 @@ class StreamedMoELayer:
         self.spec = spec
 
 
+def _pool_moe_cfg(spec: MoESpec) -> L.MoECfg:
+    return L.MoECfg(hidden=spec.hidden, inter=spec.inter, n_experts=spec.n_experts, top_k=spec.top_k,
+                    bits=spec.bits, group_size=spec.group_size, n_shared=0, shared_inter=0,
+                    act_dtype=L.EF_DT_BF16 if spec.act_dtype == "bfloat16" else L.EF_DT_F16,
+                    path=L.EF_PATH_AUTO, router_mode=spec.router_mode, norm_topk=int(spec.norm_topk),
+                    n_group=spec.n_group if spec.router != "softmax" else 1,
+                    topk_group=spec.topk_group if spec.router != "softmax" else 1,
+                    routed_scaling=spec.routed_scaling if spec.router != "softmax" else 1.0,
+                    gate_dtype=L.EF_DT_F16 if spec.gate_dtype == "float16" else L.EF_DT_BF16)
+
+
+_PROJS = ("gate", "up", "down")
+
+
+class ExpertStore:
+    """Expert weights read from model files by the library's reader threads
+    (``ef_store_*``): the cold tier below the slot pool's pinned host blobs,
+    standing in for the reference's memory-mapped expert reads and its
+    page-cache prefetcher (ef_deepseek_mmap.py:431-570,
+    experiments/ef_v18_prefetch2.py:76-200).
+
+    ranges: per layer, 9 ``(file index, bf16, offset, stride)`` tuples in the
+    order gate w, s, b, up w, s, b, down w, s, b -- expert e's copy of an
+    array is ``size`` bytes at ``offset + e * stride`` (``size`` follows from
+    the layer shape).  ``direct`` opens the files with O_DIRECT.  Host only:
+    a store reads without a GPU.
+    """
+
+    def __init__(self, spec: MoESpec, paths: Sequence[str], ranges: Sequence[Sequence[tuple]], n_readers: int = 0,
+                 direct: bool = False):
+        if spec.n_shared:
+            raise ValueError("the store holds routed experts only")
+        self.spec = spec
+        self.paths = [os.fspath(p) for p in paths]
+        self.n_layers = len(ranges)
+        arr = (L.FileArray * (9 * self.n_layers))()
+        for li, rs in enumerate(ranges):
+            if len(rs) != 9:
+                raise ValueError(f"layer {li}: 9 arrays expected, got {len(rs)}")
+            for a, (f, bf16, off, stride) in enumerate(rs):
+                arr[9 * li + a] = L.FileArray(int(f), int(bool(bf16)), int(off), int(stride))
+        self.cfg = _pool_moe_cfg(spec)
+        cpaths = (ctypes.c_char_p * len(self.paths))(*[p.encode() for p in self.paths])
+        h = ctypes.c_void_p()
+        L.check(L.lib().ef_store_open(ctypes.byref(self.cfg), self.n_layers, ctypes.cast(cpaths, ctypes.c_void_p),
+                                      len(self.paths), arr, int(n_readers), int(bool(direct)), ctypes.byref(h)))
+        self._h = h
+
+    @classmethod
+    def from_safetensors(cls, path_or_index, layers: Optional[Sequence[int]] = None, spec: Optional[MoESpec] = None,
+                         n_readers: int = 0, direct: bool = False) -> "ExpertStore":
+        """A store over the switch_mlp experts of a safetensors checkpoint
+        (layers: the checkpoint's MoE layer indices, in pool order; default
+        every layer that has switch_mlp experts)."""
+        from . import weights as W
+
+        index = path_or_index if isinstance(path_or_index, W.SafetensorsIndex) else W.SafetensorsIndex(path_or_index)
+        if layers is None:
+            layers = W.moe_layers(index)
+        if not layers:
+            raise KeyError("no switch_mlp experts in the checkpoint")
+        spec = spec or replace(W.infer_spec(index, layers[0]), n_shared=0)
+        files, ranges = [], []
+        for layer in layers:
+            rs = []
+            for fpath, bf16, off, stride in W.expert_ranges(index, layer, spec):
+                if fpath not in files:
+                    files.append(fpath)
+                rs.append((files.index(fpath), bf16, off, stride))
+            ranges.append(rs)
+        return cls(spec, files, ranges, n_readers=n_readers, direct=direct)
+
+    def info(self) -> dict:
+        i = L.StoreInfo()
+        L.check(L.lib().ef_store_get_info(self._h, ctypes.byref(i)))
+        return {"blob_bytes": int(i.blob_bytes), "offsets": [int(v) for v in i.offsets], "n_layers": i.n_layers,
+                "n_readers": i.n_readers, "direct": bool(i.direct), "reads": int(i.reads),
+                "file_bytes": float(i.file_bytes)}
+
+    def read(self, layers: Sequence[int], experts: Sequence[int]) -> list:
+        """Expert blobs (numpy uint8, blob_bytes each) read in parallel."""
+        n = len(layers)
+        if len(experts) != n:
+            raise ValueError("one expert per layer entry")
+        nb = self.info()["blob_bytes"]
+        bufs = [np.empty(nb, np.uint8) for _ in range(n)]
+        li = (ctypes.c_int32 * max(n, 1))(*layers)
+        ei = (ctypes.c_int32 * max(n, 1))(*experts)
+        dst = (ctypes.c_void_p * max(n, 1))(*[b.ctypes.data for b in bufs])
+        L.check(L.lib().ef_store_read(self._h, n, li, ei, dst))
+        return bufs
+
+    def split_blob(self, blob: np.ndarray) -> dict:
+        """{"gate": (w uint32 [out, words], s fp16 [out, groups], b fp16), "up": ..., "down": ...} views of a blob."""
+        off = self.info()["offsets"]
+        H, I, bits = self.spec.hidden, self.spec.inter, self.spec.bits
+        shapes = {"gate": (I, H), "up": (I, H), "down": (H, I)}
+        out = {}
+        for j, m in enumerate(_PROJS):
+            rows, cols = shapes[m]
+            w = blob[off[3 * j]:off[3 * j] + rows * cols * bits // 8].view(np.uint32).reshape(rows, cols * bits // 32)
+            sb = rows * (cols // 64) * 2
+            s = blob[off[3 * j + 1]:off[3 * j + 1] + sb].view(np.float16).reshape(rows, cols // 64)
+            b = blob[off[3 * j + 2]:off[3 * j + 2] + sb].view(np.float16).reshape(rows, cols // 64)
+            out[m] = (w, s, b)
+        return out
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            L.lib().ef_store_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class ExpertSlotPool:
     """HBM expert slots over a pinned-host expert pool (see module docstring).
 
@@ -104,40 +228,53 @@ class ExpertSlotPool:
     of CPU tensors in the stacked MLX layout ([E, out, in*bits/32] int32
     words, [E, out, in/64] fp16 scales and biases).  The pool copies them into
     its own pinned store (one blob per expert) when it is created.
+
+    ``ExpertSlotPool.from_store`` builds the pool over an ``ExpertStore``
+    instead: only ``host_blobs`` experts stay in pinned host memory, and the
+    rest are read from the model files when needed (or ahead, by the
+    lookahead).
     """
 
-    def __init__(self, spec: MoESpec, host_layers: Sequence[dict], budget: int, headroom: Optional[int] = None,
-                 policy: str = "freq", decay: float = 0.95, device=None):
+    def __init__(self, spec: MoESpec, host_layers: Optional[Sequence[dict]], budget: int,
+                 headroom: Optional[int] = None, policy: str = "freq", decay: float = 0.95, device=None,
+                 store: Optional[ExpertStore] = None, host_blobs: int = 0):
         if spec.n_shared:
             raise ValueError("the slot pool streams routed experts only")
         self.spec = spec
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-        self.n_layers = len(host_layers)
-        host = list(host_layers)
-        for hl in host:
-            for k in ("gate", "up", "down"):
-                for a in hl[k]:
-                    if a.is_cuda or not a.is_contiguous():
-                        raise ValueError("host expert arrays must be contiguous CPU tensors")
-        arr = L.QWeight * self.n_layers
-        self._qw = {k: arr(*[L.QWeight(hl[k][0].data_ptr(), hl[k][1].data_ptr(), hl[k][2].data_ptr())
-                             for hl in host]) for k in ("gate", "up", "down")}
-        self.cfg = L.MoECfg(hidden=spec.hidden, inter=spec.inter, n_experts=spec.n_experts, top_k=spec.top_k,
-                            bits=spec.bits, group_size=spec.group_size, n_shared=0, shared_inter=0,
-                            act_dtype=L.EF_DT_BF16 if spec.act_dtype == "bfloat16" else L.EF_DT_F16,
-                            path=L.EF_PATH_AUTO, router_mode=spec.router_mode, norm_topk=int(spec.norm_topk),
-                            n_group=spec.n_group if spec.router != "softmax" else 1,
-                            topk_group=spec.topk_group if spec.router != "softmax" else 1,
-                            routed_scaling=spec.routed_scaling if spec.router != "softmax" else 1.0,
-                            gate_dtype=L.EF_DT_F16 if spec.gate_dtype == "float16" else L.EF_DT_BF16)
+        self.cfg = _pool_moe_cfg(spec)
+        self.store = store
+        if store is not None:
+            self.n_layers = store.n_layers
+        else:
+            self.n_layers = len(host_layers)
+            host = list(host_layers)
+            for hl in host:
+                for k in _PROJS:
+                    for a in hl[k]:
+                        if a.is_cuda or not a.is_contiguous():
+                            raise ValueError("host expert arrays must be contiguous CPU tensors")
+            arr = L.QWeight * self.n_layers
+            self._qw = {k: arr(*[L.QWeight(hl[k][0].data_ptr(), hl[k][1].data_ptr(), hl[k][2].data_ptr())
+                                 for hl in host]) for k in _PROJS}
         self.pool_cfg = L.PoolCfg(n_layers=self.n_layers, budget=budget,
                                   headroom=spec.top_k if headroom is None else headroom,
                                   policy=_POLICIES[policy], decay=decay)
         h = ctypes.c_void_p()
         with torch.cuda.device(self.device):
-            L.check(L.lib().ef_pool_create(ctypes.byref(self.cfg), ctypes.byref(self.pool_cfg), self._qw["gate"],
-                                           self._qw["up"], self._qw["down"], ctypes.byref(h)))
+            if store is not None:
+                L.check(L.lib().ef_pool_create_from_store(ctypes.byref(self.cfg), ctypes.byref(self.pool_cfg),
+                                                          store._h, int(host_blobs), ctypes.byref(h)))
+            else:
+                L.check(L.lib().ef_pool_create(ctypes.byref(self.cfg), ctypes.byref(self.pool_cfg), self._qw["gate"],
+                                               self._qw["up"], self._qw["down"], ctypes.byref(h)))
         self._h = h
+
+    @classmethod
+    def from_store(cls, store: ExpertStore, budget: int, host_blobs: int, headroom: Optional[int] = None,
+                   policy: str = "freq", decay: float = 0.95, device=None) -> "ExpertSlotPool":
+        return cls(store.spec, None, budget, headroom=headroom, policy=policy, decay=decay, device=device,
+                   store=store, host_blobs=host_blobs)
 
     # -- the reference's call -------------------------------------------------
     def forward_layer(self, moe_module: StreamedMoELayer, x: torch.Tensor, next_moe: Optional[StreamedMoELayer] = None,

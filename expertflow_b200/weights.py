@@ -179,56 +179,42 @@ def _cfg_get(cfg: dict, *names, default=None):
     return default
 
 
-def load_layer_arrays(path_or_index, layer: int, group_size: Optional[int] = None,
-                      bits: Optional[int] = None) -> Tuple[dict, MoESpec]:
-    """One MoE layer as the library's layer dict (numpy, memory-mapped codes)
-    and the MoESpec that describes it (shapes from the tensors, routing from
-    config.json when the index has one)."""
+def infer_spec(path_or_index, layer: int, group_size: Optional[int] = None, bits: Optional[int] = None) -> MoESpec:
+    """The MoESpec of one MoE layer from its tensors' shapes and dtypes and
+    config.json (when the index has one); reads no tensor data."""
     index = path_or_index if isinstance(path_or_index, SafetensorsIndex) else SafetensorsIndex(path_or_index)
     cfg = index.config
     qcfg = cfg.get("quantization", cfg.get("quantization_config", {})) or {}
     group = group_size or int(qcfg.get("group_size", 64))
     pre = layer_prefix(index, layer)
-    gate = _qtriple(index, f"{pre}.switch_mlp.gate_proj")
-    up = _qtriple(index, f"{pre}.switch_mlp.up_proj")
-    down = _qtriple(index, f"{pre}.switch_mlp.down_proj")
-    E, inter, words = gate[0].shape
-    hidden = gate[1].shape[-1] * group
+    shape = {p: index.tensors[f"{pre}.switch_mlp.{p}.weight"].shape for p in _PROJ}
+    if any(len(v) != 3 for v in shape.values()):
+        raise ValueError(f"{pre}.switch_mlp: stacked [E, out, words] codes expected")
+    E, inter, words = shape["gate_proj"]
+    sname = f"{pre}.switch_mlp.gate_proj.scales"
+    if sname not in index:
+        raise ValueError(f"{pre}.switch_mlp.gate_proj: no scales")
+    hidden = index.tensors[sname].shape[-1] * group
     b = bits or (words * 32 // hidden)
     if words * 32 != hidden * b or b not in (4, 8):
         raise ValueError(f"{pre}: {words} words per row do not give a 4/8-bit code at hidden {hidden}")
-    for name, t, shp in (("up", up, (E, inter, words)), ("down", down, (E, hidden, inter * b // 32))):
-        if t[0].shape != shp:
-            raise ValueError(f"{pre}.switch_mlp.{name}_proj: shape {t[0].shape}, expected {shp}")
-    # router
+    for name, shp in (("up_proj", (E, inter, words)), ("down_proj", (E, hidden, inter * b // 32))):
+        if shape[name] != shp:
+            raise ValueError(f"{pre}.switch_mlp.{name}: shape {shape[name]}, expected {shp}")
     gname = f"{pre}.gate.weight"
-    gti = index.tensors[gname]
-    if f"{pre}.gate.scales" in index:  # quantised router: dequantise once (fp32 -> fp16)
-        gw, gs, gb = _qtriple(index, f"{pre}.gate")
-        gate_w = dequantize_np(gw, gs, gb, int(qcfg.get("bits", b)), group).astype(np.float16)
-        gate_dtype = "float16"
-    elif gti.dtype == "BF16":
-        gate_w = np.asarray(index.array(gname))  # uint16 bit patterns
-        gate_dtype = "bfloat16"
+    if f"{pre}.gate.scales" in index:
+        gate_dtype = "float16"  # a quantised router is dequantised to fp16
     else:
-        gate_w = _half(index, gname)
-        gate_dtype = "float16"
-    e_bias = None
-    ebn = f"{pre}.gate.e_score_correction_bias"
-    if ebn in index:
-        raw = np.asarray(index.array(ebn))
-        e_bias = ((raw.astype(np.uint32) << 16).view(np.float32) if index.tensors[ebn].dtype == "BF16"
-                  else raw.astype(np.float32))
-    shared = None
-    if f"{pre}.shared_experts.gate_proj.weight" in index:
-        shared = tuple(_qtriple(index, f"{pre}.shared_experts.{p}") for p in _PROJ)
+        gate_dtype = "bfloat16" if index.tensors[gname].dtype == "BF16" else "float16"
+    has_bias = f"{pre}.gate.e_score_correction_bias" in index
     n_shared = 0
-    if shared is not None:
-        s_inter = shared[0][0].shape[0]
+    sgn = f"{pre}.shared_experts.gate_proj.weight"
+    if sgn in index:
+        s_inter = index.tensors[sgn].shape[0]
         if s_inter % inter:
             raise ValueError(f"{pre}.shared_experts: inter {s_inter} is not a multiple of {inter}")
         n_shared = s_inter // inter
-    sigmoid = e_bias is not None or _cfg_get(cfg, "scoring_func") == "sigmoid"
+    sigmoid = has_bias or _cfg_get(cfg, "scoring_func") == "sigmoid"
     spec = MoESpec(
         hidden=hidden, n_experts=E, top_k=int(_cfg_get(cfg, "num_experts_per_tok", "num_experts_per_token",
                                                      default=8)),
@@ -240,8 +226,82 @@ def load_layer_arrays(path_or_index, layer: int, group_size: Optional[int] = Non
         n_shared=n_shared, act_dtype="float16" if _cfg_get(cfg, "torch_dtype") == "float16" else "bfloat16",
         gate_dtype=gate_dtype)
     spec.validate()
+    return spec
+
+
+def load_layer_arrays(path_or_index, layer: int, group_size: Optional[int] = None,
+                      bits: Optional[int] = None) -> Tuple[dict, MoESpec]:
+    """One MoE layer as the library's layer dict (numpy, memory-mapped codes)
+    and the MoESpec that describes it (shapes from the tensors, routing from
+    config.json when the index has one)."""
+    index = path_or_index if isinstance(path_or_index, SafetensorsIndex) else SafetensorsIndex(path_or_index)
+    spec = infer_spec(index, layer, group_size, bits)
+    qcfg = index.config.get("quantization", index.config.get("quantization_config", {})) or {}
+    pre = layer_prefix(index, layer)
+    gate = _qtriple(index, f"{pre}.switch_mlp.gate_proj")
+    up = _qtriple(index, f"{pre}.switch_mlp.up_proj")
+    down = _qtriple(index, f"{pre}.switch_mlp.down_proj")
+    # router
+    gname = f"{pre}.gate.weight"
+    if f"{pre}.gate.scales" in index:  # quantised router: dequantise once (fp32 -> fp16)
+        gw, gs, gb = _qtriple(index, f"{pre}.gate")
+        gate_w = dequantize_np(gw, gs, gb, int(qcfg.get("bits", spec.bits)), spec.group_size).astype(np.float16)
+    elif index.tensors[gname].dtype == "BF16":
+        gate_w = np.asarray(index.array(gname))  # uint16 bit patterns
+    else:
+        gate_w = _half(index, gname)
+    e_bias = None
+    ebn = f"{pre}.gate.e_score_correction_bias"
+    if ebn in index:
+        raw = np.asarray(index.array(ebn))
+        e_bias = ((raw.astype(np.uint32) << 16).view(np.float32) if index.tensors[ebn].dtype == "BF16"
+                  else raw.astype(np.float32))
+    shared = None
+    if spec.n_shared:
+        shared = tuple(_qtriple(index, f"{pre}.shared_experts.{p}") for p in _PROJ)
     layer_dict = {"gate_w": gate_w, "e_bias": e_bias, "gate": gate, "up": up, "down": down, "shared": shared}
     return layer_dict, spec
+
+
+def moe_layers(index: SafetensorsIndex) -> list:
+    """Layer indices (ascending) whose switch_mlp experts the index holds."""
+    out = set()
+    for name in index.tensors:
+        if name.endswith(".switch_mlp.gate_proj.weight") and name.startswith("model.layers."):
+            part = name.split(".")[2]
+            if part.isdigit():
+                out.add(int(part))
+    return sorted(out)
+
+
+def expert_ranges(index: SafetensorsIndex, layer: int, spec: MoESpec) -> list:
+    """Where each expert's bytes lie in the files: 9 ``(file, bf16, offset,
+    stride)`` in the order gate w, s, b, up w, s, b, down w, s, b.  A stacked
+    tensor [E, ...] is contiguous, so expert e's slice starts at
+    ``offset + e * stride`` with stride = tensor bytes / E -- the per-expert
+    offsets of the reference's prefetcher (experiments/ef_v18_prefetch2.py:137-146).
+    Scales / biases may be F16 or BF16 (bf16 = True: converted on read)."""
+    pre = layer_prefix(index, layer)
+    H, I, bits, E = spec.hidden, spec.inter, spec.bits, spec.n_experts
+    dims = {"gate_proj": (I, H), "up_proj": (I, H), "down_proj": (H, I)}
+    out = []
+    for p in _PROJ:
+        rows, cols = dims[p]
+        want = {"weight": (rows, cols * bits // 32), "scales": (rows, cols // spec.group_size),
+                "biases": (rows, cols // spec.group_size)}
+        for part in ("weight", "scales", "biases"):
+            name = f"{pre}.switch_mlp.{p}.{part}"
+            if name not in index:
+                raise KeyError(f"{name}: missing")
+            ti = index.tensors[name]
+            if ti.shape != (E, *want[part]):
+                raise ValueError(f"{name}: shape {ti.shape}, expected {(E, *want[part])}")
+            if part == "weight" and ti.dtype not in ("U32", "I32"):
+                raise ValueError(f"{name}: expected packed uint32 codes, got {ti.dtype}")
+            if part != "weight" and ti.dtype not in ("F16", "BF16"):
+                raise ValueError(f"{name}: scales / biases must be F16 or BF16 to stream, got {ti.dtype}")
+            out.append((ti.file, ti.dtype == "BF16", ti.offset, ti.nbytes // E))
+    return out
 
 
 def load_moe_layer(path_or_index, layer: int, device="cuda", spec: Optional[MoESpec] = None, **kw):
@@ -262,22 +322,23 @@ def load_moe_layer(path_or_index, layer: int, device="cuda", spec: Optional[MoES
 def write_safetensors(path: str, tensors: Dict[str, Tuple[np.ndarray, str]], metadata: Optional[dict] = None):
     """Write {name: (array, safetensors dtype)} (arrays in name order, 8-byte
     aligned data); BF16 arrays are given as their uint16 bit patterns."""
-    header, blobs, off = {}, [], 0
-    for name in sorted(tensors):
+    header, off = {}, 0
+    names = sorted(tensors)
+    for name in names:
         arr, dt = tensors[name]
-        data = np.ascontiguousarray(arr).tobytes()
-        header[name] = {"dtype": dt, "shape": list(arr.shape), "data_offsets": [off, off + len(data)]}
-        blobs.append(data)
-        off += len(data)
+        n = int(np.asarray(arr).nbytes)
+        header[name] = {"dtype": dt, "shape": list(arr.shape), "data_offsets": [off, off + n]}
+        off += n
     if metadata:
         header["__metadata__"] = metadata
     h = json.dumps(header, separators=(",", ":")).encode()
     h += b" " * ((-len(h)) % 8)
-    with open(path, "wb") as f:
+    with open(path, "wb") as f:  # tensor by tensor: no copy of the whole model in memory
         f.write(struct.pack("<Q", len(h)))
         f.write(h)
-        for d in blobs:
-            f.write(d)
+        for name in names:
+            arr = np.ascontiguousarray(np.asarray(tensors[name][0]))
+            f.write(memoryview(arr.reshape(-1).view(np.uint8)))
 
 
 def layer_tensors(layer_dict: dict, layer: int, prefix: str = "model.layers.{i}.mlp",

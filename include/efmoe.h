@@ -28,6 +28,8 @@
  *   ef_moe_experts_forward  per-(row, expert) SwiGLU loop                  ef_engine.py:678-695
  *   ef_slotpool_*         FrequencyWeightedCache get/put/trim              ef_engine.py:48-104
  *                         + mmap page-in of misses                        ef_engine.py:650-675
+ *   ef_store_*            expert byte ranges read out of the checkpoint     ef_deepseek_mmap.py:431-570,
+ *                         files on reader threads                          experiments/ef_v18_prefetch2.py:76-200
  */
 #ifndef EFMOE_H
 #define EFMOE_H
@@ -49,6 +51,7 @@ typedef int ef_status;
 #define EF_ERR_SLOT_MISS (-6)   /* expert not resident in the slot pool */
 #define EF_ERR_RANGE (-7)       /* activation outside the fp16 range */
 #define EF_ERR_NOT_READY (-8)   /* no CUDA device / extension not initialised */
+#define EF_ERR_IO (-9)          /* a file read failed, or read a value the format cannot carry */
 
 enum { EF_DT_BF16 = 0, EF_DT_F16 = 1, EF_DT_F32 = 2 };
 enum { EF_ROUTER_SOFTMAX = 0, EF_ROUTER_SIGMOID_GROUP = 1 };
@@ -245,6 +248,12 @@ typedef struct {
   long long tokens;          /* ef_pool_end_token calls */
   double h2d_bytes;          /* expert bytes copied host -> HBM */
   double copy_ms;            /* copy-stream time spent in those copies */
+  /* pools over an ef_expert_store (zero otherwise): */
+  long long host_hits;       /* experts found in the pinned host tier when asked for */
+  long long host_reads;      /* experts read from the files (on demand + ahead) */
+  long long host_reads_ahead;/* of those, reads started by the lookahead */
+  long long host_evictions;  /* host-tier blobs replaced */
+  double read_wait_ms;       /* host time the pool waited for file reads */
 } ef_pool_stats;
 typedef struct ef_slot_pool ef_slot_pool;
 /* cfg: the layer configuration (n_shared must be 0); host_*: n_layers entries of
@@ -276,6 +285,52 @@ ef_status ef_pool_decode_step(ef_slot_pool* pool, float* r, int T, const void* c
                               const float* const* e_bias, int lookahead, float eps, void* workspace,
                               size_t workspace_bytes, void* stream);
 ef_status ef_pool_resident(const ef_slot_pool* pool, int layer, int32_t* experts, int cap, int* n);
+
+/* ---- cold tier: expert blobs read from the model files ----------------------------- */
+/* Expert e's copy of one stacked array (w, scales or biases of gate, up or
+ * down) occupies bytes [offset + e * stride, offset + e * stride + size) of
+ * file `file`, size fixed by the layer shape (MLX safetensors store a stacked
+ * tensor [E, ...] contiguously, so stride = size).  bf16 != 0 (scales and
+ * biases only): the file holds bf16, converted to fp16 on read; a value fp16
+ * cannot hold exactly fails that read with EF_ERR_IO. */
+typedef struct {
+  int file;
+  int bf16;
+  long long offset;
+  long long stride;
+} ef_file_array;
+typedef struct ef_expert_store ef_expert_store;
+typedef struct {
+  size_t blob_bytes;   /* one expert's blob */
+  size_t offsets[10];  /* array a (3 * projection + {w, scales, biases}) starts at offsets[a]; [9] = used bytes */
+  int n_layers;
+  int n_readers;
+  int direct;          /* files opened with O_DIRECT */
+  long long reads;     /* expert blobs read so far */
+  double file_bytes;   /* bytes read so far */
+} ef_store_info;
+/* Opens n_files files (read-only; direct != 0: O_DIRECT, page cache bypassed)
+ * and starts n_readers reader threads (<= 0: min(8, cores)).  arrays:
+ * [n_layers][9] entries in the order gate w, s, b, up w, s, b, down w, s, b;
+ * every expert's range is checked against the file size here.  Host only: no
+ * CUDA call. */
+ef_status ef_store_open(const ef_moe_cfg* cfg, int n_layers, const char* const* paths, int n_files,
+                        const ef_file_array* arrays, int n_readers, int direct, ef_expert_store** out);
+ef_status ef_store_get_info(const ef_expert_store* store, ef_store_info* out);
+/* Reads n expert blobs (layer layers[i], expert experts[i]) into host buffers
+ * dst[i] of blob_bytes each, in parallel on the reader threads; returns when
+ * all are done (the first error, if any). */
+ef_status ef_store_read(ef_expert_store* store, int n, const int32_t* layers, const int32_t* experts,
+                        void* const* dst);
+ef_status ef_store_close(ef_expert_store* store);
+/* A slot pool whose host tier is host_blobs pinned expert blobs (all layers
+ * together, least recently used replaced) over `store`: a miss in HBM that
+ * is also a miss in the host tier reads the expert from the files; the
+ * lookahead starts the reads of the next layer's predicted experts, which
+ * overlap this layer's compute.  The store must outlive the pool.  host_blobs
+ * >= 2 * top_k; one step needs at most host_blobs distinct experts. */
+ef_status ef_pool_create_from_store(const ef_moe_cfg* cfg, const ef_pool_cfg* pool_cfg, ef_expert_store* store,
+                                    int host_blobs, ef_slot_pool** out);
 ef_status ef_pool_get_stats(ef_slot_pool* pool, ef_pool_stats* out);
 ef_status ef_pool_reset_stats(ef_slot_pool* pool);
 ef_status ef_pool_destroy(ef_slot_pool* pool);
