@@ -499,6 +499,52 @@ def stream_from_files(spec, host, gates, run, steps, budget, ms_res, args):
         shutil.rmtree(root, ignore_errors=True)
 
 
+def section_kquant(args, dev, peaks):
+    """GGUF K-quant decode GEMV (ef_kquant_matmul) on a stack of 32
+    DeepSeek-V3 gate projections (N = 32 x 2048 rows, K = 7168) per format:
+    weights larger than L2, CUDA events around each launch.  Algorithmic bytes
+    per launch = the blocks (N x K/256 x block bytes) + x + y."""
+    import numpy as np
+    import torch
+    from expertflow_b200 import gguf as G, kquant as KQ
+
+    N, K = 32 * 2048, 7168
+    out = {"workload": "deepseek-v3 gate_proj x32 stacked, GGUF K-quant rows", "N": N, "K": K, "bound": "hbm",
+           "points": []}
+    for dtype, name in ((G.GGML_TYPE_Q2_K, "Q2_K"), (G.GGML_TYPE_Q3_K, "Q3_K"), (G.GGML_TYPE_Q4_K, "Q4_K")):
+        bb = G.GGML_BLOCK_SIZES[dtype][1]
+        nbytes = N * (K // 256) * bb
+        w = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device=dev)
+        # fp16 super-block scales of the usual magnitude at the format's offsets
+        wb = w.view(-1, bb)
+        d = (torch.randn(wb.shape[0], device=dev).abs() * 0.01).to(torch.float16).view(torch.uint8).view(-1, 2)
+        offs = {G.GGML_TYPE_Q2_K: (80, 82), G.GGML_TYPE_Q3_K: (108,), G.GGML_TYPE_Q4_K: (0, 2)}[dtype]
+        for o in offs:
+            wb[:, o:o + 2] = d
+        for T in (1, 8, 32):
+            x = torch.randn((T, K), device=dev).to(torch.bfloat16)
+            for _ in range(max(3, args.warmup)):
+                KQ.matmul(x, w, dtype, N, K)
+            torch.cuda.synchronize()
+            reps = max(10, args.steps)
+            st = torch.cuda.current_stream()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+            for a, b in evs:
+                a.record(st)
+                KQ.matmul(x, w, dtype, N, K)
+                b.record(st)
+            torch.cuda.synchronize()
+            ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+            alg = nbytes + T * K * 2 + T * N * 4
+            gbs = alg / (ms * 1e-3) / 1e9
+            out["points"].append({"format": name, "tokens": T, "us_per_launch": round(ms * 1e3, 2),
+                                  "weight_bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm"], 4),
+                                  "bits_per_weight": round(8 * bb / 256, 3)})
+        del w, wb
+        torch.cuda.empty_cache()
+    return out
+
+
 def bench_ours(args):
     import torch
     from expertflow_b200 import build, moe, synthetic, _lib
@@ -639,6 +685,9 @@ def bench_ours(args):
         sections["c4"] = section_prefill("deepseek-v3-moe-8bit", WORKLOADS["deepseek-v3-moe-8bit"], 4096, args, pg,
                                          dev, rank, ws, peaks)
         torch.cuda.empty_cache()
+    if "kq" in want and ws == 1:
+        sections["kq"] = section_kquant(args, dev, peaks)
+        torch.cuda.empty_cache()
     if "c3" in want and ws == 1:
         sections["c3"] = section_stream("qwen3-30b-a3b-moe x48 streamed", WORKLOADS["qwen3-30b-a3b-moe"], args, dev)
         torch.cuda.empty_cache()
@@ -692,9 +741,10 @@ def main():
     ap.add_argument("--sweep", type=int, nargs="*", default=[1, 8, 32, 64])
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--sections", nargs="*", default=["c2", "c4", "c3"],
+    ap.add_argument("--sections", nargs="*", default=["c2", "c4", "c3", "kq"],
                     help="other workloads measured after the headline: c2 (DeepSeek-V3 decode), "
-                         "c4 (DeepSeek-V3 8-bit prefill), c3 (48-layer streamed decode)")
+                         "c4 (DeepSeek-V3 8-bit prefill), c3 (48-layer streamed decode), "
+                         "kq (GGUF K-quant decode GEMV)")
     ap.add_argument("--stream-layers", type=int, default=48)
     ap.add_argument("--stream-steps", type=int, default=512)
     ap.add_argument("--stream-files", default="direct", choices=["direct", "buffered", "off"],

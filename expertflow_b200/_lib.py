@@ -143,6 +143,9 @@ SIGNATURES = {
     "ef_pool_get_stats": (_I, [_P, ctypes.POINTER(PoolStats)]),
     "ef_pool_reset_stats": (_I, [_P]),
     "ef_pool_destroy": (_I, [_P]),
+    "ef_kquant_dequantize": (_I, [_I, _P, ctypes.c_longlong, _P, _P]),
+    "ef_kquant_matmul_workspace_size": (_SZ, [_I, _I]),
+    "ef_kquant_matmul": (_I, [_P, _I, _I, _P, _I, _I, _I, _P, _P, _SZ, _P]),
     "ef_store_open": (_I, [_CFGP, _I, _P, _I, ctypes.POINTER(FileArray), _I, _I, _P]),
     "ef_store_get_info": (_I, [_P, ctypes.POINTER(StoreInfo)]),
     "ef_store_read": (_I, [_P, _I, _P, _P, _P]),

@@ -1,0 +1,469 @@
+// ef_kquant.cu -- GGUF K-quant blocks (Q2_K, Q3_K, Q4_K): decode to fp16 and
+// the decode GEMV y = x . W^T over rows stored as such blocks.
+//
+// Formats, as the reference's decoders read them (256 elements per block;
+// value = RN16(d*sc*q - dmin*mn) with the products exact in fp32):
+//   Q2_K  84 B: scales[16] @0 (sc = lo nibble, mn = hi nibble of group i/16),
+//               qs[64] @16 (element i: bits 2(i%4) of byte i/4), d @80, dmin @82
+//               (ef_deepseek_mmap.py:330-378)
+//   Q3_K 110 B: hmask[32] @0, qs[64] @32, scales[12] @96, d @108; element
+//               i = 128h + 32s + b: q = ((qs[32h+b] >> 2s) & 3) - 4 (hmask bit
+//               4h+s of byte b clear); 6-bit group scale (low nibble of byte
+//               g%8, >> 4 for g >= 8; high 2 bits from byte 8 + g%4, shifted
+//               2(g/4)) minus 32 (ef_deepseek_mmap.py:717-773)
+//   Q4_K 144 B: d @0, dmin @2, scales[12] @4, qs[128] @16; elements 0..127 the
+//               low nibbles, 128..255 the high nibbles; sub-block j = i/32:
+//               sc = s[j] & 63, mn = s[8+j] & 63 (j < 4) or
+//               (s[j-4] >> 6) | ((s[j+4] >> 2) & 0x30) (ef_deepseek_mmap.py:655-714)
+// Every product d*sc*q and dmin*mn fits in fp32's 24-bit significand, so one
+// fused multiply-add gives exactly the reference's RN32(d*sc*q - dmin*mn); the
+// fp16 conversion rounds to nearest-even as numpy's astype does.
+//
+// GEMV (decode): mma.sync m16n8k16 with fp32 accumulation.  A warp owns 16
+// rows; lane (g = lane/4, c = lane%4) decodes rows g and g+8 straight into its
+// A fragments.  Within each 256-element block the reduction index is permuted
+// so that lane c's 64 elements of a row sit in whole code words of the block
+// (the order depends on the format); the activations are permuted the same
+// way by kquant_prep_kernel, so every MMA pairs matching weights and inputs.
+// Permuted activations: xp[token][256 kb + 8 (4 q + c) + r] holds
+// x[token][256 kb + elem(c, 2q + r/4, r%4)], so lane c reads 16 bytes per two
+// MMAs.  Warps of a CTA share one 16-row tile when the matrix is too small to
+// fill the GPU (split over the blocks of K, reduced through shared memory in
+// a fixed order, so results do not depend on timing).
+
+namespace ef {
+
+constexpr int kKqQ2 = 10, kKqQ3 = 11, kKqQ4 = 12;
+constexpr int kKqWarps = 8;  // warps per GEMV CTA
+
+__host__ __device__ constexpr int kq_block_bytes(int type) {
+  return type == kKqQ2 ? 84 : type == kKqQ3 ? 110 : 144;
+}
+
+// Element (0..255) of a block that lane c's slot t (0..3) of MMA j (0..15) carries.
+__host__ __device__ inline int kq_elem(int type, int c, int j, int t) {
+  if (type == kKqQ2) return 64 * c + 4 * j + t;
+  if (type == kKqQ3) {
+    const int h = j >> 3, s = (j >> 1) & 3, u = j & 1;
+    return 128 * h + 32 * s + 8 * c + 4 * u + t;
+  }
+  const int w = j >> 1, v = j & 1;
+  return (t >= 2 ? 128 : 0) + 32 * c + 4 * w + 2 * v + (t & 1);
+}
+
+EF_DEV float kq_f16(const uint8_t* p) {  // fp16 field (2-byte aligned)
+  return __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(p)));
+}
+EF_DEV float code_f32(uint32_t q) {  // exact float of a small unsigned code
+  return __uint_as_float(0x4B000000u | q) - 8388608.0f;
+}
+// 32-bit word at a 2-byte aligned address (two aligned loads + funnel shift).
+EF_DEV uint32_t ld_u32_a2(const uint8_t* p) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  if ((a & 3) == 0) return __ldg(w);
+  return __funnelshift_r(__ldg(w), __ldg(w + 1), 16);
+}
+EF_DEV uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// One row's data for lane c of one block, and its per-MMA fp16 pairs.
+template <int TYPE>
+struct KqRow;
+
+template <>
+struct KqRow<kKqQ2> {
+  uint32_t qw[4];  // qs bytes 16c .. 16c+15 (groups 4c .. 4c+3)
+  uint32_t sc;     // scale bytes 4c .. 4c+3
+  uint32_t dd;     // d | dmin << 16
+  EF_DEV void load(const uint8_t* blk, int c) {
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(blk + 16 + 16 * c);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qw[i] = __ldg(q + i);
+    sc = __ldg(reinterpret_cast<const uint32_t*>(blk + 4 * c));
+    dd = __ldg(reinterpret_cast<const uint32_t*>(blk + 80));
+  }
+  // pairs (t0, t1) and (t2, t3) of MMA j = 4 w + jb
+  template <int W>
+  EF_DEV void frags(int, uint32_t (&lo)[4], uint32_t (&hi)[4]) const {
+    const float d = __half2float(__ushort_as_half((uint16_t)dd));
+    const float m = __half2float(__ushort_as_half((uint16_t)(dd >> 16)));
+    const uint32_t s = (sc >> (8 * W)) & 0xffu;
+    const float A = d * (float)(s & 15u), B = m * (float)(s >> 4);
+#pragma unroll
+    for (int jb = 0; jb < 4; ++jb) {
+      const uint32_t b = qw[W] >> (8 * jb);
+      float v[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) v[t] = fmaf(A, code_f32((b >> (2 * t)) & 3u), -B);
+      lo[jb] = pack_h2(v[0], v[1]);
+      hi[jb] = pack_h2(v[2], v[3]);
+    }
+  }
+};
+
+template <>
+struct KqRow<kKqQ3> {
+  uint32_t qw[4];  // [2h + u]: qs bytes 32h + 8c + 4u .. +3
+  uint32_t hw[2];  // [u]: hmask bytes 8c + 4u .. +3
+  float A[8];      // [2h + s/... ] scale of group 8h + 2s + c/2, times d: index 4h + s
+  EF_DEV void load(const uint8_t* blk, int c) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) qw[2 * h + u] = ld_u32_a2(blk + 32 + 32 * h + 8 * c + 4 * u);
+    hw[0] = ld_u32_a2(blk + 8 * c);
+    hw[1] = ld_u32_a2(blk + 8 * c + 4);
+    const uint32_t s0 = ld_u32_a2(blk + 96), s1 = ld_u32_a2(blk + 100), s2 = ld_u32_a2(blk + 104);
+    const float d = kq_f16(blk + 108);
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const int g = 8 * h + 2 * s + (c >> 1);
+        const int lb = g & 7;
+        const uint32_t lw = lb < 4 ? s0 : s1;
+        const uint32_t lo = ((lw >> (8 * (lb & 3))) >> (g >= 8 ? 4 : 0)) & 15u;
+        const uint32_t hi = ((s2 >> (8 * (g & 3))) >> (2 * (g >> 2))) & 3u;
+        A[4 * h + s] = d * ((float)(lo | (hi << 4)) - 32.0f);
+      }
+  }
+  template <int QQ>
+  EF_DEV void frags(int, uint32_t (&lo)[4], uint32_t (&hi)[4]) const {  // MMAs j = 4QQ .. 4QQ+3
+    constexpr int H = QQ >> 1;
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4) {
+      const int jj = 4 * (QQ & 1) + j4;
+      const int s = jj >> 1, u = jj & 1;
+      const float a = A[4 * H + s];
+      const uint32_t q = qw[2 * H + u] >> (2 * s), hb = hw[u] >> (4 * H + s);
+      float v[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const uint32_t u3 = ((q >> (8 * t)) & 3u) | (((hb >> (8 * t)) & 1u) << 2);
+        v[t] = fmaf(a, code_f32(u3), -4.0f * a);
+      }
+      lo[j4] = pack_h2(v[0], v[1]);
+      hi[j4] = pack_h2(v[2], v[3]);
+    }
+  }
+};
+
+template <>
+struct KqRow<kKqQ4> {
+  uint4 q0, q1;    // qs bytes 32c .. 32c+31
+  uint32_t s[3];   // scales[12]
+  uint32_t dd;     // d | dmin << 16
+  EF_DEV void load(const uint8_t* blk, int c) {
+    const uint4* q = reinterpret_cast<const uint4*>(blk + 16 + 32 * c);
+    q0 = __ldg(q);
+    q1 = __ldg(q + 1);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(blk);
+    dd = __ldg(w);
+    s[0] = __ldg(w + 1);
+    s[1] = __ldg(w + 2);
+    s[2] = __ldg(w + 3);
+  }
+  EF_DEV void scales(int c, float& Alo, float& Blo, float& Ahi, float& Bhi) const {
+    const float d = __half2float(__ushort_as_half((uint16_t)dd));
+    const float m = __half2float(__ushort_as_half((uint16_t)(dd >> 16)));
+    const uint32_t sc_lo = (s[0] >> (8 * c)) & 0xffu;  // byte c
+    const uint32_t sc_hi = (s[1] >> (8 * c)) & 0xffu;  // byte 4 + c
+    const uint32_t mn_b = (s[2] >> (8 * c)) & 0xffu;   // byte 8 + c
+    Alo = d * (float)(sc_lo & 63u);
+    Blo = m * (float)(mn_b & 63u);
+    Ahi = d * (float)(sc_hi & 63u);
+    Bhi = m * (float)((sc_lo >> 6) | ((mn_b >> 2) & 0x30u));
+  }
+  // MMAs j = 4QQ .. 4QQ+3 (j = 2w + v: word w of the lane's 32 bytes, bytes 2v, 2v+1)
+  template <int QQ>
+  EF_DEV void frags(int c, uint32_t (&lo)[4], uint32_t (&hi)[4]) const {
+    float Alo, Blo, Ahi, Bhi;
+    scales(c, Alo, Blo, Ahi, Bhi);
+    const uint4 qq = QQ < 2 ? q0 : q1;
+    const uint32_t ws[2] = {(QQ & 1) ? qq.z : qq.x, (QQ & 1) ? qq.w : qq.y};
+#pragma unroll
+    for (int w = 0; w < 2; ++w)
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        const uint32_t b = ws[w] >> (16 * v);
+        lo[2 * w + v] = pack_h2(fmaf(Alo, code_f32(b & 15u), -Blo), fmaf(Alo, code_f32((b >> 8) & 15u), -Blo));
+        hi[2 * w + v] = pack_h2(fmaf(Ahi, code_f32((b >> 4) & 15u), -Bhi), fmaf(Ahi, code_f32((b >> 12) & 15u), -Bhi));
+      }
+  }
+};
+
+// Permute and convert the activations: xp fp16 [n_tok8][K] (tokens >= T zero).
+template <int TYPE>
+__global__ void kquant_prep_kernel(const uint16_t* __restrict__ x, int act_bf16, int T, int K, int n_tok8,
+                                   uint16_t* __restrict__ xp) {
+  const long long total = (long long)n_tok8 * K;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int tok = (int)(i / K), kk = (int)(i % K);
+    const int kb = kk >> 8, p = kk & 255;
+    const int q = p >> 5, c = (p >> 3) & 3, r = p & 7;
+    const int src = 256 * kb + kq_elem(TYPE, c, 2 * q + (r >> 2), r & 3);
+    uint16_t out = 0;
+    if (tok < T) {
+      const float v = act_to_f32(x[(size_t)tok * K + src], act_bf16);
+      if (!(fabsf(v) <= 65504.0f)) ef_set_error(kDevErrRange);
+      out = __half_as_ushort(__float2half_rn(v));
+    }
+    xp[i] = out;
+  }
+}
+
+// One lane's contribution of one block for one 16-row tile: per quarter of
+// the block, decode 4 MMAs' fragments of both rows, then run them for every
+// token group.
+template <int TYPE, int NT, int QQ>
+EF_DEV void kq_quarter_mma(const KqRow<TYPE>& r0, const KqRow<TYPE>& r1, int c, const uint16_t* __restrict__ xrow,
+                           size_t tok_stride, float (&acc)[NT][4]) {
+  uint32_t a0l[4], a0h[4], a1l[4], a1h[4];
+  r0.template frags<QQ>(c, a0l, a0h);
+  r1.template frags<QQ>(c, a1l, a1h);
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const uint16_t* xr = xrow + (size_t)n * 8 * tok_stride + 64 * QQ;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 b = __ldg(reinterpret_cast<const uint4*>(xr + 32 * h));
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        const int j = 2 * h + v;
+        const uint32_t a[4] = {a0l[j], a1l[j], a0h[j], a1h[j]};
+        mma_16816(acc[n], a, v ? b.z : b.x, v ? b.w : b.y);
+      }
+    }
+  }
+}
+
+template <int TYPE, int NT>
+EF_DEV void kq_block_mma(const KqRow<TYPE>& r0, const KqRow<TYPE>& r1, int c, const uint16_t* __restrict__ xrow,
+                         size_t tok_stride, float (&acc)[NT][4]) {
+  // xrow: this lane's token (g) of token group 0, at 256 kb + 8 c
+  kq_quarter_mma<TYPE, NT, 0>(r0, r1, c, xrow, tok_stride, acc);
+  kq_quarter_mma<TYPE, NT, 1>(r0, r1, c, xrow, tok_stride, acc);
+  kq_quarter_mma<TYPE, NT, 2>(r0, r1, c, xrow, tok_stride, acc);
+  kq_quarter_mma<TYPE, NT, 3>(r0, r1, c, xrow, tok_stride, acc);
+}
+
+// y [T, N] fp32.  Grid: ceil(n_tiles / tiles_per_cta) CTAs of kKqWarps warps;
+// `split` warps share a tile (each a contiguous range of blocks).
+template <int TYPE, int NT>
+__global__ void __launch_bounds__(kKqWarps * 32, (NT == 1 && TYPE != kKqQ3) ? 3 : 2) kquant_gemv_kernel(const uint8_t* __restrict__ w,
+                                                                   const uint16_t* __restrict__ xp, int T, int N,
+                                                                   int K, int split, float* __restrict__ y) {
+  constexpr int BB = kq_block_bytes(TYPE);
+  __shared__ float red[kKqWarps][32][NT * 4];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int tiles_per_cta = kKqWarps / split;
+  const int tile = blockIdx.x * tiles_per_cta + warp / split;
+  const int part = warp % split;
+  const int nb = K >> 8;
+  const int n_tiles = N >> 4;
+  float acc[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+  if (tile < n_tiles) {
+    const int kb0 = (int)((long long)nb * part / split), kb1 = (int)((long long)nb * (part + 1) / split);
+    const size_t row_bytes = (size_t)nb * BB;
+    const uint8_t* row0 = w + (size_t)(16 * tile + g) * row_bytes;
+    const uint8_t* row1 = row0 + 8 * row_bytes;
+    const size_t tok_stride = (size_t)K;
+    const uint16_t* xl = xp + (size_t)g * tok_stride + 8 * c;
+    if (kb0 < kb1) {
+      KqRow<TYPE> cur0, cur1, nxt0, nxt1;
+      cur0.load(row0 + (size_t)kb0 * BB, c);
+      cur1.load(row1 + (size_t)kb0 * BB, c);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (kb + 1 < kb1) {
+          nxt0.load(row0 + (size_t)(kb + 1) * BB, c);
+          nxt1.load(row1 + (size_t)(kb + 1) * BB, c);
+        }
+        kq_block_mma<TYPE, NT>(cur0, cur1, c, xl + (size_t)kb * 256, tok_stride, acc);
+        cur0 = nxt0;
+        cur1 = nxt1;
+      }
+    }
+  }
+  if (split > 1) {
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) red[warp][lane][4 * n + i] = acc[n][i];
+    __syncthreads();
+    if (part != 0) return;
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float sum = 0.0f;
+        for (int p = 0; p < split; ++p) sum += red[warp + p][lane][4 * n + i];
+        acc[n][i] = sum;
+      }
+  }
+  if (tile >= n_tiles) return;
+  // accumulator (row g / g+8, tokens 2c, 2c+1 of each group of 8)
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int tok = 8 * n + 2 * c + (i & 1);
+      const int row = 16 * tile + g + ((i & 2) ? 8 : 0);
+      if (tok < T) y[(size_t)tok * N + row] = acc[n][i];
+    }
+}
+
+// fp16 out[n_blocks * 256]: the reference's decode, one thread per 16 elements.
+template <int TYPE>
+__global__ void kquant_dequant_kernel(const uint8_t* __restrict__ blocks, long long n_blocks,
+                                      uint16_t* __restrict__ out) {
+  constexpr int BB = kq_block_bytes(TYPE);
+  const long long n16 = n_blocks * 16;
+  for (long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x; u < n16;
+       u += (long long)gridDim.x * blockDim.x) {
+    const uint8_t* b = blocks + (u >> 4) * BB;
+    const int e0 = (int)(u & 15) * 16;  // elements e0 .. e0+15 of the block
+    float v[16];
+    if (TYPE == kKqQ2) {
+      const int grp = e0 >> 4;
+      const float A = kq_f16(b + 80) * (float)(b[grp] & 15), B = kq_f16(b + 82) * (float)(b[grp] >> 4);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = fmaf(A, (float)((b[16 + ((e0 + i) >> 2)] >> (2 * ((e0 + i) & 3))) & 3), -B);
+    } else if (TYPE == kKqQ3) {
+      const int grp = e0 >> 4;
+      const uint32_t lo = (grp < 8 ? b[96 + grp] : (b[96 + grp - 8] >> 4)) & 15u;
+      const uint32_t hi = (b[104 + (grp & 3)] >> (2 * (grp >> 2))) & 3u;
+      const float A = kq_f16(b + 108) * ((float)(lo | (hi << 4)) - 32.0f);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int e = e0 + i, h = e >> 7, s = (e >> 5) & 3, bb = e & 31;
+        const int q = (int)((b[32 + 32 * h + bb] >> (2 * s)) & 3) - (((b[bb] >> (4 * h + s)) & 1) ? 0 : 4);
+        v[i] = fmaf(A, (float)q, -0.0f);
+      }
+    } else {
+      const int e = e0 & 127, j = (e0 >> 7) * 4 + (e >> 5);  // sub-block of these 16 elements
+      const uint8_t* s = b + 4;
+      const uint32_t sc = s[j] & 63u;
+      const uint32_t mn = j < 4 ? (s[8 + j] & 63u) : (uint32_t)((s[j - 4] >> 6) | ((s[j + 4] >> 2) & 0x30));
+      const float A = kq_f16(b) * (float)sc, B = kq_f16(b + 2) * (float)mn;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = fmaf(A, (float)((b[16 + e + i] >> (e0 >= 128 ? 4 : 0)) & 15), -B);
+    }
+    uint4 o[2];
+    uint32_t* ow = reinterpret_cast<uint32_t*>(o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ow[i] = pack_h2(v[2 * i], v[2 * i + 1]);
+    uint4* dst = reinterpret_cast<uint4*>(out + u * 16);
+    dst[0] = o[0];
+    dst[1] = o[1];
+  }
+}
+
+template <int TYPE>
+cudaError_t launch_kquant_gemv_t(const uint8_t* w, const uint16_t* xp, int T, int N, int K, int split, float* y,
+                                 int n_sm, cudaStream_t st) {
+  const int n_tiles = N >> 4, tiles_per_cta = kKqWarps / split;
+  const int grid = (n_tiles + tiles_per_cta - 1) / tiles_per_cta;
+  const int nt = (T + 7) / 8;
+  (void)n_sm;
+  if (nt == 1) kquant_gemv_kernel<TYPE, 1><<<grid, kKqWarps * 32, 0, st>>>(w, xp, T, N, K, split, y);
+  else if (nt == 2) kquant_gemv_kernel<TYPE, 2><<<grid, kKqWarps * 32, 0, st>>>(w, xp, T, N, K, split, y);
+  else kquant_gemv_kernel<TYPE, 4><<<grid, kKqWarps * 32, 0, st>>>(w, xp, T, N, K, split, y);
+  return cudaGetLastError();
+}
+
+}  // namespace ef
+
+namespace {
+
+int kq_split(int N, int K, int n_sm) {
+  // warps sharing a tile: enough warps to cover the SMs several times over
+  const int n_tiles = N >> 4, nb = K >> 8;
+  int split = 1;
+  while (split < ef::kKqWarps && (long long)n_tiles * split < 24LL * n_sm && split * 2 <= nb) split *= 2;
+  return split;
+}
+
+ef_status check_kquant(int type, int N, int K) {
+  if (type != ef::kKqQ2 && type != ef::kKqQ3 && type != ef::kKqQ4)
+    return fail(EF_ERR_UNSUPPORTED, "K-quant type must be Q2_K (10), Q3_K (11) or Q4_K (12), got %d", type);
+  if (N <= 0 || N % 16) return fail(EF_ERR_UNSUPPORTED, "N must be a positive multiple of 16 (got %d)", N);
+  if (K <= 0 || K % 256) return fail(EF_ERR_UNSUPPORTED, "K must be a positive multiple of 256 (got %d)", K);
+  return EF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+ef_status ef_kquant_dequantize(int type, const void* blocks, long long n_blocks, void* out, void* stream) {
+  if (type != ef::kKqQ2 && type != ef::kKqQ3 && type != ef::kKqQ4)
+    return fail(EF_ERR_UNSUPPORTED, "K-quant type must be Q2_K (10), Q3_K (11) or Q4_K (12), got %d", type);
+  if (n_blocks < 0) return fail(EF_ERR_INVALID, "n_blocks < 0");
+  if (n_blocks == 0) return EF_OK;
+  if (!blocks || !out) return fail(EF_ERR_INVALID, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(blocks) & 3))
+    return fail(EF_ERR_INVALID, "out must be 16-byte and blocks 4-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long n16 = n_blocks * 16;
+  const int grid = (int)std::min<long long>((n16 + 255) / 256, 148LL * 64);
+  const uint8_t* b = static_cast<const uint8_t*>(blocks);
+  uint16_t* o = static_cast<uint16_t*>(out);
+  if (type == ef::kKqQ2) ef::kquant_dequant_kernel<ef::kKqQ2><<<grid, 256, 0, st>>>(b, n_blocks, o);
+  else if (type == ef::kKqQ3) ef::kquant_dequant_kernel<ef::kKqQ3><<<grid, 256, 0, st>>>(b, n_blocks, o);
+  else ef::kquant_dequant_kernel<ef::kKqQ4><<<grid, 256, 0, st>>>(b, n_blocks, o);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(EF_ERR_CUDA, "kquant_dequant: %s", cudaGetErrorString(e));
+  return EF_OK;
+}
+
+size_t ef_kquant_matmul_workspace_size(int T, int K) {
+  if (T < 0 || K < 0) return 0;
+  const int nt = (T + 7) / 8;
+  return (size_t)(nt <= 2 ? nt : 4) * 8 * K * 2 + 256;  // token groups the kernel reads: 1, 2 or 4
+}
+
+ef_status ef_kquant_matmul(const void* x, int act_dtype, int T, const void* blocks, int type, int N, int K, float* y,
+                           void* workspace, size_t ws_bytes, void* stream) {
+  ef_status s = check_kquant(type, N, K);
+  if (s) return s;
+  if (act_dtype != EF_DT_BF16 && act_dtype != EF_DT_F16) return fail(EF_ERR_UNSUPPORTED, "act_dtype");
+  if (T < 0) return fail(EF_ERR_INVALID, "T < 0");
+  if (T == 0) return EF_OK;
+  if (T > 32) return fail(EF_ERR_UNSUPPORTED, "T must be <= 32 for the K-quant GEMV (decode)");
+  if (!x || !blocks || !y || !workspace) return fail(EF_ERR_INVALID, "null pointer");
+  const uintptr_t need_align = type == ef::kKqQ4 ? 15 : type == ef::kKqQ2 ? 3 : 3;
+  if ((reinterpret_cast<uintptr_t>(blocks) & need_align) || (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return fail(EF_ERR_INVALID, "blocks must be %d-byte aligned, workspace 16-byte aligned", (int)need_align + 1);
+  if (ws_bytes < ef_kquant_matmul_workspace_size(T, K)) return fail(EF_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nt = (T + 7) / 8;
+  const int n_tok_k = (nt <= 2 ? nt : 4) * 8;  // token rows the kernel reads (zero beyond T)
+  uint16_t* xp = static_cast<uint16_t*>(workspace);
+  int dev = 0, n_sm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+  const int pgrid = (int)std::min<long long>(((long long)n_tok_k * K + 255) / 256, (long long)n_sm * 16);
+  const uint16_t* xs = static_cast<const uint16_t*>(x);
+  const int bf = act_dtype == EF_DT_BF16;
+  if (type == ef::kKqQ2) ef::kquant_prep_kernel<ef::kKqQ2><<<pgrid, 256, 0, st>>>(xs, bf, T, K, n_tok_k, xp);
+  else if (type == ef::kKqQ3) ef::kquant_prep_kernel<ef::kKqQ3><<<pgrid, 256, 0, st>>>(xs, bf, T, K, n_tok_k, xp);
+  else ef::kquant_prep_kernel<ef::kKqQ4><<<pgrid, 256, 0, st>>>(xs, bf, T, K, n_tok_k, xp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(EF_ERR_CUDA, "kquant_prep: %s", cudaGetErrorString(e));
+  const int split = kq_split(N, K, n_sm);
+  const uint8_t* w = static_cast<const uint8_t*>(blocks);
+  if (type == ef::kKqQ2) e = ef::launch_kquant_gemv_t<ef::kKqQ2>(w, xp, T, N, K, split, y, n_sm, st);
+  else if (type == ef::kKqQ3) e = ef::launch_kquant_gemv_t<ef::kKqQ3>(w, xp, T, N, K, split, y, n_sm, st);
+  else e = ef::launch_kquant_gemv_t<ef::kKqQ4>(w, xp, T, N, K, split, y, n_sm, st);
+  if (e != cudaSuccess) return fail(EF_ERR_CUDA, "kquant_gemv: %s", cudaGetErrorString(e));
+  return EF_OK;
+}
+
+}  // extern "C"

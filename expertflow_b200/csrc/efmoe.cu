@@ -8,6 +8,7 @@
 #include "ef_qgemm2.cu"
 #include "ef_api.cu"
 #include "ef_store.cu"
+#include "ef_kquant.cu"
 #include "ef_pool.cu"
 #include "ef_ep.cu"
 #include "ef_noalloc.cu"

@@ -28,6 +28,7 @@
  *   ef_moe_experts_forward  per-(row, expert) SwiGLU loop                  ef_engine.py:678-695
  *   ef_slotpool_*         FrequencyWeightedCache get/put/trim              ef_engine.py:48-104
  *                         + mmap page-in of misses                        ef_engine.py:650-675
+ *   ef_kquant_*           GGUF Q2_K/Q3_K/Q4_K decode (+ GEMV)              ef_deepseek_mmap.py:330-378,655-773
  *   ef_store_*            expert byte ranges read out of the checkpoint     ef_deepseek_mmap.py:431-570,
  *                         files on reader threads                          experiments/ef_v18_prefetch2.py:76-200
  */
@@ -285,6 +286,26 @@ ef_status ef_pool_decode_step(ef_slot_pool* pool, float* r, int T, const void* c
                               const float* const* e_bias, int lookahead, float eps, void* workspace,
                               size_t workspace_bytes, void* stream);
 ef_status ef_pool_resident(const ef_slot_pool* pool, int layer, int32_t* experts, int cap, int* n);
+
+/* ---- GGUF K-quants ------------------------------------------------------------------ */
+/* Blocks of 256 elements as the reference decodes them (ef_deepseek_mmap.py:330-378,
+ * 655-773): Q2_K 84 B, Q3_K 110 B, Q4_K 144 B per block; value = RN16(d*sc*q - dmin*mn).
+ * The reference's Q2_K and Q4_K element orders and Q4_K scale packing are its own
+ * (they differ from ggml's); these calls follow the reference. */
+#define EF_GGML_Q2_K 10
+#define EF_GGML_Q3_K 11
+#define EF_GGML_Q4_K 12
+/* out fp16 [n_blocks * 256] (16-byte aligned) = the decode of n_blocks consecutive
+ * blocks (4-byte aligned), bit-identical to the reference's decoders. */
+ef_status ef_kquant_dequantize(int type, const void* blocks, long long n_blocks, void* out, void* stream);
+/* Decode GEMV: y fp32 [T, N] = x [T, K] . W^T, W [N, K] stored as N rows of K/256
+ * blocks (row r = blocks [r K/256, (r+1) K/256)), i.e. one GGML tensor of shape
+ * (K, N) or one expert's slice of a stacked (K, N, E) tensor.  T <= 32, N % 16 == 0,
+ * K % 256 == 0; blocks 16-byte (Q4_K) or 4-byte aligned.  Weights are decoded to the
+ * same fp16 values as ef_kquant_dequantize, products accumulated in fp32. */
+size_t ef_kquant_matmul_workspace_size(int T, int K);
+ef_status ef_kquant_matmul(const void* x, int act_dtype, int T, const void* blocks, int type, int N, int K, float* y,
+                           void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- cold tier: expert blobs read from the model files ----------------------------- */
 /* Expert e's copy of one stacked array (w, scales or biases of gate, up or

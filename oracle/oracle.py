@@ -19,6 +19,11 @@ What they restate (reference file:line, relative to the reference root):
 * ``ef_cpu_fast.py:70-125``  dequantise-then-matmul CPU path (mx.dequantize).
 * ``ef_engine_v2.py:88-91``  stacked expert layout ``[E, out, in*bits/32]``
   uint32 codes, ``[E, out, in/group]`` fp16 scales and biases.
+* ``ef_deepseek_mmap.py:330-378, 655-773``  the reference's GGUF K-quant
+  decoders (Q2_K, Q3_K, Q4_K blocks of 256 -> fp16), as ``np_dequant_kquant``;
+  pinned by ``tests/golden/kquant_gguf.npz`` (generator:
+  ``tests/golden/make_gguf_golden.py``, which runs the reference's own
+  decoders), and the GEMV over such rows as ``np_kquant_matmul``.
 
 Parity pin: the reference's routing/combine code (``streaming_moe_forward``)
 and its expert cache (``FrequencyWeightedCache``) are executed on this
@@ -407,3 +412,84 @@ def moe_forward(x_bits, x_bf16, gate_w_bits, gate_w_bf16, spec: RouterSpec, e_bi
     inds, wts = route(logits, spec, e_bias)
     y = c_moe_ffn(x_bits, x_bf16, inds, wts, gate, up, down, bits, group, shared)
     return inds, wts, y
+
+
+# ---------------------------------------------------------------- GGUF K-quants
+# Block layouts and element orders as the reference's decoders read them
+# (QK_K = 256 elements per block; value = d * sc * q - dmin * mn in fp32, then
+# rounded to fp16):
+#   Q2_K (84 B)  scales[16] @0 (lo nibble sc, hi nibble mn of group i/16),
+#                qs[64] @16 (element i: bits 2(i%4).. of byte i/4), d @80, dmin @82
+#                                                   ef_deepseek_mmap.py:330-378
+#   Q3_K (110 B) hmask[32] @0, qs[64] @32, scales[12] @96, d @108; element
+#                i = 32(4h + s) + b: q = ((qs[32h + b] >> 2s) & 3) - 4 * (1 - hmask bit
+#                (4h + s) of byte b); 6-bit scale of group i/16 (low nibble from
+#                bytes 0..7, high 2 bits from bytes 8..11) minus 32; no min
+#                                                   ef_deepseek_mmap.py:717-773
+#   Q4_K (144 B) d @0, dmin @2, scales[12] @4, qs[128] @16; elements 0..127 the
+#                low nibbles of qs, 128..255 the high nibbles; sub-block i/32 has
+#                sc = s[j] & 63 (j < 8), mn = s[8 + j] & 63 (j < 4) or
+#                (s[j - 4] >> 6) | ((s[j + 4] >> 2) & 0x30) (j >= 4)
+#                                                   ef_deepseek_mmap.py:655-714
+KQ_BLOCK_BYTES = {10: 84, 11: 110, 12: 144}
+
+
+def _f16_field(blocks: np.ndarray, off: int) -> np.ndarray:
+    return blocks[:, off:off + 2].copy().view(np.float16).reshape(-1).astype(np.float32)
+
+
+def np_kquant_codes(blocks: np.ndarray, dtype: int):
+    """(q [n, 256] fp32, A [n, 256] fp32, B [n, 256] fp32) with value = A*q - B."""
+    n = blocks.shape[0]
+    if dtype == 10:
+        sc = blocks[:, 0:16]
+        qs = blocks[:, 16:80]
+        d, dm = _f16_field(blocks, 80), _f16_field(blocks, 82)
+        q = ((qs[:, :, None] >> (2 * np.arange(4, dtype=np.uint8))[None, None, :]) & 3).reshape(n, 256)
+        A = np.repeat(d[:, None] * (sc & 15).astype(np.float32), 16, axis=1)
+        B = np.repeat(dm[:, None] * (sc >> 4).astype(np.float32), 16, axis=1)
+        return q.astype(np.float32), A, B
+    if dtype == 11:
+        hm, qs, sb = blocks[:, 0:32], blocks[:, 32:96], blocks[:, 96:108]
+        d = _f16_field(blocks, 108)
+        g = np.arange(16)
+        lo = np.where(g < 8, sb[:, g % 8] & 15, sb[:, g % 8] >> 4)
+        hi = (sb[:, 8 + g % 4] >> (2 * (g // 4)).astype(np.uint8)) & 3
+        sc = (lo | (hi << 4)).astype(np.float32) - 32.0
+        i = np.arange(256)
+        h, sh, b = i // 128, (i // 32) % 4, i % 32
+        q2 = (qs[:, 32 * h + b] >> (2 * sh).astype(np.uint8)) & 3
+        hb = (hm[:, b] >> (4 * h + sh).astype(np.uint8)) & 1
+        q = q2.astype(np.float32) - 4.0 * (1 - hb).astype(np.float32)
+        A = np.repeat(d[:, None] * sc, 16, axis=1)
+        return q, A, np.zeros_like(A)
+    if dtype == 12:
+        d, dm = _f16_field(blocks, 0), _f16_field(blocks, 2)
+        s = blocks[:, 4:16]
+        j = np.arange(8)
+        sc = (s[:, j] & 63).astype(np.float32)
+        mn = np.where(j < 4, s[:, 8 + j % 4] & 63, (s[:, j % 4] >> 6) | ((s[:, 8 + j % 4] >> 2) & 0x30))
+        qs = blocks[:, 16:144]
+        q = np.concatenate([qs & 15, qs >> 4], axis=1).astype(np.float32)
+        A = np.repeat(d[:, None] * sc, 32, axis=1)
+        B = np.repeat(dm[:, None] * mn.astype(np.float32), 32, axis=1)
+        return q, A, B
+    raise ValueError(f"not a K-quant type: {dtype}")
+
+
+def np_dequant_kquant(raw, dtype: int) -> np.ndarray:
+    """fp16 [n_blocks * 256] of raw K-quant blocks, as the reference decodes them."""
+    bb = KQ_BLOCK_BYTES[dtype]
+    blocks = np.frombuffer(bytes(raw), np.uint8)
+    blocks = blocks[:len(blocks) // bb * bb].reshape(-1, bb)
+    q, A, B = np_kquant_codes(blocks, dtype)
+    with np.errstate(over="ignore", invalid="ignore"):
+        v = (A * q - B).astype(np.float32)  # A*q is exact in fp32; one rounding at the subtraction
+        return v.astype(np.float16).reshape(-1)
+
+
+def np_kquant_matmul(x: np.ndarray, raw, dtype: int, N: int, K: int) -> np.ndarray:
+    """y [T, N] fp64 = x [T, K] . W^T, W [N, K] the fp16 rows decoded from
+    N * K / 256 K-quant blocks (row r = blocks [r K/256, (r+1) K/256))."""
+    w = np_dequant_kquant(raw, dtype).astype(np.float64).reshape(N, K)
+    return np.asarray(x, np.float64) @ w.T
