@@ -42,7 +42,7 @@ __host__ __device__ constexpr int kq_block_bytes(int type) {
 
 // Element (0..255) of a block that lane c's slot t (0..3) of MMA j (0..15) carries.
 __host__ __device__ inline int kq_elem(int type, int c, int j, int t) {
-  if (type == kKqQ2) return 64 * c + 4 * j + t;
+  if (type == kKqQ2) return 64 * c + 16 * (j >> 2) + (j & 3) + 4 * t;
   if (type == kKqQ3) {
     const int h = j >> 3, s = (j >> 1) & 3, u = j & 1;
     return 128 * h + 32 * s + 8 * c + 4 * u + t;
@@ -75,7 +75,7 @@ struct KqRow;
 
 template <>
 struct KqRow<kKqQ2> {
-  uint32_t qw[4];  // qs bytes 16c .. 16c+15 (groups 4c .. 4c+3)
+  uint32_t qw[4];  // qs bytes 16c .. 16c+15: word w is group 4c + w (element 16w' + e at bits 2e)
   uint32_t sc;     // scale bytes 4c .. 4c+3
   uint32_t dd;     // d | dmin << 16
   EF_DEV void load(const uint8_t* blk, int c) {
@@ -85,21 +85,25 @@ struct KqRow<kKqQ2> {
     sc = __ldg(reinterpret_cast<const uint32_t*>(blk + 4 * c));
     dd = __ldg(reinterpret_cast<const uint32_t*>(blk + 80));
   }
-  // pairs (t0, t1) and (t2, t3) of MMA j = 4 w + jb
+  EF_DEV void prep(int) {}
+  // A group takes only four values, RN16(A q - B) for q = 0..3 (exactly the
+  // reference's rounding); they sit as halves 0..3 of (L01, L23) and each
+  // pair of codes selects its two halves with one byte permute.  MMA
+  // j = 4W + m carries the group's elements m, m+4 (t0, t1) and m+8, m+12 (t2, t3).
   template <int W>
   EF_DEV void frags(int, uint32_t (&lo)[4], uint32_t (&hi)[4]) const {
     const float d = __half2float(__ushort_as_half((uint16_t)dd));
     const float m = __half2float(__ushort_as_half((uint16_t)(dd >> 16)));
     const uint32_t s = (sc >> (8 * W)) & 0xffu;
     const float A = d * (float)(s & 15u), B = m * (float)(s >> 4);
+    const uint32_t L01 = pack_h2(fmaf(A, 0.0f, -B), fmaf(A, 1.0f, -B));
+    const uint32_t L23 = pack_h2(fmaf(A, 2.0f, -B), fmaf(A, 3.0f, -B));
 #pragma unroll
-    for (int jb = 0; jb < 4; ++jb) {
-      const uint32_t b = qw[W] >> (8 * jb);
-      float v[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) v[t] = fmaf(A, code_f32((b >> (2 * t)) & 3u), -B);
-      lo[jb] = pack_h2(v[0], v[1]);
-      hi[jb] = pack_h2(v[2], v[3]);
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t r4 = (qw[W] >> (2 * e)) & 0x03030303u;  // codes of elements e, e+4, e+8, e+12
+      const uint32_t S = r4 * 0x22u + 0x10101010u;           // byte pair (2q, 2q+1) per code
+      lo[e] = prmt(L01, L23, S);
+      hi[e] = prmt(L01, L23, S >> 16);
     }
   }
 };
@@ -130,6 +134,7 @@ struct KqRow<kKqQ3> {
         A[4 * h + s] = d * ((float)(lo | (hi << 4)) - 32.0f);
       }
   }
+  EF_DEV void prep(int) {}
   template <int QQ>
   EF_DEV void frags(int, uint32_t (&lo)[4], uint32_t (&hi)[4]) const {  // MMAs j = 4QQ .. 4QQ+3
     constexpr int H = QQ >> 1;
@@ -156,6 +161,9 @@ struct KqRow<kKqQ4> {
   uint4 q0, q1;    // qs bytes 32c .. 32c+31
   uint32_t s[3];   // scales[12]
   uint32_t dd;     // d | dmin << 16
+  // after prep(): A of the low (sub-block c) and high (4 + c) nibbles times
+  // 2^-p for the bit position p each code is read at, and the two mins
+  float al[4], ah[4], bl, bh;
   EF_DEV void load(const uint8_t* blk, int c) {
     const uint4* q = reinterpret_cast<const uint4*>(blk + 16 + 32 * c);
     q0 = __ldg(q);
@@ -166,32 +174,42 @@ struct KqRow<kKqQ4> {
     s[1] = __ldg(w + 2);
     s[2] = __ldg(w + 3);
   }
-  EF_DEV void scales(int c, float& Alo, float& Blo, float& Ahi, float& Bhi) const {
+  EF_DEV void prep(int c) {
     const float d = __half2float(__ushort_as_half((uint16_t)dd));
     const float m = __half2float(__ushort_as_half((uint16_t)(dd >> 16)));
     const uint32_t sc_lo = (s[0] >> (8 * c)) & 0xffu;  // byte c
     const uint32_t sc_hi = (s[1] >> (8 * c)) & 0xffu;  // byte 4 + c
     const uint32_t mn_b = (s[2] >> (8 * c)) & 0xffu;   // byte 8 + c
-    Alo = d * (float)(sc_lo & 63u);
-    Blo = m * (float)(mn_b & 63u);
-    Ahi = d * (float)(sc_hi & 63u);
-    Bhi = m * (float)((sc_lo >> 6) | ((mn_b >> 2) & 0x30u));
+    const float Alo = d * (float)(sc_lo & 63u), Ahi = d * (float)(sc_hi & 63u);
+    bl = m * (float)(mn_b & 63u);
+    bh = m * (float)((sc_lo >> 6) | ((mn_b >> 2) & 0x30u));
+    // positions: low nibbles at 0, 8, 16 (word) and 12 (word >> 12);
+    //            high nibbles at 4, 12 (word) and 8, 16 (word >> 12)
+    al[0] = Alo;
+    al[1] = Alo * 0x1p-8f;
+    al[2] = Alo * 0x1p-16f;
+    al[3] = Alo * 0x1p-12f;
+    ah[0] = Ahi * 0x1p-4f;
+    ah[1] = Ahi * 0x1p-12f;
+    ah[2] = Ahi * 0x1p-8f;
+    ah[3] = Ahi * 0x1p-16f;
   }
-  // MMAs j = 4QQ .. 4QQ+3 (j = 2w + v: word w of the lane's 32 bytes, bytes 2v, 2v+1)
+  // MMAs j = 4QQ .. 4QQ+3 (j = 2w + v: word w of the lane's 32 bytes, bytes
+  // 2v, 2v+1; t0, t1 their low nibbles, t2, t3 their high nibbles).  A code
+  // at bit position p is read as the float q 2^p (its bits OR'ed into the
+  // mantissa of 2^23, minus 2^23) and scaled by A 2^-p: the same exact A q.
   template <int QQ>
-  EF_DEV void frags(int c, uint32_t (&lo)[4], uint32_t (&hi)[4]) const {
-    float Alo, Blo, Ahi, Bhi;
-    scales(c, Alo, Blo, Ahi, Bhi);
+  EF_DEV void frags(int, uint32_t (&lo)[4], uint32_t (&hi)[4]) const {
     const uint4 qq = QQ < 2 ? q0 : q1;
     const uint32_t ws[2] = {(QQ & 1) ? qq.z : qq.x, (QQ & 1) ? qq.w : qq.y};
 #pragma unroll
-    for (int w = 0; w < 2; ++w)
-#pragma unroll
-      for (int v = 0; v < 2; ++v) {
-        const uint32_t b = ws[w] >> (16 * v);
-        lo[2 * w + v] = pack_h2(fmaf(Alo, code_f32(b & 15u), -Blo), fmaf(Alo, code_f32((b >> 8) & 15u), -Blo));
-        hi[2 * w + v] = pack_h2(fmaf(Ahi, code_f32((b >> 4) & 15u), -Bhi), fmaf(Ahi, code_f32((b >> 12) & 15u), -Bhi));
-      }
+    for (int w = 0; w < 2; ++w) {
+      const uint32_t W = ws[w], Wh = W >> 12;
+      lo[2 * w] = pack_h2(fmaf(al[0], code_f32(W & 0xFu), -bl), fmaf(al[1], code_f32(W & 0xF00u), -bl));
+      hi[2 * w] = pack_h2(fmaf(ah[0], code_f32(W & 0xF0u), -bh), fmaf(ah[1], code_f32(W & 0xF000u), -bh));
+      lo[2 * w + 1] = pack_h2(fmaf(al[2], code_f32(W & 0xF0000u), -bl), fmaf(al[3], code_f32(Wh & 0xF000u), -bl));
+      hi[2 * w + 1] = pack_h2(fmaf(ah[2], code_f32(Wh & 0xF00u), -bh), fmaf(ah[3], code_f32(Wh & 0xF0000u), -bh));
+    }
   }
 };
 
@@ -221,13 +239,13 @@ __global__ void kquant_prep_kernel(const uint16_t* __restrict__ x, int act_bf16,
 // token group.
 template <int TYPE, int NT, int QQ>
 EF_DEV void kq_quarter_mma(const KqRow<TYPE>& r0, const KqRow<TYPE>& r1, int c, const uint16_t* __restrict__ xrow,
-                           size_t tok_stride, float (&acc)[NT][4]) {
+                           const size_t (&tok_off)[NT], float (&acc)[NT][4]) {
   uint32_t a0l[4], a0h[4], a1l[4], a1h[4];
   r0.template frags<QQ>(c, a0l, a0h);
   r1.template frags<QQ>(c, a1l, a1h);
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
-    const uint16_t* xr = xrow + (size_t)n * 8 * tok_stride + 64 * QQ;
+    const uint16_t* xr = xrow + tok_off[n] + 64 * QQ;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint4 b = __ldg(reinterpret_cast<const uint4*>(xr + 32 * h));
@@ -242,19 +260,25 @@ EF_DEV void kq_quarter_mma(const KqRow<TYPE>& r0, const KqRow<TYPE>& r1, int c, 
 }
 
 template <int TYPE, int NT>
-EF_DEV void kq_block_mma(const KqRow<TYPE>& r0, const KqRow<TYPE>& r1, int c, const uint16_t* __restrict__ xrow,
-                         size_t tok_stride, float (&acc)[NT][4]) {
-  // xrow: this lane's token (g) of token group 0, at 256 kb + 8 c
-  kq_quarter_mma<TYPE, NT, 0>(r0, r1, c, xrow, tok_stride, acc);
-  kq_quarter_mma<TYPE, NT, 1>(r0, r1, c, xrow, tok_stride, acc);
-  kq_quarter_mma<TYPE, NT, 2>(r0, r1, c, xrow, tok_stride, acc);
-  kq_quarter_mma<TYPE, NT, 3>(r0, r1, c, xrow, tok_stride, acc);
+EF_DEV void kq_block_mma(KqRow<TYPE>& r0, KqRow<TYPE>& r1, int c, const uint16_t* __restrict__ xrow,
+                         const size_t (&tok_off)[NT], float (&acc)[NT][4]) {
+  // xrow: column 256 kb + 8 c of the permuted activations; tok_off[n]: this
+  // lane's token row of token group n
+  r0.prep(c);
+  r1.prep(c);
+  kq_quarter_mma<TYPE, NT, 0>(r0, r1, c, xrow, tok_off, acc);
+  kq_quarter_mma<TYPE, NT, 1>(r0, r1, c, xrow, tok_off, acc);
+  kq_quarter_mma<TYPE, NT, 2>(r0, r1, c, xrow, tok_off, acc);
+  kq_quarter_mma<TYPE, NT, 3>(r0, r1, c, xrow, tok_off, acc);
 }
+
+// Blocks in flight per warp (register ring depth).
+__host__ __device__ constexpr int kq_depth(int type, int nt) { return 2; }
 
 // y [T, N] fp32.  Grid: ceil(n_tiles / tiles_per_cta) CTAs of kKqWarps warps;
 // `split` warps share a tile (each a contiguous range of blocks).
 template <int TYPE, int NT>
-__global__ void __launch_bounds__(kKqWarps * 32, (NT == 1 && TYPE != kKqQ3) ? 3 : 2) kquant_gemv_kernel(const uint8_t* __restrict__ w,
+__global__ void __launch_bounds__(kKqWarps * 32, (NT == 1 && TYPE == kKqQ2) ? 3 : 2) kquant_gemv_kernel(const uint8_t* __restrict__ w,
                                                                    const uint16_t* __restrict__ xp, int T, int N,
                                                                    int K, int split, float* __restrict__ y) {
   constexpr int BB = kq_block_bytes(TYPE);
@@ -275,19 +299,32 @@ __global__ void __launch_bounds__(kKqWarps * 32, (NT == 1 && TYPE != kKqQ3) ? 3 
     const uint8_t* row0 = w + (size_t)(16 * tile + g) * row_bytes;
     const uint8_t* row1 = row0 + 8 * row_bytes;
     const size_t tok_stride = (size_t)K;
-    const uint16_t* xl = xp + (size_t)g * tok_stride + 8 * c;
-    if (kb0 < kb1) {
-      KqRow<TYPE> cur0, cur1, nxt0, nxt1;
-      cur0.load(row0 + (size_t)kb0 * BB, c);
-      cur1.load(row1 + (size_t)kb0 * BB, c);
-      for (int kb = kb0; kb < kb1; ++kb) {
-        if (kb + 1 < kb1) {
-          nxt0.load(row0 + (size_t)(kb + 1) * BB, c);
-          nxt1.load(row1 + (size_t)(kb + 1) * BB, c);
+    const uint16_t* xl = xp + 8 * c;
+    // token rows past T hold zeros: every lane whose token is one of them
+    // reads row T, so those loads collapse into one broadcast per warp
+    size_t tok_off[NT];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) tok_off[n] = (size_t)(8 * n + g < T ? 8 * n + g : T) * tok_stride;
+    // ring of D blocks in flight per warp: the load of block kb + D is issued
+    // as soon as block kb has been consumed
+    constexpr int D = kq_depth(TYPE, NT);
+    KqRow<TYPE> b0[D], b1[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i)
+      if (kb0 + i < kb1) {
+        b0[i].load(row0 + (size_t)(kb0 + i) * BB, c);
+        b1[i].load(row1 + (size_t)(kb0 + i) * BB, c);
+      }
+    for (int kb = kb0; kb < kb1; kb += D) {
+#pragma unroll
+      for (int i = 0; i < D; ++i) {
+        if (kb + i < kb1) {
+          kq_block_mma<TYPE, NT>(b0[i], b1[i], c, xl + (size_t)(kb + i) * 256, tok_off, acc);
+          if (kb + i + D < kb1) {
+            b0[i].load(row0 + (size_t)(kb + i + D) * BB, c);
+            b1[i].load(row1 + (size_t)(kb + i + D) * BB, c);
+          }
         }
-        kq_block_mma<TYPE, NT>(cur0, cur1, c, xl + (size_t)kb * 256, tok_stride, acc);
-        cur0 = nxt0;
-        cur1 = nxt1;
       }
     }
   }

@@ -234,8 +234,13 @@ def test_gpu_matmul_rejects_and_flags(K):
 
     w = torch.zeros(16 * 84, dtype=torch.uint8, device="cuda")
     x = torch.zeros((1, 256), dtype=torch.bfloat16, device="cuda")
-    with pytest.raises(L.EfmoeError):
-        K.matmul(x, w, 13, 16, 256)            # Q5_K: not supported
+    with pytest.raises(ValueError):
+        K.matmul(x, w, 13, 16, 256)            # Q5_K: refused by the wrapper ...
+    y = torch.empty((1, 16), dtype=torch.float32, device="cuda")
+    ws = torch.empty(1 << 16, dtype=torch.uint8, device="cuda")
+    st = L.lib().ef_kquant_matmul(x.data_ptr(), L.EF_DT_BF16, 1, w.data_ptr(), 13, 16, 256, y.data_ptr(),
+                                  ws.data_ptr(), ws.numel(), None)
+    assert st == -2                            # ... and by the C ABI (EF_ERR_UNSUPPORTED)
     with pytest.raises(L.EfmoeError):
         K.matmul(torch.zeros((1, 200), dtype=torch.bfloat16, device="cuda"), w, 10, 16, 200)  # K % 256
     with pytest.raises(L.EfmoeError):

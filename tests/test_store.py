@@ -311,7 +311,7 @@ def test_pool_over_store_failed_read_leaves_pool_usable(P, tmp_path):
     a.reshape(a.shape[0], -1)[:, 0] = 0x4780  # 65536.0: above fp16's range, in every expert
     tens[name] = (a, "BF16")
     W.write_safetensors(str(d / "model.safetensors"), tens)
-    store = P.ExpertStore.from_safetensors(str(d / "model.safetensors"))
+    store = P.ExpertStore.from_safetensors(str(d / "model.safetensors"), spec=spec)
     gates = _gates(spec, 2, 3)
     pool = P.ExpertSlotPool.from_store(store, budget=4, host_blobs=8)
     x = synthetic.make_x_torch(spec, 1, seed=1)
