@@ -62,3 +62,32 @@ def load_expert(experts: G.GGUFExperts, layer: int, e: int, proj: str, device="c
     raw, dtype, shape = experts.load_expert_raw(layer, e, proj)
     t = torch.from_numpy(np.frombuffer(raw, np.uint8).copy()).to(device)
     return t, dtype, tuple(int(v) for v in shape)
+
+
+def _main(argv=None) -> None:
+    """Launch the GEMV on random blocks (for profiling):
+    python -m expertflow_b200.kquant --type 10 --rows 32768 --cols 7168 --tokens 1 --reps 3"""
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--type", type=int, default=G.GGML_TYPE_Q2_K)
+    ap.add_argument("--rows", type=int, default=32768)
+    ap.add_argument("--cols", type=int, default=7168)
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--reps", type=int, default=3)
+    a = ap.parse_args(argv)
+    bb = G.GGML_BLOCK_SIZES[a.type][1]
+    w = torch.randint(0, 256, (a.rows * (a.cols // 256) * bb,), dtype=torch.uint8, device="cuda")
+    x = torch.randn((a.tokens, a.cols), device="cuda").to(torch.bfloat16)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(a.reps):
+        if i == a.reps - 1:
+            e0.record()
+        matmul(x, w, a.type, a.rows, a.cols)
+    e1.record()
+    torch.cuda.synchronize()
+    print(f"type {a.type}: {w.numel() / 1e6:.1f} MB of blocks, last launch {e0.elapsed_time(e1) * 1e3:.1f} us")
+
+
+if __name__ == "__main__":
+    _main()
