@@ -82,7 +82,7 @@ class PoolStats(ctypes.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
-EF_POLICY_FREQ, EF_POLICY_LRU = 0, 1
+EF_POLICY_FREQ, EF_POLICY_LRU, EF_POLICY_BELADY = 0, 1, 2
 
 
 class FileArray(ctypes.Structure):
@@ -133,6 +133,9 @@ SIGNATURES = {
     "ef_policy_keys": (_I, [_P, _P, _I]),
     "ef_policy_score": (ctypes.c_double, [_P, ctypes.c_longlong]),
     "ef_policy_destroy": (None, [_P]),
+    "ef_policy_end_token": (None, [_P]),
+    "ef_policy_set_predictor": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _I]),
+    "ef_pool_set_predictor": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _I]),
     "ef_pool_create": (_I, [_CFGP, ctypes.POINTER(PoolCfg), _QWP, _QWP, _QWP, _P]),
     "ef_pool_workspace_size": (_SZ, [_P, _I]),
     "ef_pool_moe_forward": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ, _P]),

@@ -33,6 +33,7 @@
 //     follow when that layer runs), then it waits for its own reads.
 #include <algorithm>
 #include <chrono>
+#include <cmath>
 #include <cstring>
 #include <memory>
 #include <set>
@@ -41,6 +42,37 @@
 #include <vector>
 
 namespace ef {
+
+// Learned eviction scorer of the reference's BeladyExpertCache
+// (ef_engine.py:107-161): 3 -> H -> H -> 1, SiLU between layers, input
+// [1/recency, count/max_count, gap_ema/max_gap]; the cached key with the
+// highest score is evicted.  Evaluated in double precision.
+struct BeladyNet {
+  int hidden = 0;
+  bool trained = false;
+  std::vector<double> w1, b1, w2, b2, w3;  // w1 [3][H], w2 [H][H], w3 [H]
+  double b3 = 0.0;
+  static double silu(double x) {
+    const double c = std::min(20.0, std::max(-20.0, x));
+    return x / (1.0 + std::exp(-c));
+  }
+  double score(const float (&f)[3]) const {
+    std::vector<double> h1(hidden), h2(hidden);
+    for (int j = 0; j < hidden; ++j) {
+      double z = b1[j];
+      for (int i = 0; i < 3; ++i) z += (double)f[i] * w1[(size_t)i * hidden + j];
+      h1[j] = silu(z);
+    }
+    for (int j = 0; j < hidden; ++j) {
+      double z = b2[j];
+      for (int i = 0; i < hidden; ++i) z += h1[i] * w2[(size_t)i * hidden + j];
+      h2[j] = silu(z);
+    }
+    double sc = b3;
+    for (int i = 0; i < hidden; ++i) sc += h2[i] * w3[i];
+    return sc;
+  }
+};
 
 class CachePolicy {
  public:
@@ -51,6 +83,7 @@ class CachePolicy {
     if (it == ents_.end()) return false;
     it->second.score += 1.0;
     it->second.last = ++clock_;
+    if (kind_ == EF_POLICY_BELADY) touch(key);
     return true;
   }
   void put(long long key) {
@@ -58,19 +91,30 @@ class CachePolicy {
     if (it != ents_.end()) {  // a put of a resident key only refreshes it (the dict keeps its place)
       it->second.score += 1.0;
       it->second.last = ++clock_;
-      return;
+    } else {
+      Ent e;
+      e.score = 1.0;
+      e.seq = ++seq_;
+      e.last = ++clock_;
+      ents_.emplace(key, e);
     }
-    Ent e;
-    e.score = 1.0;
-    e.seq = ++seq_;
-    e.last = ++clock_;
-    ents_.emplace(key, e);
+    if (kind_ == EF_POLICY_BELADY) touch(key);
   }
   bool contains(long long key) const { return ents_.count(key) != 0; }
   int size() const { return (int)ents_.size(); }
-  // Evicts down to the budget, then decays (FREQ); returns the evicted keys in order.
+  // Evicts down to the budget, then decays (FREQ: scores; BELADY: access
+  // counts, truncated to integers); returns the evicted keys in order.
   std::vector<long long> trim() {
     std::vector<long long> out;
+    if (kind_ == EF_POLICY_BELADY) {
+      while ((int)ents_.size() > budget_) {
+        const long long v = belady_victim(nullptr);
+        out.push_back(v);
+        ents_.erase(v);
+      }
+      for (auto& kv : recs_) kv.second.count = (long long)((double)kv.second.count * decay_);
+      return out;
+    }
     while ((int)ents_.size() > budget_) {
       auto victim = ents_.begin();
       for (auto it = ents_.begin(); it != ents_.end(); ++it) {
@@ -88,6 +132,8 @@ class CachePolicy {
       for (auto& kv : ents_) kv.second.score *= decay_;
     return out;
   }
+  // Advances the token clock of the learned policy (BeladyExpertCache.end_token).
+  void end_token() { ++token_; }
   // Resident keys, ascending.
   std::vector<long long> keys() const {
     std::vector<long long> k;
@@ -96,13 +142,25 @@ class CachePolicy {
     std::sort(k.begin(), k.end());
     return k;
   }
+  // FREQ/LRU: the key's score; BELADY: its eviction score (the predictor's
+  // output, or count * decay^recency when untrained).
   double score(long long key) const {
+    if (kind_ == EF_POLICY_BELADY) {
+      if (!ents_.count(key)) return 0.0;
+      if (net_.trained) {
+        float f[3];
+        features(key, f);
+        return net_.score(f);
+      }
+      return fallback_score(key);
+    }
     auto it = ents_.find(key);
     return it == ents_.end() ? 0.0 : it->second.score;
   }
   // Lowest-priority resident key not in `keep` (or -1): the victim an
   // immediate eviction would take.
   long long victim_excluding(const std::vector<char>& keep) const {
+    if (kind_ == EF_POLICY_BELADY) return belady_victim(&keep);
     long long best = -1;
     const Ent* be = nullptr;
     for (const auto& kv : ents_) {
@@ -120,6 +178,7 @@ class CachePolicy {
     return best;
   }
   void erase(long long key) { ents_.erase(key); }
+  void set_net(BeladyNet n) { net_ = std::move(n); }
 
  private:
   struct Ent {
@@ -127,10 +186,77 @@ class CachePolicy {
     unsigned long long seq;   // insertion order
     unsigned long long last;  // recency
   };
+  struct Rec {  // BeladyExpertCache.access_records entry
+    long long last = 0, count = 0;
+    double gap_ema = 0.0;
+  };
+  // BeladyExpertCache._update_access (ef_engine.py:211-220)
+  void touch(long long key) {
+    Rec& r = recs_[key];
+    if (r.count > 0) {
+      const double a = 0.7 * r.gap_ema;
+      const double b = 0.3 * (double)(token_ - r.last);
+      r.gap_ema = a + b;
+      max_gap_ = std::max(max_gap_, r.gap_ema);
+    }
+    r.last = token_;
+    r.count += 1;
+    max_freq_ = std::max(max_freq_, r.count);
+  }
+  // BeladyExpertCache._build_features (ef_engine.py:231-241), float32 like the reference
+  void features(long long key, float (&f)[3]) const {
+    auto it = recs_.find(key);
+    const Rec r = it == recs_.end() ? Rec{} : it->second;
+    const long long rec = token_ - r.last;
+    f[0] = (float)(1.0 / (double)std::max(rec, 1LL));
+    f[1] = (float)((double)r.count / (double)std::max(max_freq_, 1LL));
+    f[2] = (float)(r.gap_ema / std::max(max_gap_, 1.0));
+  }
+  double fallback_score(long long key) const {  // count * decay^recency (ef_engine.py:256-260)
+    auto it = recs_.find(key);
+    const Rec r = it == recs_.end() ? Rec{} : it->second;
+    return (double)r.count * std::pow(decay_, (double)(token_ - r.last));
+  }
+  // BeladyExpertCache.trim's choice (ef_engine.py:243-261): among the
+  // resident keys in insertion order, the first with the highest predictor
+  // score (trained, more than one key) or the lowest fallback score.
+  long long belady_victim(const std::vector<char>* keep) const {
+    std::vector<std::pair<unsigned long long, long long>> order;
+    order.reserve(ents_.size());
+    for (const auto& kv : ents_) {
+      if (keep && kv.first >= 0 && kv.first < (long long)keep->size() && (*keep)[kv.first]) continue;
+      order.push_back({kv.second.seq, kv.first});
+    }
+    if (order.empty()) return -1;
+    std::sort(order.begin(), order.end());
+    const bool learned = net_.trained && ents_.size() > 1;
+    long long best = -1;
+    double bs = 0.0;
+    for (const auto& o : order) {
+      double sc;
+      if (learned) {
+        float f[3];
+        features(o.second, f);
+        sc = net_.score(f);
+      } else {
+        sc = fallback_score(o.second);
+      }
+      if (best < 0 || (learned ? sc > bs : sc < bs)) {
+        best = o.second;
+        bs = sc;
+      }
+    }
+    return best;
+  }
   int kind_, budget_;
   double decay_;
   unsigned long long seq_ = 0, clock_ = 0;
   std::unordered_map<long long, Ent> ents_;
+  // learned policy state
+  std::unordered_map<long long, Rec> recs_;
+  long long token_ = 0, max_freq_ = 1;
+  double max_gap_ = 1.0;
+  BeladyNet net_;
 };
 
 }  // namespace ef
@@ -536,13 +662,30 @@ ef_status pool_route(const ef_moe_cfg& cfg, const void* x, int T, const void* gw
   return EF_OK;
 }
 
+ef_status make_net(int hidden, const float* w1, const float* b1, const float* w2, const float* b2, const float* w3,
+                   const float* b3, int trained, ef::BeladyNet& n) {
+  if (hidden < 1 || hidden > 4096) return fail(EF_ERR_INVALID, "hidden must be in 1..4096");
+  if (!w1 || !b1 || !w2 || !b2 || !w3 || !b3) return fail(EF_ERR_INVALID, "null predictor weight");
+  const size_t H = (size_t)hidden;
+  n.hidden = hidden;
+  n.trained = trained != 0;
+  n.w1.assign(w1, w1 + 3 * H);
+  n.b1.assign(b1, b1 + H);
+  n.w2.assign(w2, w2 + H * H);
+  n.b2.assign(b2, b2 + H);
+  n.w3.assign(w3, w3 + H);
+  n.b3 = b3[0];
+  return EF_OK;
+}
+
 ef_status check_pool_cfg(const ef_moe_cfg* cfg, const ef_pool_cfg* pc) {
   ef_status s = check_cfg(cfg);
   if (s) return s;
   if (!pc) return fail(EF_ERR_INVALID, "null pointer");
   if (pc->n_layers <= 0 || pc->budget < 0 || pc->headroom < cfg->top_k)
     return fail(EF_ERR_INVALID, "need n_layers > 0, budget >= 0, headroom >= top_k");
-  if (pc->policy != EF_POLICY_FREQ && pc->policy != EF_POLICY_LRU) return fail(EF_ERR_INVALID, "unknown policy");
+  if (pc->policy != EF_POLICY_FREQ && pc->policy != EF_POLICY_LRU && pc->policy != EF_POLICY_BELADY)
+    return fail(EF_ERR_INVALID, "unknown policy");
   if (cfg->n_shared) return fail(EF_ERR_UNSUPPORTED, "the slot pool streams routed experts only (n_shared = 0)");
   return EF_OK;
 }
@@ -614,7 +757,8 @@ extern "C" {
 ef_status ef_policy_create(int kind, int budget, double decay, ef_cache_policy** out) {
   if (!out) return fail(EF_ERR_INVALID, "out is NULL");
   *out = nullptr;
-  if (kind != EF_POLICY_FREQ && kind != EF_POLICY_LRU) return fail(EF_ERR_INVALID, "unknown policy %d", kind);
+  if (kind != EF_POLICY_FREQ && kind != EF_POLICY_LRU && kind != EF_POLICY_BELADY)
+    return fail(EF_ERR_INVALID, "unknown policy %d", kind);
   if (budget < 0) return fail(EF_ERR_INVALID, "budget < 0");
   *out = new ef_cache_policy{ef::CachePolicy(kind, budget, decay)};
   return EF_OK;
@@ -637,6 +781,18 @@ int ef_policy_keys(const ef_cache_policy* p, long long* keys, int cap) {
   return (int)k.size();
 }
 double ef_policy_score(const ef_cache_policy* p, long long key) { return p ? p->p.score(key) : 0.0; }
+void ef_policy_end_token(ef_cache_policy* p) {
+  if (p) p->p.end_token();
+}
+ef_status ef_policy_set_predictor(ef_cache_policy* p, int hidden, const float* w1, const float* b1, const float* w2,
+                                  const float* b2, const float* w3, const float* b3, int trained) {
+  if (!p) return fail(EF_ERR_INVALID, "policy is NULL");
+  ef::BeladyNet n;
+  ef_status s = make_net(hidden, w1, b1, w2, b2, w3, b3, trained, n);
+  if (s) return s;
+  p->p.set_net(std::move(n));
+  return EF_OK;
+}
 void ef_policy_destroy(ef_cache_policy* p) { delete p; }
 
 // ---------------------------------------------------------------- slot pool
@@ -950,8 +1106,19 @@ ef_status ef_pool_end_token(ef_slot_pool* P) {
       L.expert_slot[e] = -1;
       P->st.evictions++;
     }
+    L.policy.end_token();  // trim, then end_token, as the reference's decode loop does
   }
   P->st.tokens++;
+  return EF_OK;
+}
+
+ef_status ef_pool_set_predictor(ef_slot_pool* P, int hidden, const float* w1, const float* b1, const float* w2,
+                                const float* b2, const float* w3, const float* b3, int trained) {
+  if (!P) return fail(EF_ERR_INVALID, "pool is NULL");
+  ef::BeladyNet n;
+  ef_status s = make_net(hidden, w1, b1, w2, b2, w3, b3, trained, n);
+  if (s) return s;
+  for (auto& L : P->layers) L.policy.set_net(n);
   return EF_OK;
 }
 

@@ -28,16 +28,52 @@ from . import _lib as L
 from .moe import MoEGate, _act_dt, _need_cuda, _stream_ptr, workspace
 from .spec import MoESpec
 
-_POLICIES = {"freq": L.EF_POLICY_FREQ, "lru": L.EF_POLICY_LRU}
+_POLICIES = {"freq": L.EF_POLICY_FREQ, "lru": L.EF_POLICY_LRU, "belady": L.EF_POLICY_BELADY}
+_NET = ("w1", "b1", "w2", "b2", "w3", "b3")
+
+
+def load_predictor(src) -> dict:
+    """Eviction-predictor weights: a dict, or the .npz that the reference's
+    ``BeladyPredictor.save`` writes (ef_engine.py:143-148): w1 [3, H], b1 [H],
+    w2 [H, H], b2 [H], w3 [H, 1], b3 [1], trained."""
+    if isinstance(src, (str, os.PathLike)):
+        z = np.load(src)
+        src = {k: z[k] for k in z.files}
+    out = {k: np.ascontiguousarray(np.asarray(src[k], np.float32)) for k in _NET}
+    H = out["b1"].shape[0]
+    if out["w1"].shape != (3, H) or out["w2"].shape != (H, H) or out["b2"].shape != (H,) or out["w3"].size != H \
+            or out["b3"].size != 1:
+        raise ValueError("predictor weights do not have the 3 -> H -> H -> 1 shapes")
+    out["w3"] = out["w3"].reshape(H)
+    out["trained"] = bool(np.asarray(src.get("trained", True)).reshape(-1)[0])
+    return out
+
+
+def _net_args(w: dict):
+    H = w["b1"].shape[0]
+    ptrs = [ctypes.c_void_p(w[k].ctypes.data) for k in _NET]
+    return (H, *ptrs, int(w["trained"]))
 
 
 class CachePolicy:
-    """FrequencyWeightedCache(budget, decay) semantics: get / put / trim."""
+    """FrequencyWeightedCache(budget, decay) semantics: get / put / trim;
+    ``kind="lru"``; ``kind="belady"``: BeladyExpertCache (learned eviction,
+    ``set_predictor``; call ``trim()`` then ``end_token()`` once per token)."""
 
-    def __init__(self, budget: int, decay: float = 0.95, kind: str = "freq"):
+    def __init__(self, budget: int, decay: float = 0.95, kind: str = "freq", predictor=None):
         h = ctypes.c_void_p()
         L.check(L.lib().ef_policy_create(_POLICIES[kind], budget, decay, ctypes.byref(h)))
         self._h = h
+        if predictor is not None:
+            self.set_predictor(predictor)
+
+    def set_predictor(self, predictor) -> None:
+        w = load_predictor(predictor)
+        self._net = w  # the library copies; kept for inspection
+        L.check(L.lib().ef_policy_set_predictor(self._h, *_net_args(w)))
+
+    def end_token(self) -> None:
+        L.lib().ef_policy_end_token(self._h)
 
     def get(self, key: int) -> bool:
         return bool(L.lib().ef_policy_get(self._h, key))
@@ -332,6 +368,10 @@ class ExpertSlotPool:
 
     def end_token(self) -> None:
         L.check(L.lib().ef_pool_end_token(self._h))
+
+    def set_predictor(self, predictor) -> None:
+        """Learned-eviction weights for every layer (pools made with policy="belady")."""
+        L.check(L.lib().ef_pool_set_predictor(self._h, *_net_args(load_predictor(predictor))))
 
     def resident(self, layer: int) -> list:
         n = ctypes.c_int()

@@ -209,6 +209,16 @@ ef_status ef_ep_combine(const ef_moe_cfg* cfg, const float* back_rows, const int
  * evicts the least recently used key and does not decay. */
 #define EF_POLICY_FREQ 0
 #define EF_POLICY_LRU 1
+/* EF_POLICY_BELADY is the reference's BeladyExpertCache (ef_engine.py:163-279):
+ * per key it records the last access token, an access count and an EMA of the
+ * gap between accesses; trim() evicts, among the resident keys in insertion
+ * order, the first with the highest learned score (a 3 -> H -> H -> 1 SiLU
+ * network on [1/recency, count/max_count, gap/max_gap], weights from
+ * ef_policy_set_predictor) or, while the predictor is untrained, the first
+ * with the lowest count * decay^recency; then every count becomes
+ * floor(count * decay).  ef_policy_end_token advances its token clock (the
+ * reference calls trim, then end_token, once per token). */
+#define EF_POLICY_BELADY 2
 typedef struct ef_cache_policy ef_cache_policy;
 ef_status ef_policy_create(int kind, int budget, double decay, ef_cache_policy** out);
 int ef_policy_get(ef_cache_policy* p, long long key);  /* 1 on a hit (FrequencyWeightedCache.get) */
@@ -219,6 +229,12 @@ int ef_policy_trim(ef_cache_policy* p, long long* evicted, int cap);
 int ef_policy_size(const ef_cache_policy* p);
 int ef_policy_keys(const ef_cache_policy* p, long long* keys, int cap); /* resident keys, ascending */
 double ef_policy_score(const ef_cache_policy* p, long long key);
+void ef_policy_end_token(ef_cache_policy* p);
+/* Predictor weights (row-major, the reference's BeladyPredictor layout):
+ * w1 [3][hidden], b1 [hidden], w2 [hidden][hidden], b2 [hidden], w3 [hidden],
+ * b3 [1]; trained = 0 keeps the frequency fallback. Copied. */
+ef_status ef_policy_set_predictor(ef_cache_policy* p, int hidden, const float* w1, const float* b1, const float* w2,
+                                  const float* b2, const float* w3, const float* b3, int trained);
 void ef_policy_destroy(ef_cache_policy* p);
 
 /* Streaming-decode expert pool: the experts of n_layers MoE layers live in
@@ -235,7 +251,7 @@ typedef struct {
   int n_layers;
   int budget;    /* experts per layer kept across tokens */
   int headroom;  /* extra slots per layer for one step's misses */
-  int policy;    /* EF_POLICY_FREQ | EF_POLICY_LRU */
+  int policy;    /* EF_POLICY_FREQ | EF_POLICY_LRU | EF_POLICY_BELADY */
   double decay;  /* EF_POLICY_FREQ score decay per token (reference: 0.95) */
 } ef_pool_cfg;
 typedef struct {
@@ -286,6 +302,10 @@ ef_status ef_pool_decode_step(ef_slot_pool* pool, float* r, int T, const void* c
                               const float* const* e_bias, int lookahead, float eps, void* workspace,
                               size_t workspace_bytes, void* stream);
 ef_status ef_pool_resident(const ef_slot_pool* pool, int layer, int32_t* experts, int cap, int* n);
+/* The learned policy's predictor for every layer of a pool created with
+ * policy EF_POLICY_BELADY (same layout as ef_policy_set_predictor). */
+ef_status ef_pool_set_predictor(ef_slot_pool* pool, int hidden, const float* w1, const float* b1, const float* w2,
+                                const float* b2, const float* w3, const float* b3, int trained);
 
 /* ---- GGUF K-quants ------------------------------------------------------------------ */
 /* Blocks of 256 elements as the reference decodes them (ef_deepseek_mmap.py:330-378,

@@ -191,3 +191,146 @@ def test_pool_decode_step_independent_of_residency(P):
     assert sa["tokens"] == steps and sa["copies_prefetch"] > 0
     assert sb["copies_sync"] <= spec.n_experts * n_layers
     assert moe.device_error() == 0
+
+
+# ---------------------------------------------------------------- learned eviction
+BELADY = os.path.join(REPO, "tests", "golden", "belady_trace.npz")
+_NETK = ("w1", "b1", "w2", "b2", "w3", "b3")
+
+
+def _trace_tokens():
+    c = np.load(GOLDEN)
+    toks, cur = [], []
+    for a in c["accesses"].tolist():
+        if a == -2:
+            toks.append(cur)
+            cur = []
+        elif a >= 0:
+            cur.append(a)
+    return toks
+
+
+def _net(z, name):
+    return {k: z[f"{name}_{k}"] for k in _NETK} | {"trained": True}
+
+
+@pytest.mark.parametrize("name", ["untrained", "seed0", "seed4x4", "trained"])
+def test_belady_policy_replays_reference(P, name):
+    """BeladyExpertCache (ef_engine.py:163-279) driven by the reference's Zipf
+    trace with its own predictors: every hit/miss, eviction count and resident
+    set.  (seed1 / seed1x4 are left to the score test below: their rankings
+    hold exact ties that the reference breaks by fp32 BLAS rounding noise.)"""
+    z = np.load(BELADY)
+    pol = P.CachePolicy(int(z["budget"]), float(z["decay"]), kind="belady",
+                        predictor=None if name == "untrained" else _net(z, name))
+    hits, ev = [], []
+    for t, tok in enumerate(_trace_tokens()):
+        for key in tok:
+            h = pol.get(key)
+            if not h:
+                pol.put(key)
+            hits.append(int(h))
+        ev.append(len(pol.trim()))
+        pol.end_token()
+        assert pol.keys() == sorted(int(r) for r in z[f"{name}_resident"][t] if r >= 0), (name, t)
+    np.testing.assert_array_equal(np.asarray(hits, np.int8), z[f"{name}_hits"])
+    np.testing.assert_array_equal(np.asarray(ev), z[f"{name}_evicted"])
+    pol.close()
+
+
+def test_belady_scores_match_reference(P):
+    """The predictor's score of every resident key just before the reference's
+    first eviction (seed1), within fp32 rounding of the reference's numpy."""
+    z = np.load(BELADY)
+    pol = P.CachePolicy(int(z["budget"]), float(z["decay"]), kind="belady", predictor=_net(z, "seed1"))
+    toks = _trace_tokens()
+    T = int(z["snapshot_token"])
+    for t in range(T + 1):
+        for key in toks[t]:
+            if not pol.get(key):
+                pol.put(key)
+        if t < T:
+            assert pol.trim() == []
+            pol.end_token()
+    ours = np.array([pol.score(int(k)) for k in z["snapshot_keys"]])
+    np.testing.assert_allclose(ours, z["snapshot_scores"].astype(np.float64), rtol=2e-6, atol=1e-9)
+    pol.close()
+
+
+def test_belady_untrained_is_frequency_fallback(P):
+    """Untrained: evict the lowest count * decay^recency, the first inserted
+    among equals; counts are truncated by decay after each trim."""
+    pol = P.CachePolicy(2, 0.5, kind="belady")
+    for k in (5, 6, 7):
+        pol.put(k)
+    assert pol.trim() == [5] and pol.keys() == [6, 7]   # equal scores: first inserted goes
+    pol.end_token()
+    assert pol.get(7)                                     # count(7): 1 -> floor(0.5) = 0, +1 = 1
+    assert pol.score(6) == 0.0                            # count(6): floor(1 * 0.5) = 0
+    pol.put(8)
+    assert pol.trim() == [6]
+    pol.close()
+
+
+def test_predictor_file_format(P, tmp_path):
+    """A predictor saved the way the reference saves one (BeladyPredictor.save)."""
+    z = np.load(BELADY)
+    w = _net(z, "trained")
+    f = tmp_path / "belady.npz"
+    np.savez(f, **{k: w[k] for k in _NETK}, trained=np.array([True]), input_dim=np.array([3]),
+             hidden_dim=np.array([64]))
+    loaded = P.load_predictor(str(f))
+    assert loaded["trained"] and loaded["w3"].shape == (64,)
+    with pytest.raises(ValueError):
+        P.load_predictor({**w, "w2": w["w2"][:10]})
+
+
+@pytest.mark.gpu
+def test_pool_belady_policy_matches_host_replay(P):
+    """A pool with the learned policy: outputs bit-identical to resident layers,
+    and each layer's residency equal to a host-side BeladyExpertCache replay of
+    the routed experts (trim, then end_token, per token)."""
+    import torch
+    from expertflow_b200 import moe, synthetic
+
+    spec = _small_spec()
+    n_layers, budget, steps = 3, 6, 10
+    dev = torch.device("cuda")
+    z = np.load(BELADY)
+    net = _net(z, "trained")
+    host = P.make_host_layers(spec, n_layers, seed=300)
+    bias = torch.from_numpy(P.zipf_layer_bias(n_layers, spec.n_experts, 1.1, seed=5)).to(dev)
+    gates, resident = [], []
+    for layer in range(n_layers):
+        g = torch.Generator(device=dev)
+        g.manual_seed(800 + layer)
+        gw = (torch.randn((spec.n_experts, spec.hidden), generator=g, device=dev) * 0.02).to(torch.float16)
+        gates.append(moe.MoEGate(gw, spec.top_k, "softmax", True, e_score_correction_bias=bias[layer].contiguous()))
+        d = {"gate_w": gw, "e_bias": None, "shared": None}
+        for k in ("gate", "up", "down"):
+            d[k] = tuple(a.to(dev) for a in host[layer][k])
+        m = moe.MoELayer.from_arrays(spec, d)
+        m.gate = gates[layer]
+        resident.append(m)
+    pool = P.ExpertSlotPool(spec, host, budget=budget, headroom=spec.top_k, policy="belady")
+    pool.set_predictor(net)
+    ref = [P.CachePolicy(budget, 0.95, kind="belady", predictor=net) for _ in range(n_layers)]
+    for t in range(steps):
+        x = synthetic.make_x_torch(spec, 1, seed=950 + t)
+        for layer in range(n_layers):
+            inds = torch.empty((1, spec.top_k), dtype=torch.int32, device=dev)
+            y = pool.forward(layer, x, gates[layer], None, inds_out=inds, out_dtype=torch.float32)
+            y_ref = resident[layer](x, out_dtype=torch.float32)
+            torch.cuda.synchronize()
+            assert torch.equal(y, y_ref), (t, layer)
+            for e in sorted(set(inds.flatten().tolist())):
+                if not ref[layer].get(e):
+                    ref[layer].put(e)
+            x = (x.float() + y).to(x.dtype)
+        pool.end_token()
+        for layer in range(n_layers):
+            ref[layer].trim()
+            ref[layer].end_token()
+            assert pool.resident(layer) == ref[layer].keys(), (t, layer)
+    assert moe.device_error() == 0
+    pool.close()
