@@ -135,23 +135,33 @@ struct KqRow<kKqQ3> {
       }
   }
   EF_DEV void prep(int) {}
+  // MMAs j = 4QQ .. 4QQ+3.  A group takes eight values, a (u - 4) for
+  // u = q + 4 in 0..7 (exact products, then RN16): halves 0..3 of (L0, L1)
+  // for the codes whose hmask bit is clear, of (L2, L3) for those with it
+  // set.  Each pair of 2-bit codes selects from both tables with one byte
+  // permute each; the hmask bits, moved to the top of their bytes, become a
+  // per-half mask (sign-replicating permute) that picks between the two.
   template <int QQ>
-  EF_DEV void frags(int, uint32_t (&lo)[4], uint32_t (&hi)[4]) const {  // MMAs j = 4QQ .. 4QQ+3
+  EF_DEV void frags(int, uint32_t (&lo)[4], uint32_t (&hi)[4]) const {
     constexpr int H = QQ >> 1;
 #pragma unroll
-    for (int j4 = 0; j4 < 4; ++j4) {
-      const int jj = 4 * (QQ & 1) + j4;
-      const int s = jj >> 1, u = jj & 1;
+    for (int sp = 0; sp < 2; ++sp) {
+      const int s = 2 * (QQ & 1) + sp;
       const float a = A[4 * H + s];
-      const uint32_t q = qw[2 * H + u] >> (2 * s), hb = hw[u] >> (4 * H + s);
-      float v[4];
+      const uint32_t L0 = pack_h2(a * -4.0f, a * -3.0f), L1 = pack_h2(a * -2.0f, a * -1.0f);
+      const uint32_t L2 = pack_h2(a * 0.0f, a), L3 = pack_h2(a * 2.0f, a * 3.0f);
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const uint32_t u3 = ((q >> (8 * t)) & 3u) | (((hb >> (8 * t)) & 1u) << 2);
-        v[t] = fmaf(a, code_f32(u3), -4.0f * a);
+      for (int u = 0; u < 2; ++u) {
+        const int j4 = 2 * sp + u;
+        const uint32_t r4 = (qw[2 * H + u] >> (2 * s)) & 0x03030303u;  // 2-bit codes of bytes 0..3
+        const uint32_t S = r4 * 0x22u + 0x10101010u;
+        const uint32_t hs = hw[u] << (7 - (4 * H + s));               // hmask bit -> bit 7 of its byte
+        const uint32_t m01 = prmt(hs, 0u, 0x9988u), m23 = prmt(hs, 0u, 0xBBAAu);
+        const uint32_t lo_n = prmt(L0, L1, S), lo_p = prmt(L2, L3, S);
+        const uint32_t hi_n = prmt(L0, L1, S >> 16), hi_p = prmt(L2, L3, S >> 16);
+        lo[j4] = (lo_n & ~m01) | (lo_p & m01);
+        hi[j4] = (hi_n & ~m23) | (hi_p & m23);
       }
-      lo[j4] = pack_h2(v[0], v[1]);
-      hi[j4] = pack_h2(v[2], v[3]);
     }
   }
 };
