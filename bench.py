@@ -443,6 +443,11 @@ def stream_from_files(spec, host, gates, run, steps, budget, ms_res, args):
     from expertflow_b200 import _lib as L, pool as P, weights as W
 
     NL, E = len(host), spec.n_experts
+    need = NL * E * spec.expert_bytes()
+    base = args.stream_dir or tempfile.gettempdir()
+    free = shutil.disk_usage(base).free
+    if free < 2 * need:
+        return {"skipped": f"{free / 1e9:.1f} GB free under {base}, the model needs {need / 1e9:.1f} GB"}
     root = tempfile.mkdtemp(prefix="ef_stream_", dir=args.stream_dir or None)
     try:
         t0 = time.perf_counter()
