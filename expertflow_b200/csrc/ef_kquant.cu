@@ -430,10 +430,11 @@ cudaError_t launch_kquant_gemv_t(const uint8_t* w, const uint16_t* xp, int T, in
 namespace {
 
 int kq_split(int N, int K, int n_sm) {
-  // warps sharing a tile: enough warps to cover the SMs several times over
+  // warps sharing a tile: enough (tile, block range) units for about four
+  // waves of resident warps, so the last wave's tail stays short
   const int n_tiles = N >> 4, nb = K >> 8;
   int split = 1;
-  while (split < ef::kKqWarps && (long long)n_tiles * split < 24LL * n_sm && split * 2 <= nb) split *= 2;
+  while (split < ef::kKqWarps && (long long)n_tiles * split < 96LL * n_sm && split * 2 <= nb) split *= 2;
   return split;
 }
 
