@@ -282,8 +282,9 @@ EF_DEV void kq_block_mma(KqRow<TYPE>& r0, KqRow<TYPE>& r1, int c, const uint16_t
   kq_quarter_mma<TYPE, NT, 3>(r0, r1, c, xrow, tok_off, acc);
 }
 
-// Blocks in flight per warp (register ring depth).
-__host__ __device__ constexpr int kq_depth(int type, int nt) { return 2; }
+// Blocks in flight per warp (register ring depth).  Deeper rings cost
+// occupancy and measured slower.
+constexpr int kKqDepth = 2;
 
 // y [T, N] fp32.  Grid: ceil(n_tiles / tiles_per_cta) CTAs of kKqWarps warps;
 // `split` warps share a tile (each a contiguous range of blocks).
@@ -317,7 +318,7 @@ __global__ void __launch_bounds__(kKqWarps * 32, (NT == 1 && TYPE == kKqQ2) ? 3 
     for (int n = 0; n < NT; ++n) tok_off[n] = (size_t)(8 * n + g < T ? 8 * n + g : T) * tok_stride;
     // ring of D blocks in flight per warp: the load of block kb + D is issued
     // as soon as block kb has been consumed
-    constexpr int D = kq_depth(TYPE, NT);
+    constexpr int D = kKqDepth;
     KqRow<TYPE> b0[D], b1[D];
 #pragma unroll
     for (int i = 0; i < D; ++i)
@@ -414,11 +415,10 @@ __global__ void kquant_dequant_kernel(const uint8_t* __restrict__ blocks, long l
 
 template <int TYPE>
 cudaError_t launch_kquant_gemv_t(const uint8_t* w, const uint16_t* xp, int T, int N, int K, int split, float* y,
-                                 int n_sm, cudaStream_t st) {
+                                 cudaStream_t st) {
   const int n_tiles = N >> 4, tiles_per_cta = kKqWarps / split;
   const int grid = (n_tiles + tiles_per_cta - 1) / tiles_per_cta;
   const int nt = (T + 7) / 8;
-  (void)n_sm;
   if (nt == 1) kquant_gemv_kernel<TYPE, 1><<<grid, kKqWarps * 32, 0, st>>>(w, xp, T, N, K, split, y);
   else if (nt == 2) kquant_gemv_kernel<TYPE, 2><<<grid, kKqWarps * 32, 0, st>>>(w, xp, T, N, K, split, y);
   else kquant_gemv_kernel<TYPE, 4><<<grid, kKqWarps * 32, 0, st>>>(w, xp, T, N, K, split, y);
@@ -486,7 +486,7 @@ ef_status ef_kquant_matmul(const void* x, int act_dtype, int T, const void* bloc
   if (T == 0) return EF_OK;
   if (T > 32) return fail(EF_ERR_UNSUPPORTED, "T must be <= 32 for the K-quant GEMV (decode)");
   if (!x || !blocks || !y || !workspace) return fail(EF_ERR_INVALID, "null pointer");
-  const uintptr_t need_align = type == ef::kKqQ4 ? 15 : type == ef::kKqQ2 ? 3 : 3;
+  const uintptr_t need_align = type == ef::kKqQ4 ? 15 : 3;  // Q4_K rows are read in 16-byte vectors
   if ((reinterpret_cast<uintptr_t>(blocks) & need_align) || (reinterpret_cast<uintptr_t>(workspace) & 15))
     return fail(EF_ERR_INVALID, "blocks must be %d-byte aligned, workspace 16-byte aligned", (int)need_align + 1);
   if (ws_bytes < ef_kquant_matmul_workspace_size(T, K)) return fail(EF_ERR_WORKSPACE, "workspace too small");
@@ -507,9 +507,9 @@ ef_status ef_kquant_matmul(const void* x, int act_dtype, int T, const void* bloc
   if (e != cudaSuccess) return fail(EF_ERR_CUDA, "kquant_prep: %s", cudaGetErrorString(e));
   const int split = kq_split(N, K, n_sm);
   const uint8_t* w = static_cast<const uint8_t*>(blocks);
-  if (type == ef::kKqQ2) e = ef::launch_kquant_gemv_t<ef::kKqQ2>(w, xp, T, N, K, split, y, n_sm, st);
-  else if (type == ef::kKqQ3) e = ef::launch_kquant_gemv_t<ef::kKqQ3>(w, xp, T, N, K, split, y, n_sm, st);
-  else e = ef::launch_kquant_gemv_t<ef::kKqQ4>(w, xp, T, N, K, split, y, n_sm, st);
+  if (type == ef::kKqQ2) e = ef::launch_kquant_gemv_t<ef::kKqQ2>(w, xp, T, N, K, split, y, st);
+  else if (type == ef::kKqQ3) e = ef::launch_kquant_gemv_t<ef::kKqQ3>(w, xp, T, N, K, split, y, st);
+  else e = ef::launch_kquant_gemv_t<ef::kKqQ4>(w, xp, T, N, K, split, y, st);
   if (e != cudaSuccess) return fail(EF_ERR_CUDA, "kquant_gemv: %s", cudaGetErrorString(e));
   return EF_OK;
 }
