@@ -18,19 +18,21 @@
 //     scatters the staged blobs into their slots with one kernel, makes the
 //     compute stream wait, and runs the experts on slot ids (read by the
 //     permute kernel straight from pinned memory, so no small copy queues
-//     behind the expert copies).  The optional next-layer gate predicts the next layer's
-//     experts from the current input (experiments/ef_v16_prefetch.py:92-113)
-//     and their copies start before this layer's expert kernels, so they
-//     overlap compute.  trim() runs once per token (ef_pool_end_token), as the
-//     reference trims after each token; the headroom slots hold the token's
-//     misses until then.
+//     behind the expert copies).  The optional next-layer gate predicts the
+//     next layer's experts from the current input
+//     (experiments/ef_v16_prefetch.py:92-113) and their copies are issued
+//     right after this layer's expert kernels, so both the host work and the
+//     copies overlap those kernels.  trim() runs once per token
+//     (ef_pool_end_token), as the reference trims after each token; the
+//     headroom slots hold the token's misses until then.
 // (3) A pool over an ef_expert_store (ef_pool_create_from_store) keeps only a
 //     bounded number of pinned host blobs, the least recently used replaced;
 //     an expert in neither HBM nor the host tier is read from the model files
-//     by the store's reader threads.  The step starts its own reads first,
-//     then the lookahead starts the reads of the next layer's predicted
-//     experts (they run while this layer computes, and their copies into HBM
-//     follow when that layer runs), then it waits for its own reads.
+//     by the store's reader threads.  The step starts its own reads and waits
+//     for them before it changes any residency state; after this layer's
+//     expert kernels, the lookahead starts the reads of the next layer's
+//     predicted experts (they run while this layer computes, and their copies
+//     into HBM follow when that layer runs).
 #include <algorithm>
 #include <chrono>
 #include <cmath>
@@ -945,49 +947,6 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
         return fail(EF_ERR_SLOT_MISS, "layer %d: the host tier (%d blobs) cannot hold one step's experts", layer,
                     P->host_n);
   }
-  // 2. lookahead copies for the next layer (overlap this layer's experts); in
-  //    a pool over a store, an expert not yet in the host tier has its read
-  //    started instead, and is copied when its layer runs
-  if (next_gate_w) {
-    const int nl = layer + 1;
-    LayerSlots& N = P->layers[nl];
-    const std::vector<int> pred = distinct_sorted(P->h_pred, n, E);
-    std::vector<char> nkeep(E, 0);
-    for (int e : pred) nkeep[e] = 1;
-    bool any = false;
-    CopyTimer t{};
-    for (int e : pred) {
-      if (N.expert_slot[e] >= 0) continue;
-      int h = -1;
-      if (P->store) {
-        h = host_find(P, nl, e);
-        if (h < 0) {
-          host_fetch(P, nl, e, true);  // -1 (no blob to replace): the prediction is only a hint
-          continue;
-        }
-        if (!ef::store_done(&P->host_ticket[h]) || P->host_ticket[h].err.load()) continue;
-        host_touch(P, h);
-        P->st.host_hits++;
-      }
-      const int sl = take_slot(P, nl, nkeep);
-      if (sl < 0) break;  // no free slot: the prediction is only a hint
-      if (!any) {
-        copies_begin(P, 1, N);
-        t = timer_begin(P, P->lane[1].stream);
-        any = true;
-      }
-      if ((s = copy_expert(P, 1, nl, e, sl, h))) return s;
-      N.staged[e] = 1;
-      P->st.copies_prefetch++;
-    }
-    if (any) {
-      if ((s = flush_stage(P, 1))) return s;
-      cudaEventRecord(t.b, P->lane[1].stream);
-      P->timers.push_back(t);
-      cudaEventRecord(N.ready[1], P->lane[1].stream);
-      N.has_ready[1] = true;
-    }
-  }
   // this layer's file reads must be complete before its state changes (a
   // failed read leaves the pool as it was)
   if (P->store) {
@@ -998,7 +957,7 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
       if ((s = host_ready(P, h, layer, e))) return s;
     }
   }
-  // 3. resolve this layer's experts (ef_engine.py:650-675): policy get, put on a miss
+  // 2. resolve this layer's experts (ef_engine.py:650-675): policy get, put on a miss
   bool any = false;
   CopyTimer t{};
   for (int e : need) {
@@ -1043,7 +1002,7 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
   // this layer's experts wait for both lanes' copies into its slots
   for (int ln = 0; ln < 2; ++ln)
     if (L.has_ready[ln]) cudaStreamWaitEvent(st, L.ready[ln], 0);
-  // 4. experts on slot ids
+  // 3. experts on slot ids
   // slot ids stay in pinned memory: the permute kernel reads them over the
   // link (n ints) instead of a copy that would queue behind the expert copies
   for (int i = 0; i < n; ++i) P->h_slot[i] = L.expert_slot[P->h_inds[i]];
@@ -1057,6 +1016,51 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
   if ((s = moe_tail(&sc, x, T, P->h_slot, wts, qg, qu, qd, nullptr, nullptr, nullptr, w.f, y, st))) return s;
   cudaEventRecord(L.last_use, st);
   L.has_use = true;
+  // 4. lookahead copies for the next layer, issued after this layer's expert
+  //    kernels so that the host work and the copies overlap them (the step
+  //    synchronised once, for the routing; host time before the launches is
+  //    idle GPU time); in a pool over a store, an expert not yet in the host
+  //    tier has its read started instead, and is copied when its layer runs
+  if (next_gate_w) {
+    const int nl = layer + 1;
+    LayerSlots& N = P->layers[nl];
+    const std::vector<int> pred = distinct_sorted(P->h_pred, n, E);
+    std::vector<char> nkeep(E, 0);
+    for (int e : pred) nkeep[e] = 1;
+    bool any = false;
+    CopyTimer t{};
+    for (int e : pred) {
+      if (N.expert_slot[e] >= 0) continue;
+      int h = -1;
+      if (P->store) {
+        h = host_find(P, nl, e);
+        if (h < 0) {
+          host_fetch(P, nl, e, true);  // -1 (no blob to replace): the prediction is only a hint
+          continue;
+        }
+        if (!ef::store_done(&P->host_ticket[h]) || P->host_ticket[h].err.load()) continue;
+        host_touch(P, h);
+        P->st.host_hits++;
+      }
+      const int sl = take_slot(P, nl, nkeep);
+      if (sl < 0) break;  // no free slot: the prediction is only a hint
+      if (!any) {
+        copies_begin(P, 1, N);
+        t = timer_begin(P, P->lane[1].stream);
+        any = true;
+      }
+      if ((s = copy_expert(P, 1, nl, e, sl, h))) return s;
+      N.staged[e] = 1;
+      P->st.copies_prefetch++;
+    }
+    if (any) {
+      if ((s = flush_stage(P, 1))) return s;
+      cudaEventRecord(t.b, P->lane[1].stream);
+      P->timers.push_back(t);
+      cudaEventRecord(N.ready[1], P->lane[1].stream);
+      N.has_ready[1] = true;
+    }
+  }
   return EF_OK;
 }
 
