@@ -296,6 +296,7 @@ struct CopyTimer {
 // scales then biases (9 arrays, each 16-byte aligned); array a of blob i goes
 // to dst[a] + slot[i] * bytes[a].
 constexpr int kScatterMax = 16;
+constexpr int kScatterThreads = 64;
 struct ScatterParams {
   const uint8_t* stage;
   size_t blob_bytes;
@@ -305,7 +306,7 @@ struct ScatterParams {
   size_t off[10];   // array a starts at off[a] of a blob (16-byte aligned), off[9] = used bytes
   size_t size[9];   // bytes of array a (its stride between slots)
 };
-__global__ void pool_scatter_kernel(const __grid_constant__ ScatterParams p) {
+__global__ void __launch_bounds__(kScatterThreads) pool_scatter_kernel(const __grid_constant__ ScatterParams p) {
   const int i = blockIdx.y;
   if (i >= p.n) return;
   const uint4* src = reinterpret_cast<const uint4*>(p.stage + (size_t)i * p.blob_bytes);
@@ -464,8 +465,11 @@ ef_status flush_stage(ef_slot_pool* P, int ln) {
   auto& C = P->lane[ln];
   if (C.n_staged == 0) return EF_OK;
   C.scat.n = C.n_staged;
-  dim3 grid(64, C.n_staged);
-  ef::pool_scatter_kernel<<<grid, 256, 0, C.stream>>>(C.scat);
+  // 64-thread blocks (2,048 registers) fit beside two decode-GEMV CTAs on an
+  // SM (4,096 registers left), so the scatter runs while the experts of the
+  // current layer compute instead of waiting for them to finish
+  dim3 grid(256, C.n_staged);
+  ef::pool_scatter_kernel<<<grid, ef::kScatterThreads, 0, C.stream>>>(C.scat);
   C.n_staged = 0;
   if (cudaGetLastError() != cudaSuccess) return fail(EF_ERR_CUDA, "slot scatter launch failed");
   return EF_OK;
