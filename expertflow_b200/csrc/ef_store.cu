@@ -269,7 +269,9 @@ ef_status ef_store_open(const ef_moe_cfg* cfg, int n_layers, const char* const* 
   ef_status s = check_cfg(cfg);
   if (s) return s;
   if (n_layers <= 0 || n_files <= 0 || !paths || !arrays) return fail(EF_ERR_INVALID, "need layers, files and arrays");
-  if (n_readers <= 0) n_readers = std::max(1, std::min(8, (int)std::thread::hardware_concurrency()));
+  // readers block in pread: many more than cores keep a disk's queue full (a
+  // lone expert read measured 0.6 GB/s with 8 readers, 1.0-1.2 GB/s with 32-64)
+  if (n_readers <= 0) n_readers = std::max(8, std::min(64, 4 * (int)std::thread::hardware_concurrency()));
   if (n_readers > 64) return fail(EF_ERR_INVALID, "n_readers must be <= 64");
   ef_expert_store* S = new ef_expert_store();
   S->cfg = *cfg;

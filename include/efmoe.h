@@ -351,7 +351,7 @@ typedef struct {
   double file_bytes;   /* bytes read so far */
 } ef_store_info;
 /* Opens n_files files (read-only; direct != 0: O_DIRECT, page cache bypassed)
- * and starts n_readers reader threads (<= 0: min(8, cores)).  arrays:
+ * and starts n_readers reader threads (<= 0: 4 x cores, between 8 and 64).  arrays:
  * [n_layers][9] entries in the order gate w, s, b, up w, s, b, down w, s, b;
  * every expert's range is checked against the file size here.  Host only: no
  * CUDA call. */
