@@ -414,3 +414,48 @@ def make_host_layers(spec: MoESpec, n_layers: int, seed: int = 0, device="cuda")
         out.append({k: tuple(a.cpu() for a in d[k]) for k in ("gate", "up", "down")})
         del d
     return out
+
+
+def _main(argv=None) -> None:
+    """A streamed decode for profiling: `layers` Qwen3-30B-A3B-shaped layers,
+    25 % of each layer's experts in HBM, Zipf(1.1)-biased routing, one-layer
+    lookahead; prints the time per token.
+    python -m expertflow_b200.pool --layers 8 --steps 24"""
+    import argparse
+
+    from .moe import MoEGate
+    from .spec import WORKLOADS
+    from .synthetic import make_x_torch
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=24)
+    ap.add_argument("--lookahead", type=int, default=1)
+    a = ap.parse_args(argv)
+    spec = WORKLOADS["qwen3-30b-a3b-moe"]
+    dev = torch.device("cuda", 0)
+    host = make_host_layers(spec, a.layers, seed=3000, device=dev)
+    bias = torch.from_numpy(zipf_layer_bias(a.layers, spec.n_experts, 1.1, seed=42)).to(dev)
+    gates = []
+    for layer in range(a.layers):
+        g = torch.Generator(device=dev)
+        g.manual_seed(77 + layer)
+        gw = (torch.randn((spec.n_experts, spec.hidden), generator=g, device=dev) * spec.gate_std).to(torch.float16)
+        gates.append(MoEGate(gw, spec.top_k, "softmax", True, e_score_correction_bias=bias[layer].contiguous()))
+    pl = ExpertSlotPool(spec, host, budget=spec.n_experts // 4, headroom=spec.top_k)
+    rs = [make_x_torch(spec, 1, seed=5000 + t, device=dev).float().contiguous() for t in range(a.steps)]
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for r in rs:
+        pl.decode_step(r, gates, lookahead=bool(a.lookahead))
+    e1.record()
+    torch.cuda.synchronize()
+    st = pl.stats()
+    print(f"{a.layers} layers x {a.steps} tokens: {e0.elapsed_time(e1) / a.steps:.3f} ms per token, "
+          f"hit rate {st['hit_rate']:.3f}, {st['copies_prefetch']} prefetched, {st['copies_sync']} on demand")
+    pl.close()
+
+
+if __name__ == "__main__":
+    _main()
