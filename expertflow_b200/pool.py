@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import weakref
 from dataclasses import replace
 from typing import Optional, Sequence
 
@@ -185,6 +186,7 @@ class ExpertStore:
         L.check(L.lib().ef_store_open(ctypes.byref(self.cfg), self.n_layers, ctypes.cast(cpaths, ctypes.c_void_p),
                                       len(self.paths), arr, int(n_readers), int(bool(direct)), ctypes.byref(h)))
         self._h = h
+        self._pools = weakref.WeakSet()  # pools reading through this store (closed before it)
 
     @classmethod
     def from_safetensors(cls, path_or_index, layers: Optional[Sequence[int]] = None, spec: Optional[MoESpec] = None,
@@ -246,6 +248,10 @@ class ExpertStore:
         return out
 
     def close(self) -> None:
+        """Close the store; pools still open over it are closed first (a pool
+        reads through its store until it is destroyed)."""
+        for pl in list(getattr(self, "_pools", ())):
+            pl.close()
         if getattr(self, "_h", None):
             L.lib().ef_store_close(self._h)
             self._h = None
@@ -299,8 +305,11 @@ class ExpertSlotPool:
         h = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             if store is not None:
+                if not getattr(store, "_h", None):
+                    raise ValueError("the store is closed")
                 L.check(L.lib().ef_pool_create_from_store(ctypes.byref(self.cfg), ctypes.byref(self.pool_cfg),
                                                           store._h, int(host_blobs), ctypes.byref(h)))
+                store._pools.add(self)
             else:
                 L.check(L.lib().ef_pool_create(ctypes.byref(self.cfg), ctypes.byref(self.pool_cfg), self._qw["gate"],
                                                self._qw["up"], self._qw["down"], ctypes.byref(h)))

@@ -327,3 +327,21 @@ def test_pool_over_store_failed_read_leaves_pool_usable(P, tmp_path):
     assert moe.device_error() == 0
     pool.close()
     store.close()
+
+
+def test_store_close_closes_its_pools_first(P, tmp_path):
+    """A pool reads through its store until it is destroyed, so closing the
+    store closes the pools still open over it first."""
+    _write_model(str(tmp_path), SPEC, 1, n_shards=1)
+    store = P.ExpertStore.from_safetensors(str(tmp_path))
+    order = []
+
+    class FakePool:  # stands in for an ExpertSlotPool (creating one needs a GPU)
+        def close(self):
+            order.append(("pool", bool(store._h)))
+
+    fake = FakePool()
+    store._pools.add(fake)
+    store.close()
+    assert order == [("pool", True)] and store._h is None
+    store.close()  # idempotent
