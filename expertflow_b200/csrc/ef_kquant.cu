@@ -494,9 +494,7 @@ ef_status ef_kquant_matmul(const void* x, int act_dtype, int T, const void* bloc
   const int nt = (T + 7) / 8;
   const int n_tok_k = (nt <= 2 ? nt : 4) * 8;  // token rows the kernel reads (zero beyond T)
   uint16_t* xp = static_cast<uint16_t*>(workspace);
-  int dev = 0, n_sm = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+  const int n_sm = sm_count();
   const int pgrid = (int)std::min<long long>(((long long)n_tok_k * K + 255) / 256, (long long)n_sm * 16);
   const uint16_t* xs = static_cast<const uint16_t*>(x);
   const int bf = act_dtype == EF_DT_BF16;
