@@ -115,6 +115,9 @@ SIGNATURES = {
     "ef_moe_forward_noalloc": (_I, [_CFGP, _P, _I, _P, _P, _QW, _QW, _QW, _QWP, _QWP, _QWP, _P, _P, _P, _P]),
     "ef_router_workspace_size": (_SZ, [_CFGP, _I]),
     "ef_router_topk": (_I, [_CFGP, _P, _I, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "ef_permute_workspace_size": (_SZ, [_I, _I, _I, _I]),
+    "ef_permute": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _SZ, _P]),
+    "ef_combine": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _P]),
     "ef_experts_workspace_size": (_SZ, [_CFGP, _I]),
     "ef_moe_experts_forward": (_I, [_CFGP, _P, _I, _P, _QW, _QW, _QW, _QWP, _QWP, _QWP, _P, _P, _SZ, _P]),
     "ef_quantized_matmul_workspace_size": (_SZ, [_I, _I, _I]),

@@ -4,6 +4,7 @@
 // maps of the weight stacks and enqueues the kernel sequence on the caller's
 // stream:  router logits -> top-k -> permute -> activation prep -> gate/up
 // (+SwiGLU) -> down -> combine.  Nothing here allocates device memory.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -240,16 +241,19 @@ ef_status encode_gemm_act_map(CUtensorMap* m, const uint16_t* act, long long row
   return EF_OK;
 }
 
+// SM count of the current device, cached per device index (host threads may
+// race on a first fill; they store the same value).
 int sm_count() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int n = 0;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cache[dev] = n > 0 ? n : 148;
+    if (n <= 0) n = 148;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return n;
 }
 
 // ---- workspace carving
@@ -537,6 +541,56 @@ ef_status ef_router_topk(const ef_moe_cfg* cfg, const void* x, int T, const void
                                cfg->router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg->n_group : 1, cfg->topk_group,
                                cfg->router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg->routed_scaling : 1.0f, inds,
                                weights, st));
+  return EF_OK;
+}
+
+size_t ef_permute_workspace_size(int n_entries, int n_experts, int n_shared_rows, int seg_rows) {
+  if (n_entries < 0 || n_experts < 1 || n_shared_rows < 0 || seg_rows < 1) return 0;
+  Carver c{nullptr};
+  const int max_segs = (n_entries + n_shared_rows + seg_rows - 1) / seg_rows + n_experts + 3;
+  c.take<int>(max_segs);
+  c.take<int>(max_segs);
+  c.take<int>(max_segs);
+  c.take<int>(1);
+  return c.off + 256;
+}
+
+ef_status ef_permute(const int32_t* entries, int n_entries, int k, int n_experts, int n_shared_rows, int seg_rows,
+                     int32_t* counts, int32_t* offsets, int32_t* row_src, int32_t* inv, void* workspace,
+                     size_t ws_bytes, void* stream) {
+  if (n_entries < 0 || k < 1 || n_experts < 1 || n_experts > 512 || n_shared_rows < 0 || seg_rows < 1)
+    return fail(EF_ERR_INVALID, "bad permute arguments (n_entries %d, k %d, n_experts %d, shared rows %d, seg %d)",
+                n_entries, k, n_experts, n_shared_rows, seg_rows);
+  if (n_entries % k) return fail(EF_ERR_INVALID, "n_entries must be a multiple of k");
+  if (n_entries + n_shared_rows == 0) return EF_OK;
+  if (!entries || !counts || !offsets || !row_src || !inv) return fail(EF_ERR_INVALID, "null pointer");
+  if (!workspace || ws_bytes < ef_permute_workspace_size(n_entries, n_experts, n_shared_rows, seg_rows))
+    return fail(EF_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver c{static_cast<uint8_t*>(workspace)};
+  const int max_segs = (n_entries + n_shared_rows + seg_rows - 1) / seg_rows + n_experts + 3;
+  PermBufs pb;
+  pb.counts = counts;
+  pb.offsets = offsets;
+  pb.row_src = row_src;
+  pb.inv = inv;
+  pb.seg_expert = c.take<int>(max_segs);
+  pb.seg_row0 = c.take<int>(max_segs);
+  pb.seg_nrows = c.take<int>(max_segs);
+  pb.n_seg = c.take<int>(1);
+  EF_LAUNCH("permute", launch_permute(entries, n_entries, k, n_experts, n_shared_rows, seg_rows, pb, st));
+  return EF_OK;
+}
+
+ef_status ef_combine(const float* rows, const int32_t* inv, const float* wts, int T, int k, int H, int shared_base,
+                     void* y, int out_dtype, void* stream) {
+  if (T < 0 || k < 1 || H <= 0 || H % 4) return fail(EF_ERR_INVALID, "bad combine shape (T %d, k %d, H %d)", T, k, H);
+  if (out_dtype < EF_DT_BF16 || out_dtype > EF_DT_F32) return fail(EF_ERR_UNSUPPORTED, "out_dtype");
+  if (T == 0) return EF_OK;
+  if (!rows || !inv || !y) return fail(EF_ERR_INVALID, "null pointer");
+  if (!aligned16(rows) || !aligned16(y)) return fail(EF_ERR_INVALID, "rows and y must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  EF_LAUNCH("combine", launch_combine(rows, inv, wts, T, k, H, shared_base, y, out_dtype, st));
   return EF_OK;
 }
 

@@ -10,6 +10,8 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <atomic>
+
 #include "efmoe_internal.h"
 
 #define EF_DEV __device__ __forceinline__
@@ -99,6 +101,19 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Raises a kernel's dynamic shared-memory limit once per device (the attribute
+// belongs to the device's context); host threads may race on a first call,
+// which only repeats the idempotent attribute call.
+template <typename Kern>
+inline cudaError_t set_max_smem_once(Kern* kern, int bytes, std::atomic<bool> (&done)[64]) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  if (dev >= 0 && dev < 64 && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev].store(true, std::memory_order_release);
+  return e;
 }
 
 // ---------------------------------------------------------------- TMA / bulk copies

@@ -9,10 +9,12 @@
 //
 // The scratch lives in one file-scope __device__ array of a fixed size
 // (EF_NOALLOC_SCRATCH_BYTES); every GPU that loads the library holds it until
-// the process exits.  Host code never dereferences the array's name: the
-// first call on each device resolves the array's device address with
-// cudaGetSymbolAddress (with that device current) and caches it, so the first
-// call per device should come before any stream capture.  Every call shares
+// the process exits, whether or not this entry point is ever called (the
+// array is part of the library's one module).  Host code never dereferences
+// the array's name: the first call on each device resolves the array's device
+// address with cudaGetSymbolAddress (with that device current) and caches it
+// for that device's context, so the first call per device should come before
+// any stream capture.  Every call shares
 // the array and it keeps the previous call's contents: nothing in it needs to
 // start at zero (each region the kernels read is written earlier in the same
 // call), but calls that overlap on the GPU (other streams, other host threads)
@@ -26,30 +28,67 @@ static __device__ __align__(256) unsigned char g_ef_noalloc_scratch[EF_NOALLOC_S
 
 namespace {
 
+// The array's address belongs to the CUDA context that loaded the module: a
+// cudaDeviceReset (or a released and re-created primary context) loads it
+// again, possibly at another address.  Each device's cached address is kept
+// with the unique id of the context it was resolved in (cuCtxGetId) and
+// resolved again when the current context's id differs.
+typedef CUresult (*PFN_ctxGetCurrent_t)(CUcontext*);
+typedef CUresult (*PFN_ctxGetId_t)(CUcontext, unsigned long long*);
+
 struct NoallocSlot {
   void* ptr = nullptr;
+  unsigned long long ctx_id = 0;
   bool ready = false;
 };
 
 std::mutex g_noalloc_mu;
 NoallocSlot g_noalloc[64];
 
-// Device address of the scratch array on the current device (set up once per device).
+// Unique id of the calling thread's current context (0 when there is none or
+// the driver lacks the call).
+unsigned long long current_ctx_id() {
+  static PFN_ctxGetCurrent_t get_cur = nullptr;
+  static PFN_ctxGetId_t get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<PFN_ctxGetCurrent_t>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_ctxGetId_t>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_cur && get_id && get_cur(&ctx) == CUDA_SUCCESS && ctx && get_id(ctx, &id) == CUDA_SUCCESS) return id;
+  return 0;
+}
+
+// Device address of the scratch array on the current device (set up once per
+// device and context).
 ef_status noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(EF_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return fail(EF_ERR_UNSUPPORTED, "device index %d out of range", dev);
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc[dev].ready) {
+  NoallocSlot& slot = g_noalloc[dev];
+  const unsigned long long id = current_ctx_id();
+  if (!slot.ready || id == 0 || id != slot.ctx_id) {
     void* p = nullptr;
+    // also makes the device's primary context current when none is yet
     e = cudaGetSymbolAddress(&p, g_ef_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr)
       return fail(EF_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
-    g_noalloc[dev].ptr = p;
-    g_noalloc[dev].ready = true;
+    slot.ptr = p;
+    slot.ctx_id = current_ctx_id();
+    slot.ready = slot.ctx_id != 0;  // without a context id, resolve on every call
   }
-  *out = g_noalloc[dev].ptr;
+  *out = slot.ptr;
   return EF_OK;
 }
 

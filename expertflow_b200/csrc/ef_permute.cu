@@ -233,11 +233,9 @@ cudaError_t launch_permute(const int* entries, int n_ent, int k, int n_exp, int 
                            const PermBufs& pb, cudaStream_t st) {
   const int nb = n_exp + (n_sh > 0 ? 1 : 0);
   size_t smem = sizeof(int) * (size_t)kPermWarps * nb;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    attr_set = true;
-  }
+  static std::atomic<bool> attr_set[64];
+  const cudaError_t e = set_max_smem_once(permute_kernel, 160 * 1024, attr_set);
+  if (e != cudaSuccess) return e;
   return launch_pdl(permute_kernel, 1, kPermThreads, smem, st, entries, n_ent, k, n_exp, n_sh, seg_chunk, pb);
 }
 

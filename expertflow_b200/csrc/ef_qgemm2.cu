@@ -491,15 +491,8 @@ size_t qgemm2_smem_required(int bits) { return g2_smem_bytes(bits); }
 template <int BITS, int MODE>
 static cudaError_t launch_qgemm2_t(const GemmParams& p, int n_sm, cudaStream_t st) {
   const size_t smem = g2_smem_bytes(BITS);
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(qgemm2_kernel<BITS, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
+  static std::atomic<bool> attr_set[64];
+  if (const cudaError_t e = set_max_smem_once(qgemm2_kernel<BITS, MODE>, (int)smem, attr_set)) return e;
   qgemm2_kernel<BITS, MODE><<<(n_sm / 2) * 2, kG2Threads, smem, st>>>(p);
   return cudaGetLastError();
 }

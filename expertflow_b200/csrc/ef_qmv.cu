@@ -647,15 +647,8 @@ static cudaError_t launch_qmv_t(const QmvParams& p_in, int n_sm, cudaStream_t st
   p.n_stages = qmv_pick<BITS, MODE>(p.K, chunked, &per_sm, &p.n_slots);
   if (p.n_stages == 0) return cudaErrorInvalidValue;
   const size_t smem = qmv_smem_bytes<BITS, MODE>(p.K, p.n_stages, p.n_slots, chunked);
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(qmv_kernel<BITS, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         227 * 1024);
-    if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
+  static std::atomic<bool> attr_set[64];
+  if (const cudaError_t e = set_max_smem_once(qmv_kernel<BITS, MODE>, 227 * 1024, attr_set)) return e;
   return launch_pdl(qmv_kernel<BITS, MODE>, n_sm * per_sm, kQmvThreads, smem, st, p);
 }
 

@@ -388,6 +388,38 @@ def dequantize(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, grou
     return out
 
 
+def permute(entries: torch.Tensor, k: int, n_experts: int, n_shared_rows: int = 0, seg_rows: int = 8) -> dict:
+    """Stable counting sort of routed entries by expert (ef_permute): counts,
+    offsets, row_src (token of each sorted row) and inv (sorted row of each
+    entry), as the expert kernels consume them."""
+    _need_cuda(entries)
+    n = entries.numel()
+    nb = n_experts + (1 if n_shared_rows > 0 else 0)
+    dev = entries.device
+    out = {"counts": torch.empty(nb, dtype=torch.int32, device=dev),
+           "offsets": torch.empty(nb + 1, dtype=torch.int32, device=dev),
+           "row_src": torch.empty(n + n_shared_rows, dtype=torch.int32, device=dev),
+           "inv": torch.empty(n, dtype=torch.int32, device=dev)}
+    nbytes = L.lib().ef_permute_workspace_size(n, n_experts, n_shared_rows, seg_rows)
+    ws = workspace(nbytes, dev)
+    L.check(L.lib().ef_permute(entries.data_ptr(), n, k, n_experts, n_shared_rows, seg_rows,
+                               out["counts"].data_ptr(), out["offsets"].data_ptr(), out["row_src"].data_ptr(),
+                               out["inv"].data_ptr(), ws.data_ptr(), ws.numel(), _stream_ptr(dev)))
+    return out
+
+
+def combine(rows: torch.Tensor, inv: torch.Tensor, wts: Optional[torch.Tensor], T: int, k: int,
+            shared_base: int = -1, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """y[t] = sum_j wts[t, j] * rows[inv[t*k + j]] in j order (+ rows[shared_base + t]) (ef_combine)."""
+    _need_cuda(rows, inv, wts)
+    H = rows.shape[1]
+    y = torch.empty((T, H), dtype=out_dtype, device=rows.device)
+    dt = {torch.float32: L.EF_DT_F32, torch.float16: L.EF_DT_F16, torch.bfloat16: L.EF_DT_BF16}[out_dtype]
+    L.check(L.lib().ef_combine(rows.data_ptr(), inv.data_ptr(), wts.data_ptr() if wts is not None else None, T, k,
+                               H, shared_base, y.data_ptr(), dt, _stream_ptr(rows.device)))
+    return y
+
+
 def device_error(device=None) -> int:
     """Read and clear the device error word (0 = none)."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)

@@ -26,6 +26,8 @@
  *   ef_dequantize         mx.dequantize(w, s, b, group_size, bits)         ef_cpu_fast.py:70-75
  *   ef_gather_qmm         QuantizedSwitchLinear.__call__(x, indices)        ef_engine_v4.py:52-64
  *   ef_moe_experts_forward  per-(row, expert) SwiGLU loop                  ef_engine.py:678-695
+ *   ef_permute            unique-expert grouping of the routed entries     ef_engine.py:640-647
+ *   ef_combine            score-weighted sum over k (+ shared)             ef_engine.py:695-703
  *   ef_slotpool_*         FrequencyWeightedCache get/put/trim              ef_engine.py:48-104
  *                         + mmap page-in of misses                        ef_engine.py:650-675
  *   ef_kquant_*           GGUF Q2_K/Q3_K/Q4_K decode (+ GEMV)              ef_deepseek_mmap.py:330-378,655-773
@@ -147,6 +149,28 @@ size_t ef_router_workspace_size(const ef_moe_cfg* cfg, int T);
 ef_status ef_router_topk(const ef_moe_cfg* cfg, const void* x, int T, const void* gate_w, const float* e_bias,
                          int32_t* inds, float* weights, float* logits_out, void* workspace,
                          size_t workspace_bytes, void* stream);
+
+/* ---- permutation and combine ------------------------------------------------ */
+/* Stable counting sort of routed entries by expert (order (expert, entry)),
+ * atomic-free.  entries [n_entries] hold expert ids in [0, n_experts); entry i
+ * belongs to token i / k.  n_shared_rows > 0 adds bin n_experts holding rows
+ * for tokens 0..n_shared_rows-1 (the shared expert) after all routed rows.
+ * Outputs: counts [n_bins] rows per bin, offsets [n_bins + 1] first sorted row
+ * of each bin, row_src [n_entries + n_shared_rows] token of each sorted row,
+ * inv [n_entries] sorted row of each entry; n_bins = n_experts (+1 with shared
+ * rows).  The workspace holds the segments of <= seg_rows rows the expert
+ * kernels consume.  Replaces the unique-expert grouping of ef_engine.py:640-647
+ * and expertflow_final.py:94-113. */
+size_t ef_permute_workspace_size(int n_entries, int n_experts, int n_shared_rows, int seg_rows);
+ef_status ef_permute(const int32_t* entries, int n_entries, int k, int n_experts, int n_shared_rows, int seg_rows,
+                     int32_t* counts, int32_t* offsets, int32_t* row_src, int32_t* inv, void* workspace,
+                     size_t workspace_bytes, void* stream);
+/* y[t, :] = sum_j wts[t, j] * rows[inv[t*k + j], :] in j order (wts NULL: unit
+ * weights), + rows[shared_base + t, :] when shared_base >= 0; rows fp32
+ * [*, H], y [T, H] in out_dtype (EF_DT_*).  Replaces the score-weighted sum of
+ * ef_engine.py:695-703. */
+ef_status ef_combine(const float* rows, const int32_t* inv, const float* wts, int T, int k, int H, int shared_base,
+                     void* y, int out_dtype, void* stream);
 
 /* ---- experts on routed rows --------------------------------------------- */
 /* Rows x[N, H] (act dtype), row_expert[N] in [0, n_experts) (or n_experts for

@@ -1,6 +1,7 @@
 """Generate tests/golden/belady_trace.npz by executing the REFERENCE's own
-``BeladyExpertCache`` (ef_engine.py:163-279; read from the reference checkout,
-default /root/reference, through ``mlx_shim`` because ef_engine imports MLX).
+``BeladyExpertCache`` (ef_engine.py:163-279; read from a reference checkout
+given by --reference or the EF_REFERENCE environment variable, through
+``mlx_shim`` because ef_engine imports MLX).
 
 The access trace is the one in ``cache_trace.npz`` (the reference's
 SimulatedMoERouter Zipf trace, 4 layers x 128 experts, 160 tokens).  Per token
@@ -20,7 +21,7 @@ then ``trim()`` and ``end_token()``, the order of the reference's decode loop
 Recorded: per access hit/miss, per token the eviction count and the resident
 set, and the predictor weights.
 
-Run:  python tests/golden/make_belady_golden.py [--reference /root/reference]
+Run:  python tests/golden/make_belady_golden.py --reference <reference checkout>
 """
 from __future__ import annotations
 
@@ -81,7 +82,9 @@ def weights(p):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("EF_REFERENCE"),
+                    required="EF_REFERENCE" not in os.environ,
+                    help="reference checkout to import (default: $EF_REFERENCE)")
     args = ap.parse_args()
     sys.dont_write_bytecode = True
     import mlx_shim

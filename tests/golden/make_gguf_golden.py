@@ -1,6 +1,6 @@
 """Generate tests/golden/kquant_gguf.npz by executing the REFERENCE's own GGUF
-code (ef_deepseek_mmap.py, read from the reference checkout; default
-/root/reference):
+code (ef_deepseek_mmap.py, read from a reference checkout given by
+--reference or the EF_REFERENCE environment variable):
 
 * ``dequant_q2_k_fast`` / ``dequant_q3_k_fast`` / ``dequant_q4_k_fast``
   (ef_deepseek_mmap.py:330-378, 655-773) on seeded K-quant blocks -- typical
@@ -13,7 +13,7 @@ code (ef_deepseek_mmap.py, read from the reference checkout; default
   ``expertflow_b200.gguf.write_gguf``: parsed tensor infos, each expert's raw
   byte range and a digest of each expert's dequantised matrices.
 
-Run:  python tests/golden/make_gguf_golden.py [--reference /root/reference]
+Run:  python tests/golden/make_gguf_golden.py --reference <reference checkout>
 """
 from __future__ import annotations
 
@@ -87,7 +87,9 @@ def sha(b) -> str:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("EF_REFERENCE"),
+                    required="EF_REFERENCE" not in os.environ,
+                    help="reference checkout to import (default: $EF_REFERENCE)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import ef_deepseek_mmap as R

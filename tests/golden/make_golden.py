@@ -1,5 +1,6 @@
 """Generate the golden fixtures in this directory by executing the REFERENCE's
-own code (read from the reference checkout; default /root/reference).
+own code (read from a reference checkout given by --reference or the
+EF_REFERENCE environment variable).
 
 * ``moe_*.npz`` -- ``streaming_moe_forward`` (ef_engine.py:598-706) run on
   seeded synthetic layers through ``mlx_shim`` (numpy stand-ins for the MLX ops
@@ -11,7 +12,7 @@ own code (read from the reference checkout; default /root/reference).
 * ``cache_trace.npz`` -- ``FrequencyWeightedCache`` (ef_engine.py:48-104) driven
   by the reference's ``SimulatedMoERouter`` Zipf trace (ef_integrated_engine.py:44-118).
 
-Run:  python tests/golden/make_golden.py [--reference /root/reference]
+Run:  python tests/golden/make_golden.py --reference <reference checkout>
 The fixtures store outputs plus a digest of the regenerated inputs; the inputs
 themselves are regenerated from their seeds by expertflow_b200.synthetic.
 """
@@ -167,7 +168,9 @@ def gen_cache(ef_engine, ef_integrated_engine, out_dir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("EF_REFERENCE"),
+                    required="EF_REFERENCE" not in os.environ,
+                    help="reference checkout to import (default: $EF_REFERENCE)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     sys.dont_write_bytecode = True

@@ -150,9 +150,11 @@ def _oracle_sampled(spec, layer_t, xb, inds, wts, tokens):
 
 
 @pytest.mark.parametrize("spec,T", [(QWEN3_30B_A3B, 1), (QWEN3_30B_A3B, 8), (QWEN3_30B_A3B, 32),
-                                    (QWEN3_30B_A3B, 64), (DEEPSEEK_V3, 1), (DEEPSEEK_V3, 64),
+                                    (QWEN3_30B_A3B, 64), (DEEPSEEK_V3, 1), (DEEPSEEK_V3, 32), (DEEPSEEK_V3, 64),
                                     (DEEPSEEK_V3, 256), (MIXTRAL_SMALL, 1)])
-def test_full_size_layer_sampled_parity(spec, T):
+def test_full_size_layer_parity(spec, T):
+    """Every token of a full-size decode batch against the oracle (routing bit
+    for bit, FFN output within the tolerance)."""
     moe = _moe()
     layer = _torch_layer(spec, seed=11)
     m = moe.MoELayer.from_arrays(spec, layer)
@@ -168,10 +170,61 @@ def test_full_size_layer_sampled_parity(spec, T):
     i_ref, w_ref = O.route(lg, _spec_router(spec), eb)
     np.testing.assert_array_equal(inds.cpu().numpy(), i_ref)
     np.testing.assert_array_equal(wts.cpu().numpy().view(np.uint32), w_ref.view(np.uint32))
-    rng = np.random.default_rng(T)
-    tokens = np.sort(rng.choice(T, size=min(T, 6), replace=False))
+    tokens = np.arange(T)
     y_ref = _oracle_sampled(spec, layer, xb, i_ref, w_ref, tokens)
-    assert_ffn_close(y.cpu().numpy()[tokens], y_ref, what=f"{spec.hidden}/{T}")
+    assert_ffn_close(y.cpu().numpy(), y_ref, what=f"{spec.hidden}/{T}")
+    del m, layer
+    torch.cuda.empty_cache()
+
+
+def test_permute_matches_numpy_counting_sort():
+    """ef_permute against a numpy stable sort, with ragged expert counts, empty
+    experts, a shared bin and a maximal-size histogram."""
+    moe = _moe()
+    rng = np.random.default_rng(3)
+    for T, k, E, n_sh, seg in ((1, 1, 1, 0, 8), (37, 8, 128, 0, 8), (256, 8, 256, 256, 8), (4096, 8, 256, 0, 192),
+                               (1000, 4, 512, 1000, 192), (5, 2, 16, 5, 8)):
+        # skewed ids: a few hot experts, most empty
+        p = rng.zipf(1.3, size=T * k) % E
+        ents = p.astype(np.int32)
+        got = moe.permute(torch.from_numpy(ents).cuda(), k, E, n_sh, seg)
+        order = np.argsort(ents, kind="stable")
+        counts = np.bincount(ents, minlength=E)
+        nb = E + (1 if n_sh else 0)
+        c_ref = np.concatenate([counts, [n_sh]]) if n_sh else counts
+        off = np.concatenate([[0], np.cumsum(c_ref)])
+        inv = np.empty(T * k, np.int64)
+        inv[order] = np.arange(T * k)
+        row_src = np.concatenate([order // k, np.arange(n_sh)]) if n_sh else order // k
+        np.testing.assert_array_equal(got["counts"].cpu().numpy(), c_ref[:nb])
+        np.testing.assert_array_equal(got["offsets"].cpu().numpy(), off)
+        np.testing.assert_array_equal(got["inv"].cpu().numpy(), inv)
+        np.testing.assert_array_equal(got["row_src"].cpu().numpy(), row_src)
+
+
+def test_combine_matches_numpy_weighted_sum():
+    """ef_combine: the k-order weighted sum with a shared row, fp32 and bf16 out."""
+    moe = _moe()
+    rng = np.random.default_rng(4)
+    for T, k, H, sh in ((1, 8, 2048, False), (33, 8, 7168, True), (300, 2, 1024, False)):
+        n = T * k + (T if sh else 0)
+        rows = rng.standard_normal((n, H)).astype(np.float32)
+        inv = rng.permutation(T * k).astype(np.int32)
+        w = rng.random(T * k).astype(np.float32)
+        r = torch.from_numpy(rows).cuda()
+        y = moe.combine(r, torch.from_numpy(inv).cuda(), torch.from_numpy(w).cuda(), T, k,
+                        T * k if sh else -1).cpu().numpy()
+        acc = rows[inv].reshape(T, k, H) * w.reshape(T, k, 1)
+        ref = acc[:, 0].astype(np.float32)
+        for j in range(1, k):
+            ref = ref + acc[:, j]
+        if sh:
+            ref = ref + rows[T * k:]
+        # the kernel contracts each multiply-add (one rounding), numpy rounds twice
+        np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-5)
+        yb = moe.combine(r, torch.from_numpy(inv).cuda(), torch.from_numpy(w).cuda(), T, k,
+                         T * k if sh else -1, out_dtype=torch.bfloat16)
+        assert torch.equal(yb, torch.from_numpy(y).cuda().to(torch.bfloat16))
 
 
 def test_layer_deterministic_and_repeatable():
@@ -318,7 +371,21 @@ def test_prefill_deepseek_v3_8bit_sampled():
     lg = O.c_router_logits(xb, True, layer["gate_w"].cpu().numpy().view(np.uint16), False)
     i_ref, w_ref = O.route(lg, _spec_router(spec), layer["e_bias"].cpu().numpy())
     np.testing.assert_array_equal(inds.cpu().numpy(), i_ref)
-    tokens = np.array([0, 1, 777, 2048, 4094, 4095])
+    # every token routed to the two most-loaded experts (more rows than one
+    # 192-row GEMM segment holds, so each spans two segments), plus the first
+    # and last token of eight other experts and the batch's first and last
+    ent = i_ref.reshape(-1)
+    counts = np.bincount(ent, minlength=spec.n_experts)
+    top2 = np.argsort(-counts, kind="stable")[:2]
+    assert (counts[top2] > 192).all(), counts[top2]
+    toks = set()
+    for e in top2:
+        toks.update((np.nonzero(ent == e)[0] // spec.top_k).tolist())
+    for e in np.nonzero(counts)[0][:: max(1, len(np.nonzero(counts)[0]) // 8)][:8]:
+        te = np.nonzero(ent == e)[0] // spec.top_k
+        toks.update((int(te[0]), int(te[-1])))
+    toks.update((0, T - 1))
+    tokens = np.array(sorted(toks))
     y_ref = _oracle_sampled(spec, layer, xb, i_ref, w_ref, tokens)
     assert_ffn_close(y.cpu().numpy()[tokens], y_ref, what="prefill 8-bit")
     del m, layer

@@ -48,6 +48,8 @@ def test_noalloc_matches_workspace_entry_point_twice(which):
         rc = _call_noalloc(L, m, x, y, inds, wts)
         assert rc == 0, L.lib().ef_last_error_message()
         torch.cuda.synchronize()
+        # the same kernels on the same inputs: identical, not merely close
+        assert torch.equal(y, y_ref), f"noalloc call {call} differs from ef_moe_forward"
         assert_ffn_close(y.cpu().numpy(), y_ref.cpu().numpy(), what=f"noalloc call {call}")
         inds2 = torch.empty_like(inds)
         m(x, inds_out=inds2)
