@@ -128,6 +128,12 @@ SIGNATURES = {
     "ef_ep_dispatch_workspace_size": (_SZ, [_CFGP, _I]),
     "ef_ep_dispatch": (_I, [_CFGP, _I, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "ef_ep_combine": (_I, [_CFGP, _P, _P, _P, _I, _I, _P, _P]),
+    "ef_ep_group_create": (_I, [_CFGP, _I, _I, _I, _I, _P]),
+    "ef_ep_group_handle": (_I, [_P, _P]),
+    "ef_ep_group_open": (_I, [_P, _P]),
+    "ef_ep_workspace_size": (_SZ, [_P, _I]),
+    "ef_ep_forward": (_I, [_P, _P, _I, _P, _P, _QW, _QW, _QW, _QWP, _QWP, _QWP, _P, _I, _P, _P, _P, _SZ, _P]),
+    "ef_ep_group_destroy": (_I, [_P]),
     "ef_policy_create": (_I, [_I, _I, ctypes.c_double, _P]),
     "ef_policy_get": (_I, [_P, ctypes.c_longlong]),
     "ef_policy_put": (None, [_P, ctypes.c_longlong]),

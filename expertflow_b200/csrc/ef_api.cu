@@ -27,7 +27,8 @@ cudaError_t launch_router_select(const float* logits, const float* e_bias, int T
 cudaError_t launch_permute(const int* entries, int n_ent, int k, int n_exp, int n_sh, int seg_chunk,
                            const PermBufs& pb, cudaStream_t st);
 cudaError_t launch_prep_act(const uint16_t* act, const int* row_src, int is_bf16, int n, int K, int bits,
-                            uint16_t* out, float* sums, cudaStream_t st);
+                            uint16_t* out, float* sums, cudaStream_t st, const int* n_dev = nullptr,
+                            int max_blocks = 0);
 cudaError_t launch_combine(const float* rows, const int* inv, const float* wts, int T, int k, int H, int sh_base,
                            void* out, int out_dtype, cudaStream_t st);
 cudaError_t launch_qmv(int bits, int mode, const QmvParams& p, int n_sm, cudaStream_t st, int min_segments = 0);

@@ -47,16 +47,19 @@ __device__ int block_exclusive_scan(int v, int* s_warp, int* total) {
   return r;
 }
 
-// entries: n_ent routed entries (expert id per entry; token = entry / k).
-// n_sh: rows of the shared bin (0 or T), bin index n_exp.
-__global__ void __launch_bounds__(kPermThreads) permute_kernel(const int* __restrict__ entries, int n_ent, int k,
-                                                               int n_exp, int n_sh, int seg_chunk, PermBufs pb) {
-  pdl_wait();
-  pdl_launch_next();
-  extern __shared__ int s_hist[];  // [kPermWarps][nb]
-  __shared__ int s_warp[32];
-  __shared__ int s_total;
-  const int nb = n_exp + (n_sh > 0 ? 1 : 0);
+// Stable counting sort of n_ent entries into bins by one CTA of kPermThreads
+// threads, without atomics: warps histogram their slice of the entries with
+// __match_any_sync leaders, one block scan gives each bin's first row and each
+// warp's base within it, the same warps scatter in entry order.  bin_of(j)
+// returns entry j's bin in [0, n_bin) (out-of-range ids are reported in the
+// device error word and sorted into bin 0); emit(j, pos) records that entry j
+// landed on sorted row pos.  n_sh > 0 appends bin n_bin with n_sh rows,
+// emit_shared(t, pos) for t < n_sh.  Writes pb.counts / offsets and segments of
+// at most seg_chunk rows.  s_hist: kPermWarps * (n_bin + 1) ints of shared memory.
+template <class BinOf, class Emit, class EmitShared>
+__device__ void counting_sort_cta(int n_ent, int n_bin, int n_sh, int seg_chunk, const PermBufs& pb, int* s_hist,
+                                  int* s_warp, int* s_total, BinOf bin_of, Emit emit, EmitShared emit_shared) {
+  const int nb = n_bin + (n_sh > 0 ? 1 : 0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < kPermWarps * nb; i += kPermThreads) s_hist[i] = 0;
   __syncthreads();
@@ -66,14 +69,14 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(const int* __rest
   int* hist = s_hist + warp * nb;
   // phase 1: per-warp histogram
   for (int base = beg; base < end; base += 32) {
-    int j = base + lane;
-    bool valid = j < end;
-    int e = valid ? entries[j] : -1;
-    if (valid && (e < 0 || e >= n_exp)) {
+    const int j = base + lane;
+    const bool valid = j < end;
+    int e = valid ? bin_of(j) : -1;
+    if (valid && (e < 0 || e >= n_bin)) {
       ef_set_error(kDevErrRange);
       e = 0;
     }
-    unsigned peers = __match_any_sync(0xffffffffu, e);
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
     if (valid && lane == __ffs(peers) - 1) hist[e] += __popc(peers);
     __syncwarp();
   }
@@ -82,21 +85,21 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(const int* __rest
   int cnt = 0;
   const int b = threadIdx.x;
   if (b < nb) {
-    if (b < n_exp) {
+    if (b < n_bin) {
       for (int w = 0; w < kPermWarps; ++w) cnt += s_hist[w * nb + b];
     } else {
       cnt = n_sh;
     }
   }
-  int off = block_exclusive_scan(b < nb ? cnt : 0, s_warp, &s_total);
+  const int off = block_exclusive_scan(b < nb ? cnt : 0, s_warp, s_total);
   if (b < nb) {
     pb.counts[b] = cnt;
     pb.offsets[b] = off;
     if (b == nb - 1) pb.offsets[nb] = off + cnt;
-    if (b < n_exp) {
+    if (b < n_bin) {
       int run = off;
       for (int w = 0; w < kPermWarps; ++w) {
-        int c = s_hist[w * nb + b];
+        const int c = s_hist[w * nb + b];
         s_hist[w * nb + b] = run;
         run += c;
       }
@@ -105,86 +108,107 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(const int* __rest
   __syncthreads();
   // phase 3: stable scatter
   for (int base = beg; base < end; base += 32) {
-    int j = base + lane;
-    bool valid = j < end;
-    int e = valid ? entries[j] : -1;
-    if (valid && (e < 0 || e >= n_exp)) e = 0;
-    unsigned peers = __match_any_sync(0xffffffffu, e);
-    if (valid) {
-      int rank = __popc(peers & ((1u << lane) - 1u));
-      int pos = hist[e] + rank;
-      pb.row_src[pos] = j / k;
-      pb.inv[j] = pos;
-    }
+    const int j = base + lane;
+    const bool valid = j < end;
+    int e = valid ? bin_of(j) : -1;
+    if (valid && (e < 0 || e >= n_bin)) e = 0;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (valid) emit(j, hist[e] + __popc(peers & ((1u << lane) - 1u)));
     __syncwarp();
     if (valid && lane == __ffs(peers) - 1) hist[e] += __popc(peers);
     __syncwarp();
   }
   __syncthreads();
   if (n_sh > 0) {
-    const int base = pb.offsets[n_exp];
-    for (int t = threadIdx.x; t < n_sh; t += kPermThreads) pb.row_src[base + t] = t;
+    const int base = pb.offsets[n_bin];
+    for (int t = threadIdx.x; t < n_sh; t += kPermThreads) emit_shared(t, base + t);
   }
   // phase 4: segments of at most seg_chunk rows
-  int nseg = (b < nb) ? (cnt + seg_chunk - 1) / seg_chunk : 0;
-  int sbase = block_exclusive_scan(nseg, s_warp, &s_total);
+  const int nseg = (b < nb) ? (cnt + seg_chunk - 1) / seg_chunk : 0;
+  const int sbase = block_exclusive_scan(nseg, s_warp, s_total);
   if (b < nb) {
-    for (int s = 0; s < nseg; ++s) {
-      pb.seg_expert[sbase + s] = b;
-      pb.seg_row0[sbase + s] = off + s * seg_chunk;
-      pb.seg_nrows[sbase + s] = min(seg_chunk, cnt - s * seg_chunk);
+    for (int q = 0; q < nseg; ++q) {
+      pb.seg_expert[sbase + q] = b;
+      pb.seg_row0[sbase + q] = off + q * seg_chunk;
+      pb.seg_nrows[sbase + q] = min(seg_chunk, cnt - q * seg_chunk);
     }
   }
-  if (threadIdx.x == 0) *pb.n_seg = s_total;
+  if (threadIdx.x == 0) *pb.n_seg = *s_total;
+}
+
+// entries: n_ent routed entries (expert id per entry; token = entry / k).
+// n_sh: rows of the shared bin (0 or T), bin index n_exp.
+__global__ void __launch_bounds__(kPermThreads) permute_kernel(const int* __restrict__ entries, int n_ent, int k,
+                                                               int n_exp, int n_sh, int seg_chunk, PermBufs pb) {
+  pdl_wait();
+  pdl_launch_next();
+  extern __shared__ int s_hist[];  // [kPermWarps][nb]
+  __shared__ int s_warp[32];
+  __shared__ int s_total;
+  counting_sort_cta(
+      n_ent, n_exp, n_sh, seg_chunk, pb, s_hist, s_warp, &s_total, [&](int j) { return entries[j]; },
+      [&](int j, int pos) {
+        pb.row_src[pos] = j / k;
+        pb.inv[j] = pos;
+      },
+      [&](int t, int pos) { pb.row_src[pos] = t; });
 }
 
 // ---------------------------------------------------------------- prep
 // Output row j = act[row_src[j]] (or act[j] when row_src is null), converted
 // to fp16 in the GEMV activation layout (act_pos for `bits`), plus the sums
 // [n, sum_ld(K)] of each 64-column group.  Gathering the routed rows here makes
-// every segment's rows contiguous for the GEMV kernel's tile loads.
+// every segment's rows contiguous for the GEMV kernel's tile loads.  n_dev
+// (or null): the row count in device memory (at most n), for callers whose
+// row count is only known on the device; the grid then strides over the rows.
 __global__ void prep_act_kernel(const uint16_t* __restrict__ act, const int* __restrict__ row_src, int is_bf16, int n,
-                                int K, int bits, uint16_t* __restrict__ out, float* __restrict__ sums) {
+                                const int* __restrict__ n_dev, int K, int bits, uint16_t* __restrict__ out,
+                                float* __restrict__ sums) {
   pdl_wait();  // its successor, a persistent GEMV / GEMM, launches at its completion
   const int nblk = K >> 3;
-  long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  long long total = (long long)n * nblk;
-  bool valid = gid < total;
-  long long g = valid ? gid : 0;
-  const long long orow = g / nblk;
-  const long long irow = row_src ? __ldg(row_src + orow) : orow;
-  uint4 v = reinterpret_cast<const uint4*>(act)[irow * nblk + (g - orow * nblk)];
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  float f[8];
+  if (n_dev) n = min(n, max(0, *n_dev));
+  const long long total = (long long)n * nblk;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  // uniform trip count across the block: the group-sum shuffles need every lane
+  for (long long base = (long long)blockIdx.x * blockDim.x; base < total; base += stride) {
+    const long long gid = base + threadIdx.x;
+    const bool valid = gid < total;
+    const long long g = valid ? gid : 0;
+    const long long orow = g / nblk;
+    const long long irow = row_src ? __ldg(row_src + orow) : orow;
+    const uint4 v = reinterpret_cast<const uint4*>(act)[irow * nblk + (g - orow * nblk)];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float f[8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = act_to_f32(static_cast<uint16_t>(w[i] & 0xffffu), is_bf16);
-    f[2 * i + 1] = act_to_f32(static_cast<uint16_t>(w[i] >> 16), is_bf16);
-  }
-  uint16_t h[8];
-  float s = 0.0f;
-  bool bad = false;
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = act_to_f32(static_cast<uint16_t>(w[i] & 0xffffu), is_bf16);
+      f[2 * i + 1] = act_to_f32(static_cast<uint16_t>(w[i] >> 16), is_bf16);
+    }
+    uint16_t h[8];
+    float s = 0.0f;
+    bool bad = false;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (!(fabsf(f[i]) <= 65504.0f)) bad = true;
-    __half hv = __float2half_rn(f[i]);
-    h[i] = __half_as_ushort(hv);
-    s += __half2float(hv);
-  }
-  if (valid && bad) ef_set_error(kDevErrRange);
-  uint32_t o[4];
+    for (int i = 0; i < 8; ++i) {
+      if (!(fabsf(f[i]) <= 65504.0f)) bad = true;
+      const __half hv = __float2half_rn(f[i]);
+      h[i] = __half_as_ushort(hv);
+      s += __half2float(hv);
+    }
+    if (valid && bad) ef_set_error(kDevErrRange);
+    uint32_t o[4];
 #pragma unroll
-  for (int q = 0; q < 4; ++q)
-    o[q] = (uint32_t)h[act_col(2 * q, bits)] | ((uint32_t)h[act_col(2 * q + 1, bits)] << 16);
-  if (valid) reinterpret_cast<uint4*>(out)[g] = make_uint4(o[0], o[1], o[2], o[3]);
-  // 8 consecutive threads cover one 64-column group (nblk is a multiple of 8)
-  s += __shfl_xor_sync(0xffffffffu, s, 1);
-  s += __shfl_xor_sync(0xffffffffu, s, 2);
-  s += __shfl_xor_sync(0xffffffffu, s, 4);
-  if (valid && (gid & 7) == 0) {
-    const long long row = gid / nblk;
-    const int grp = (int)((gid - row * nblk) >> 3);
-    sums[row * sum_ld(K) + grp] = s;
+    for (int q = 0; q < 4; ++q)
+      o[q] = (uint32_t)h[act_col(2 * q, bits)] | ((uint32_t)h[act_col(2 * q + 1, bits)] << 16);
+    if (valid) reinterpret_cast<uint4*>(out)[g] = make_uint4(o[0], o[1], o[2], o[3]);
+    // 8 consecutive threads cover one 64-column group (nblk is a multiple of 8)
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    if (valid && (gid & 7) == 0) {
+      const long long row = gid / nblk;
+      const int grp = (int)((gid - row * nblk) >> 3);
+      sums[row * sum_ld(K) + grp] = s;
+    }
   }
 }
 
@@ -239,13 +263,17 @@ cudaError_t launch_permute(const int* entries, int n_ent, int k, int n_exp, int 
   return launch_pdl(permute_kernel, 1, kPermThreads, smem, st, entries, n_ent, k, n_exp, n_sh, seg_chunk, pb);
 }
 
+// n_dev (or null): the device-side row count (<= n); the grid is then capped
+// at max_blocks and strides over the rows.
 cudaError_t launch_prep_act(const uint16_t* act, const int* row_src, int is_bf16, int n, int K, int bits,
-                            uint16_t* out, float* sums, cudaStream_t st) {
+                            uint16_t* out, float* sums, cudaStream_t st, const int* n_dev, int max_blocks) {
   long long total = (long long)n * (K / 8);
   if (total == 0) return cudaSuccess;
   int threads = 256;
   long long blocks = (total + threads - 1) / threads;
-  return launch_pdl(prep_act_kernel, (unsigned)blocks, threads, 0, st, act, row_src, is_bf16, n, K, bits, out, sums);
+  if (n_dev && max_blocks > 0 && blocks > max_blocks) blocks = max_blocks;
+  return launch_pdl(prep_act_kernel, (unsigned)blocks, threads, 0, st, act, row_src, is_bf16, n, n_dev, K, bits, out,
+                    sums);
 }
 
 cudaError_t launch_combine(const float* rows, const int* inv, const float* wts, int T, int k, int H, int sh_base,

@@ -26,6 +26,8 @@ constexpr int kDevErrTimeoutEmpty = 1002;
 constexpr int kDevErrTimeoutScales = 1003;
 constexpr int kDevErrRange = 2001;
 constexpr int kDevErrTimeoutTc = 1004;
+constexpr int kDevErrTimeoutPeer = 1005;  // a peer rank's flag never arrived
+constexpr int kDevErrRecvOverflow = 2002; // more rows received than the exchange holds
 
 // Output of the permutation (all device pointers into the workspace).
 struct PermBufs {

@@ -154,3 +154,142 @@ def shard_layer(spec: MoESpec, layer: dict, rank: int, n_ranks: int, device="cud
     # the gate keeps all E rows (routing is replicated); the experts are the shard
     local = MoELayer.from_arrays(spec.with_(n_experts=e_loc), part, device=device)
     return EpDeviceOps(spec, local.gate, local.switch_mlp, local.shared_experts, n_ranks)
+
+
+def _dt_code(dt: torch.dtype) -> int:
+    return {torch.bfloat16: L.EF_DT_BF16, torch.float16: L.EF_DT_F16, torch.float32: L.EF_DT_F32}[dt]
+
+
+class PeerExpertParallelMoE:
+    """One rank's MoE layer with its experts sharded across the ranks of
+    `group`, exchanged by the library's own kernels through the peers' memory
+    over NVLink (``ef_ep_forward``): no host synchronisation and no NCCL call
+    in a forward, so a forward can be captured in a CUDA graph.
+
+    Every rank must construct it (the exchange buffers' IPC handles are
+    gathered once over `group`), run the same sequence of forwards (its own
+    token count each, 0 allowed) and call ``close()`` together.  Without an
+    initialised process group it is a single-rank layer (``ops`` holding all
+    experts)."""
+
+    def __init__(self, spec: MoESpec, ops: EpDeviceOps, group=None, max_tokens: int = 256, max_recv_rows: int = 0,
+                 act_dtype: torch.dtype = torch.bfloat16, path: int = L.EF_PATH_AUTO):
+        if dist.is_available() and dist.is_initialized():
+            self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        else:
+            self.world, self.rank = 1, 0
+        if ops.n_ranks != self.world:
+            raise ValueError(f"ops shard the experts over {ops.n_ranks} ranks, the group has {self.world}")
+        self.spec, self.ops, self.group = spec, ops, group
+        self.max_tokens, self.act_dtype = max_tokens, act_dtype
+        self.device = ops.gate.weight.device
+        cfg = ops._cfg(_dt_code(act_dtype))
+        if ops.shared_mlp is not None:
+            cfg.n_shared, cfg.shared_inter = 1, ops.shared_mlp.gate_proj.output_dims
+        cfg.path = path
+        self._cfg = cfg
+        g = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            L.check(L.lib().ef_ep_group_create(ctypes.byref(cfg), self.rank, self.world, max_tokens, max_recv_rows,
+                                               ctypes.byref(g)))
+        self._g = g
+        try:
+            h = (ctypes.c_uint8 * 64)()
+            L.check(L.lib().ef_ep_group_handle(g, h))
+            mine = bytes(h)
+            if self.world > 1:
+                on_gpu = dist.get_backend(group) == "nccl"
+                t = torch.tensor(list(mine), dtype=torch.uint8, device=self.device if on_gpu else "cpu")
+                parts = [torch.empty_like(t) for _ in range(self.world)]
+                dist.all_gather(parts, t, group=group)
+                handles = b"".join(bytes(p.cpu().tolist()) for p in parts)
+            else:
+                handles = mine
+            buf = (ctypes.c_uint8 * len(handles)).from_buffer_copy(handles)
+            with torch.cuda.device(self.device):
+                L.check(L.lib().ef_ep_group_open(g, buf))
+        except Exception:
+            L.lib().ef_ep_group_destroy(g)
+            self._g = None
+            raise
+
+    def workspace_bytes(self, T: int) -> int:
+        return int(L.lib().ef_ep_workspace_size(self._g, T))
+
+    def forward(self, x: torch.Tensor, inds_out: Optional[torch.Tensor] = None,
+                wts_out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                workspace_buf: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y = MoE(x) for this rank's tokens (x's dtype, or fp32 with out_dtype=torch.float32)."""
+        if self._g is None:
+            raise RuntimeError("the group is closed")
+        H = self.spec.hidden
+        xf = x.reshape(-1, H).contiguous()
+        _need_cuda(xf)
+        if xf.dtype != self.act_dtype:
+            raise TypeError(f"activations must be {self.act_dtype} (the group's dtype)")
+        T = xf.shape[0]
+        od = out_dtype or xf.dtype
+        y = torch.empty((T, H), dtype=od, device=xf.device)
+        n = self.workspace_bytes(T)
+        if workspace_buf is not None:
+            if workspace_buf.numel() < n:
+                raise ValueError(f"workspace_buf needs {n} bytes")
+            ws = workspace_buf
+        else:
+            ws = workspace(n, xf.device)
+        ops = self.ops
+        sp, sh = ops.local_mlp, ops.shared_mlp
+        sq = [ctypes.byref(p.qweight()) for p in (sh.gate_proj, sh.up_proj, sh.down_proj)] if sh else [None] * 3
+        eb = ops.gate.e_score_correction_bias
+        L.check(L.lib().ef_ep_forward(
+            self._g, xf.data_ptr() if T else None, T, ops.gate.weight.data_ptr(),
+            eb.data_ptr() if eb is not None else None, sp.gate_proj.qweight(), sp.up_proj.qweight(),
+            sp.down_proj.qweight(), sq[0], sq[1], sq[2], y.data_ptr() if T else None, _dt_code(od),
+            inds_out.data_ptr() if inds_out is not None else None,
+            wts_out.data_ptr() if wts_out is not None else None, ws.data_ptr(), ws.numel(),
+            _stream_ptr(xf.device)))
+        return y.reshape(*x.shape[:-1], H)
+
+    __call__ = forward
+
+    def capture(self, T: int, out_dtype: Optional[torch.dtype] = None) -> "CapturedEpForward":
+        """This rank's forward for T tokens captured in a CUDA graph (every
+        rank captures, then replays the same number of times)."""
+        return CapturedEpForward(self, T, out_dtype)
+
+    def close(self) -> None:
+        """Frees the exchange buffer after a barrier over the group (no rank
+        may still be writing into it)."""
+        if self._g is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        L.lib().ef_ep_group_destroy(self._g)
+        self._g = None
+
+
+class CapturedEpForward:
+    """A PeerExpertParallelMoE forward for a fixed token count in a CUDA graph
+    (own input, output and workspace buffers); two eager forwards first."""
+
+    def __init__(self, layer: PeerExpertParallelMoE, T: int, out_dtype: Optional[torch.dtype] = None):
+        dev = layer.device
+        self.layer = layer
+        self.x = torch.zeros((T, layer.spec.hidden), dtype=layer.act_dtype, device=dev)
+        self.ws = torch.empty(max(layer.workspace_bytes(T), 1), dtype=torch.uint8, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                layer(self.x, out_dtype=out_dtype, workspace_buf=self.ws)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.y = layer(self.x, out_dtype=out_dtype, workspace_buf=self.ws)
+
+    def __call__(self, x: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x is not None:
+            self.x.copy_(x.reshape(self.x.shape), non_blocking=True)
+        self.graph.replay()
+        return self.y

@@ -28,6 +28,8 @@
  *   ef_moe_experts_forward  per-(row, expert) SwiGLU loop                  ef_engine.py:678-695
  *   ef_permute            unique-expert grouping of the routed entries     ef_engine.py:640-647
  *   ef_combine            score-weighted sum over k (+ shared)             ef_engine.py:695-703
+ *   ef_ep_forward         the per-(token, k) expert loop, experts sharded   ef_engine.py:678-703
+ *                         across the GPUs of one box (no reference counterpart for the split)
  *   ef_slotpool_*         FrequencyWeightedCache get/put/trim              ef_engine.py:48-104
  *                         + mmap page-in of misses                        ef_engine.py:650-675
  *   ef_kquant_*           GGUF Q2_K/Q3_K/Q4_K decode (+ GEMV)              ef_deepseek_mmap.py:330-378,655-773
@@ -224,6 +226,60 @@ ef_status ef_ep_dispatch(const ef_moe_cfg* cfg, int n_ranks, const void* x, int 
  * with_shared), in j order; back_rows fp32 [T*k (+T), H]. */
 ef_status ef_ep_combine(const ef_moe_cfg* cfg, const float* back_rows, const int32_t* inv, const float* wts, int T,
                         int with_shared, void* y, void* stream);
+
+/* ---- expert parallelism over NVLink peer memory -------------------------------------- */
+/* The same split (expert e on rank e / (E / n_ranks); router and shared expert
+ * replicated; each rank routes its own tokens), exchanged by the kernels
+ * themselves through the peers' memory instead of host-issued all-to-alls:
+ *   - each rank owns one exchange buffer (receive regions for every source
+ *     rank, a row-return region for its own tokens, arrival flags); the
+ *     buffers are shared once through CUDA IPC handles;
+ *   - ef_ep_forward routes and sorts this rank's tokens, and one kernel stores
+ *     every routed token row straight into its destination rank's receive
+ *     region and raises that rank's arrival flag (release at system scope);
+ *   - a one-CTA kernel waits (bounded) for every source's flag, then sorts the
+ *     received rows by local expert; this rank's shared expert is one more bin;
+ *     the local experts run on the decode GEMV or the grouped GEMM;
+ *   - one kernel stores each fp32 output row back into its source rank's
+ *     return region (the row the source sorted the entry to) and raises the
+ *     source's done flag; the source waits for every rank's done flag and
+ *     combines in k order.
+ * The combine is the single-GPU layer's, over the same fp32 rows, so the output
+ * equals ef_moe_forward's whenever both run the same expert kernels.  Nothing
+ * in a forward waits on the host: a device-side epoch numbers the flags, so a
+ * forward can be captured in a CUDA graph.  Every rank must issue the same
+ * sequence of forwards (T may differ per rank, 0 included); a rank that stops
+ * makes the others' bounded waits run out (EF_ERR_TIMEOUT from
+ * ef_get_device_error), after which the group must be destroyed and created
+ * again.  No TMA reads peer memory.  Replaces the single-host per-(token, k)
+ * expert loop of ef_engine.py:678-703 (the reference has no multi-device path). */
+#define EF_EP_HANDLE_BYTES 64
+#define EF_EP_MAX_RANKS 64
+typedef struct ef_ep_group ef_ep_group;
+/* This rank's exchange buffer on the current device, for forwards of up to
+ * max_tokens tokens per rank; max_recv_rows (0 = the worst case, n_ranks *
+ * max_tokens * min(top_k, E / n_ranks)) bounds the rows one rank receives per
+ * forward (a forward that receives more reports EF_ERR_RANGE on the device and
+ * drops the excess).  Allocates device memory (cudaMalloc) here only. */
+ef_status ef_ep_group_create(const ef_moe_cfg* cfg, int rank, int n_ranks, int max_tokens, int max_recv_rows,
+                             ef_ep_group** out);
+/* The exchange buffer's IPC handle (EF_EP_HANDLE_BYTES bytes) for the other ranks. */
+ef_status ef_ep_group_handle(const ef_ep_group* g, void* handle);
+/* Maps every peer's buffer from the gathered handles [n_ranks][EF_EP_HANDLE_BYTES]
+ * (this rank's own entry is not used).  Every rank calls it before its first forward. */
+ef_status ef_ep_group_open(ef_ep_group* g, const void* handles);
+size_t ef_ep_workspace_size(const ef_ep_group* g, int T);
+/* y[T, H] (out_dtype: EF_DT_F32, or the activation dtype) for this rank's T
+ * tokens (T <= max_tokens; cfg->act_dtype as given at creation).  gate/up/down: this
+ * rank's local experts [E / n_ranks, ...]; shared_*: the replicated shared
+ * expert when cfg->n_shared.  inds_out / wts_out [T, k] optional. */
+ef_status ef_ep_forward(ef_ep_group* g, const void* x, int T, const void* gate_w, const float* e_bias,
+                        ef_qweight gate, ef_qweight up, ef_qweight down, const ef_qweight* shared_gate,
+                        const ef_qweight* shared_up, const ef_qweight* shared_down, void* y, int out_dtype,
+                        int32_t* inds_out, float* wts_out, void* workspace, size_t workspace_bytes, void* stream);
+/* Unmaps the peers and frees the buffer; call only when no rank has a forward
+ * in flight (e.g. after a barrier). */
+ef_status ef_ep_group_destroy(ef_ep_group* g);
 
 /* ---- expert residency: cache policy and HBM slot pool ------------------------------ */
 /* Eviction policies.  EF_POLICY_FREQ is the reference's FrequencyWeightedCache
