@@ -9,9 +9,16 @@ copies (each larger than L2) are rotated so every step reads cold weights.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--tokens T]
 
-Multi-GPU (torchrun, one process per GPU): the decode layer does not shard,
-so every rank runs an independent replica (no collective in the data path);
-time is the max over ranks, value = all ranks' tokens / that time.
+Multi-GPU (torchrun, one process per GPU): the line's workload becomes the
+DeepSeek-V3-shaped layer (hidden 7168, 256 routed experts + 1 shared, top-8
+sigmoid group-limited routing, inter 2048, 4-bit) with its experts sharded
+across the GPUs (E/N each) and the token rows exchanged over NVLink peer
+memory by the library's own kernels (ef_ep_forward, captured in a CUDA
+graph).  Strong scaling: a global batch of --ep-tokens decode tokens split
+evenly; value = that batch / the max-over-ranks step time.  The line also
+carries the same run's single-GPU layer on the same batch (box_speedup),
+weak scaling, per-phase kernel times, the EP output checked bit for bit
+against the single-GPU layer (ep_parity) and the NCCL all-to-all version.
 """
 from __future__ import annotations
 
@@ -154,19 +161,29 @@ def bench_reference(args):
         return 0
     from expertflow_b200.spec import WORKLOADS
 
-    spec = WORKLOADS[args.workload]
-    T = args.tokens
+    if ws > 1:  # the workload of our N > 1 line: DeepSeek-V3 layer, sampled to a few tokens per step
+        wl = "deepseek-v3-moe"
+        spec = WORKLOADS[wl]
+        T = min(8, args.ep_tokens)
+        cfg = {"workload": wl, "tokens_global": args.ep_tokens, "hidden": spec.hidden, "experts": spec.n_experts,
+               "top_k": spec.top_k, "inter": spec.inter, "bits": spec.bits, "shared_experts": spec.n_shared}
+        sample = f"{T}-token forwards of the {args.ep_tokens}-token workload's layer"
+    else:
+        wl = args.workload
+        spec = WORKLOADS[wl]
+        T = args.tokens
+        cfg = {"workload": wl, "tokens": T, "hidden": spec.hidden, "experts": spec.n_experts, "top_k": spec.top_k,
+               "inter": spec.inter, "bits": spec.bits}
+        sample = f"full {T}-token layer forwards"
     budget = max(2.0, min(20.0, 2.0 * (args.steps + args.warmup)))
     r = run_cpu_reference(spec, T, budget)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(r["tokens_per_s"], 3), "unit": UNIT,
         "n_gpus": args.gpus, "steps": r["steps"], "warmup": 1, "ms_per_step": round(r["s_per_step"] * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4/u8 codes, f32 accumulate",
-        "data": "synthetic (seeded)", "config": {"workload": args.workload, "tokens": T, "hidden": spec.hidden,
-                                                 "experts": spec.n_experts, "top_k": spec.top_k,
-                                                 "inter": spec.inter, "bits": spec.bits},
+        "higher_is_better": True, "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None,
+        "dtype": "u4/u8 codes, f32 accumulate", "data": "synthetic (seeded)", "config": cfg,
         "cpu_baseline": {"value": round(r["tokens_per_s"], 3), "unit": UNIT, "cores": r["cores"], "kind": "port",
-                         "sample": f"{r['steps']} full {T}-token layer forwards (median), oracle/ef_oracle.c"},
+                         "sample": f"{r['steps']} {sample} (median), oracle/ef_oracle.c"},
         "e2e": {"value": round(r["tokens_per_s"], 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -550,6 +567,343 @@ def section_kquant(args, dev, peaks):
     return out
 
 
+class _PeerEpLayers:
+    """Expert-parallel copies of one layer over the peer-memory exchange
+    (ef_ep_forward): this rank holds experts [rank * E/P, (rank + 1) * E/P)
+    of each copy, the gate and shared expert replicated.  Copies are rotated
+    per step so that every step reads weights that are not in L2."""
+
+    def __init__(self, spec, dev, rank, ws, max_tokens, path=None, min_bytes=1.5e9, seed0=1000, keep_full=False):
+        import torch
+        from expertflow_b200 import moe, synthetic, _lib
+        from expertflow_b200.ep import PeerExpertParallelMoE, shard_layer
+
+        self.spec = spec
+        self.layer_bytes = spec.n_experts // ws * spec.expert_bytes()
+        self.n = max(2, math.ceil(min_bytes / self.layer_bytes))
+        p = _lib.EF_PATH_AUTO if path is None else path
+        self.layers, self.full = [], None
+        for i in range(self.n):
+            full = synthetic.make_layer_torch(spec, seed=seed0 + i, device=dev)
+            ops = shard_layer(spec, full, rank, ws, device=dev)
+            if keep_full and i == 0:  # copy 0 also as a whole single-GPU layer (parity and the 1-GPU number)
+                self.full = moe.MoELayer.from_arrays(spec, full, device=dev, path=p)
+            del full
+            torch.cuda.empty_cache()
+            self.layers.append(PeerExpertParallelMoE(spec, ops, max_tokens=max_tokens, path=p))
+
+    def close(self):
+        for m in self.layers:
+            m.close()
+
+
+def _time_ep(L, T, steps, warmup, pg, dev, x_seed, rank, graphs=True, trace=False):
+    """CUDA-event time per step (max over ranks) of T tokens per rank through
+    the rotated expert-parallel copies; with trace, the per-launch times of a
+    separate eager pass (kernel name -> mean ms, max over ranks)."""
+    import torch
+    from expertflow_b200 import synthetic, _lib
+
+    spec = L.spec
+    xs = [synthetic.make_x_torch(spec, T, seed=x_seed + 97 * rank + i, device=dev) for i in range(L.n)]
+    if graphs:
+        cfs = [m.capture(T) for m in L.layers]
+        for cf, x in zip(cfs, xs):
+            cf.x.copy_(x)
+        fwd = [cf.graph.replay for cf in cfs]
+    else:
+        cfs = None
+        fwd = [(lambda m=m, x=x: m(x)) for m, x in zip(L.layers, xs)]
+    for s in range(warmup):
+        fwd[s % L.n]()
+    torch.cuda.synchronize()
+    pg.barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for s in range(steps):
+        fwd[s % L.n]()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    t = torch.tensor([ms], device=dev)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms = float(t.item())
+    phases = {}
+    if trace:
+        n_tr = 2 * L.n
+        _lib.trace_enable(True)
+        _lib.trace_read()
+        for s in range(n_tr):
+            L.layers[s % L.n](xs[s % L.n])
+        torch.cuda.synchronize()
+        recs = _lib.trace_read()
+        _lib.trace_enable(False)
+        by = _by_kernel(recs)
+        names = sorted(by)
+        # every rank launches the same kernel sequence: reduce per name
+        v = torch.tensor([sum(by[k]) / n_tr for k in names], device=dev, dtype=torch.float64)
+        pg.all_reduce(v, op=pg.ReduceOp.MAX)
+        phases = {k: round(float(x), 5) for k, x in zip(names, v.tolist())}
+        phases["_launches_per_step"] = len(recs) // n_tr
+    del cfs
+    return ms, phases, xs
+
+
+def bench_ep(args, pg, dev, rank, ws, local, peaks):
+    """N > 1: the DeepSeek-V3-shaped layer with its experts sharded across the
+    ranks (E/N per GPU), exchanged over NVLink peer memory by the library's
+    kernels.  Headline: strong scaling, a fixed global batch split evenly over
+    the ranks; alongside: weak scaling, the same-run single-GPU layer on the
+    same global batch, per-phase kernel times, the EP output checked bit for
+    bit against the single-GPU layer, and the NCCL all-to-all version."""
+    import torch
+    from expertflow_b200 import synthetic, _lib
+    from expertflow_b200.ep import ExpertParallelMoE, shard_layer
+    from expertflow_b200.spec import WORKLOADS
+
+    name = "deepseek-v3-moe"
+    spec = WORKLOADS[name]
+    Tg = args.ep_tokens
+    if Tg % ws:
+        raise SystemExit(f"--ep-tokens {Tg} must be a multiple of the GPU count {ws}")
+    Tl, Tw = Tg // ws, args.ep_weak_tokens
+    L = _PeerEpLayers(spec, dev, rank, ws, max_tokens=max(Tl, Tw), keep_full=True)
+
+    # parity: every rank's EP output equals the single-GPU layer on its tokens
+    x0 = synthetic.make_x_torch(spec, Tl, seed=11 + rank, device=dev)
+    inds = torch.empty((Tl, spec.top_k), dtype=torch.int32, device=dev)
+    y_ep = L.layers[0](x0, inds_out=inds, out_dtype=torch.float32)
+    y_1 = L.full(x0, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ok = torch.tensor([int(torch.equal(y_ep, y_1))], device=dev)
+    pg.all_reduce(ok, op=pg.ReduceOp.MIN)
+    ep_parity = bool(ok.item())
+    # distinct local experts this rank runs per step (every rank's routing)
+    allinds = [torch.empty_like(inds) for _ in range(ws)]
+    pg.all_gather(allinds, inds)
+    el = spec.n_experts // ws
+    ai = torch.cat(allinds).reshape(-1)
+    n_local = int(torch.unique(ai[(ai >= rank * el) & (ai < (rank + 1) * el)]).numel())
+
+    with ClockSampler(local) as clk:
+        ms, _, _ = _time_ep(L, Tl, args.steps, args.warmup, pg, dev, 7, rank)
+    clocks = clk.summary()
+    value = Tg / (ms * 1e-3)
+    _, phases, _ = _time_ep(L, Tl, 2, 1, pg, dev, 7, rank, graphs=False, trace=True)
+    ms_w, phases_w, _ = _time_ep(L, Tw, max(5, args.steps // 2), args.warmup, pg, dev, 31, rank, trace=True)
+
+    # the single-GPU layer on the same global batch (each rank its own, concurrently; max over ranks)
+    xg = synthetic.make_x_torch(spec, Tg, seed=5, device=dev)
+    cf1 = L.full.capture(Tg)
+    cf1.x.copy_(xg)
+    for _ in range(args.warmup):
+        cf1.graph.replay()
+    torch.cuda.synchronize()
+    pg.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n1 = max(5, args.steps // 2)
+    e0.record()
+    for _ in range(n1):
+        cf1.graph.replay()  # one layer copy: its weights (6.3 GB) are far larger than L2
+    e1.record()
+    torch.cuda.synchronize()
+    t1 = torch.tensor([e0.elapsed_time(e1) / n1], device=dev)
+    pg.all_reduce(t1, op=pg.ReduceOp.MAX)
+    ms1 = float(t1.item())
+    del cf1
+    single = Tg / (ms1 * 1e-3)
+
+    # roofline of the dominant kernel on this rank (algorithmic bytes of the
+    # distinct local experts it ran, + the shared expert)
+    kern = max((k for k in phases if not k.startswith("_")), key=lambda k: phases[k])
+    per_e = spec.expert_bytes()
+    k_bytes = {"qmv_gate_up": (n_local + 1) * per_e * 2 // 3, "qmv_down": (n_local + 1) * (per_e - per_e * 2 // 3)}
+    kb = k_bytes.get(kern)
+    achieved = kb / (phases[kern] * 1e-3) / 1e9 if kb else None
+
+    # e2e: pinned host tokens -> captured EP forward -> pinned host output, copies in the timed region
+    cfs = [m.capture(Tl) for m in L.layers]
+    xh = [synthetic.make_x_torch(spec, Tl, seed=7 + 97 * rank + i, device=dev).cpu().pin_memory() for i in range(L.n)]
+    yh = [torch.empty((Tl, spec.hidden), dtype=xh[0].dtype).pin_memory() for _ in range(L.n)]
+    st = torch.cuda.current_stream()
+
+    def serve(n):
+        for s in range(n):
+            i = s % L.n
+            cfs[i].x.copy_(xh[i], non_blocking=True)
+            cfs[i].graph.replay()
+            yh[i].copy_(cfs[i].y, non_blocking=True)
+
+    serve(args.warmup)
+    torch.cuda.synchronize()
+    pg.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    serve(args.steps)
+    e1.record(st)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    pg.all_reduce(te, op=pg.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+    del cfs
+
+    # the same split exchanged with NCCL all-to-alls issued by the host (the baseline this path replaces)
+    nccl = None
+    if not args.no_nccl_baseline:
+        full0 = synthetic.make_layer_torch(spec, seed=1000, device=dev)
+        ops = shard_layer(spec, full0, rank, ws, device=dev)
+        del full0
+        torch.cuda.empty_cache()
+        m = ExpertParallelMoE(spec, ops)
+        for _ in range(2):
+            m(x0)
+        torch.cuda.synchronize()
+        pg.barrier()
+        e0.record()
+        nn = 10
+        for _ in range(nn):
+            m(x0)
+        e1.record()
+        torch.cuda.synchronize()
+        tn = torch.tensor([e0.elapsed_time(e1) / nn], device=dev)
+        pg.all_reduce(tn, op=pg.ReduceOp.MAX)
+        nccl = {"ms_per_step": round(float(tn.item()), 4), "tokens_per_s": round(Tg / (float(tn.item()) * 1e-3), 1),
+                "what": "ExpertParallelMoE: host-issued NCCL all-to-alls of counts, rows, ids and fp32 outputs"}
+        del m, ops
+        torch.cuda.empty_cache()
+    n_copies, layer_bytes = L.n, L.layer_bytes
+    L.close()
+    del L
+    torch.cuda.empty_cache()
+    return {
+        "spec": spec, "value": value, "ms": ms, "clocks": clocks, "phases": phases, "Tg": Tg, "Tl": Tl, "Tw": Tw,
+        "weak": {"tokens_per_rank": Tw, "tokens_per_s": round(ws * Tw / (ms_w * 1e-3), 1),
+                 "ms_per_step": round(ms_w, 5), "phases_ms": phases_w},
+        "single": {"tokens": Tg, "tokens_per_s": round(single, 1), "ms_per_step": round(ms1, 5),
+                   "what": "the whole layer on one GPU (same run, CUDA graph)"},
+        "ep_parity": ep_parity, "kern": kern, "k_ms": phases[kern], "k_bytes": kb, "achieved": achieved,
+        "n_local": n_local, "e2e_ms": e2e_ms, "nccl": nccl, "n_copies": n_copies, "layer_bytes": layer_bytes,
+    }
+
+
+def section_prefill_ep(name, spec, Tg, args, pg, dev, rank, ws, peaks):
+    """c4 at N > 1: the 8-bit DeepSeek-V3 prefill batch split over the ranks,
+    experts sharded, exchanged over peer memory, grouped GEMM; the same-run
+    single-GPU layer on the whole batch beside it."""
+    import torch
+    from expertflow_b200 import synthetic, _lib
+
+    Tl = Tg // ws
+    L = _PeerEpLayers(spec, dev, rank, ws, max_tokens=Tl, path=_lib.EF_PATH_GEMM, min_bytes=1.0, keep_full=True)
+    steps = max(3, min(args.steps, 10))
+    ms, phases, _ = _time_ep(L, Tl, steps, args.warmup, pg, dev, 51, rank, trace=True)
+    x0 = synthetic.make_x_torch(spec, Tl, seed=13 + rank, device=dev)
+    ok = torch.tensor([int(torch.equal(L.layers[0](x0, out_dtype=torch.float32),
+                                       L.full(x0, out_dtype=torch.float32)))], device=dev)
+    pg.all_reduce(ok, op=pg.ReduceOp.MIN)
+    xg = synthetic.make_x_torch(spec, Tg, seed=5, device=dev)
+    for _ in range(2):
+        L.full(xg)
+    torch.cuda.synchronize()
+    pg.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        L.full(xg)
+    e1.record()
+    torch.cuda.synchronize()
+    t1 = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+    pg.all_reduce(t1, op=pg.ReduceOp.MAX)
+    ms1 = float(t1.item())
+    rows = Tg * (spec.top_k + spec.n_shared)  # whole box, per step
+    gemm_ms = sum(v for k, v in phases.items() if k.startswith("qgemm"))
+    # every rank runs about 1/ws of the rows: box TFLOP/s over the max-over-ranks kernel time
+    gemm_tf = 6.0 * spec.hidden * spec.inter * rows / ws / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
+    out = {"workload": name, "tokens_global": Tg, "tokens_per_rank": Tl, "tokens_per_s": round(Tg / (ms * 1e-3), 1),
+           "ms_per_step": round(ms, 4), "single_gpu_tokens_per_s": round(Tg / (ms1 * 1e-3), 1),
+           "single_gpu_ms_per_step": round(ms1, 4), "box_speedup": round(ms1 / ms, 3),
+           "ep_parity": bool(ok.item()), "phases_ms": phases,
+           "gemm_tflops_per_gpu": round(gemm_tf, 1) if gemm_tf else None,
+           "gemm_frac_sustained": round(gemm_tf / peaks["bf16_sustained"], 4) if gemm_tf else None,
+           "parallelism": f"ep{ws} (experts sharded, peer-memory exchange over NVLink)"}
+    L.close()
+    del L
+    torch.cuda.empty_cache()
+    return out
+
+
+def _ep_line(r, args, ws, peaks, sections):
+    spec = r["spec"]
+    hbm = peaks["hbm"]
+    return {
+        "metric": METRIC, "value": round(r["value"], 1), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(r["ms"], 5), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "u4 codes x f16 activations, f32 accumulate",
+        "data": "synthetic (seeded; random-init weights of the named shape)",
+        "config": {"workload": "deepseek-v3-moe", "tokens_global": r["Tg"], "tokens_per_rank": r["Tl"],
+                   "hidden": spec.hidden, "experts": spec.n_experts, "experts_per_gpu": spec.n_experts // ws,
+                   "top_k": spec.top_k, "inter": spec.inter, "bits": spec.bits, "shared_experts": spec.n_shared,
+                   "parallelism": f"ep{ws} (experts sharded, peer-memory exchange over NVLink, no host sync)",
+                   "launch": "CUDA graph per layer copy (PeerExpertParallelMoE.capture)",
+                   "layer_copies": r["n_copies"],
+                   "l2": f"rotating {r['n_copies']} shard copies of {r['layer_bytes'] / 1e6:.0f} MB per GPU"},
+        "box_speedup": round(r["value"] / r["single"]["tokens_per_s"], 3),
+        "single_gpu": r["single"],
+        "weak": r["weak"],
+        "ep_parity": r["ep_parity"],
+        "nccl_alltoall": r["nccl"],
+        "phases_ms": r["phases"],
+        "roofline": {"kernel": r["kern"], "bound": "hbm",
+                     "achieved": round(r["achieved"], 1) if r["achieved"] else None, "peak": hbm, "unit": "GB/s",
+                     "frac": round(r["achieved"] / hbm, 4) if r["achieved"] else None, "traffic": None,
+                     "peak_kind": peaks["kind"], "kernel_ms": r["k_ms"], "algorithmic_bytes": r["k_bytes"],
+                     "local_experts_run": r["n_local"],
+                     "timing": "CUDA events around each launch, eager traced pass, max over ranks"},
+        "cpu_baseline": None,
+        "e2e": {"value": round(r["Tg"] / (r["e2e_ms"] * 1e-3), 1), "unit": UNIT, "ms_per_step": round(r["e2e_ms"], 5),
+                "h2d_bytes_per_step": r["Tg"] * spec.hidden * 2, "d2h_bytes_per_step": r["Tg"] * spec.hidden * 2,
+                "api": "PeerExpertParallelMoE.capture (C ABI ef_ep_forward in a CUDA graph); pinned host tokens "
+                       "copied in and the output read back on every rank every step"},
+        "gpu_launches": r["phases"].get("_launches_per_step", 0) * args.steps,
+        "clocks": r["clocks"],
+        "workloads": sections,
+    }
+
+
+def _summary(line, sections):
+    """The per-workload figures in a few keys, printed last in the line so
+    that a tail of the output keeps them."""
+    out = {"headline": {"workload": line["config"]["workload"], "tokens_per_s": line["value"],
+                        "roofline_frac": (line.get("roofline") or {}).get("frac")}}
+    if "box_speedup" in line:
+        out["headline"]["box_speedup"] = line["box_speedup"]
+        out["headline"]["ep_parity"] = line["ep_parity"]
+    c2 = sections.get("c2")
+    if c2:
+        out["c2"] = {f"T{p['tokens']}": {"tok_s": p["tokens_per_s"], "kernel_frac": p.get("kernel_frac")}
+                     for p in c2["points"]}
+    c4 = sections.get("c4")
+    if c4:
+        if "gemm" in c4:
+            g = c4["gemm"].get("qgemm_gate_up", {})
+            out["c4"] = {"tok_s": c4["tokens_per_s"], "gemm_tflops": c4.get("gemm_tflops"),
+                         "gate_up_frac_burst": g.get("frac_burst"), "gate_up_frac_sustained": g.get("frac_sustained"),
+                         "frac_sustained": c4.get("gemm_frac_sustained")}
+        else:
+            out["c4"] = {"tok_s": c4["tokens_per_s"], "box_speedup": c4["box_speedup"],
+                         "ep_parity": c4["ep_parity"], "gemm_frac_sustained": c4["gemm_frac_sustained"]}
+    c3 = sections.get("c3")
+    if c3:
+        la = c3.get("lookahead", {})
+        out["c3"] = {"tok_s": la.get("tokens_per_s"), "h2d_overlap": la.get("h2d_overlap"),
+                     "resident_tok_s": c3.get("resident_tokens_per_s")}
+    kq = sections.get("kq")
+    if kq:
+        out["kq"] = {f"{p['format']}_T{p['tokens']}": p["frac"] for p in kq["points"] if p["tokens"] == 1}
+    return out
+
+
 def bench_ours(args):
     import torch
     from expertflow_b200 import build, moe, synthetic, _lib
@@ -569,6 +923,20 @@ def bench_ours(args):
     spec = WORKLOADS[args.workload]
     peaks = _peaks()
     hbm_peak = peaks["hbm"]
+    if ws > 1:
+        r = bench_ep(args, pg, dev, rank, ws, local, peaks)
+        sections = {}
+        if "c4" in args.sections:
+            sections["c4"] = section_prefill_ep("deepseek-v3-moe-8bit", WORKLOADS["deepseek-v3-moe-8bit"], 4096,
+                                                args, pg, dev, rank, ws, peaks)
+            torch.cuda.empty_cache()
+        line = _ep_line(r, args, ws, peaks, sections)
+        line["workloads_summary"] = _summary(line, sections)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        pg.barrier()
+        pg.destroy_process_group()
+        return 0
 
     # ---- headline: T tokens through the configured workload (decode, GEMV)
     L = _Layers(spec, dev, rank)
@@ -727,11 +1095,9 @@ def bench_ours(args):
         "clocks": clocks,
         "workloads": sections,
     }
+    line["workloads_summary"] = _summary(line, sections)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if pg:
-        pg.barrier()
-        pg.destroy_process_group()
     return 0
 
 
@@ -756,6 +1122,10 @@ def main():
                     help="c3 again with the experts in safetensors files under a bounded pinned host tier")
     ap.add_argument("--stream-host-frac", type=float, default=0.25)
     ap.add_argument("--stream-dir", default=None, help="where the c3 model files go (default: the temp dir)")
+    ap.add_argument("--ep-tokens", type=int, default=256,
+                    help="N > 1: global decode batch of the DeepSeek-V3 layer, split over the GPUs (strong scaling)")
+    ap.add_argument("--ep-weak-tokens", type=int, default=256, help="N > 1: tokens per GPU of the weak-scaling run")
+    ap.add_argument("--no-nccl-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
