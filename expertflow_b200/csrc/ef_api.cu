@@ -30,7 +30,8 @@ cudaError_t launch_prep_act(const uint16_t* act, const int* row_src, int is_bf16
                             uint16_t* out, float* sums, cudaStream_t st, const int* n_dev = nullptr,
                             int max_blocks = 0);
 cudaError_t launch_combine(const float* rows, const int* inv, const float* wts, int T, int k, int H, int sh_base,
-                           void* out, int out_dtype, cudaStream_t st);
+                           void* out, int out_dtype, cudaStream_t st, const uint32_t* wait_flags = nullptr,
+                           int n_wait = 0, const uint32_t* epoch = nullptr);
 cudaError_t launch_qmv(int bits, int mode, const QmvParams& p, int n_sm, cudaStream_t st, int min_segments = 0);
 size_t qmv_smem_required(int bits, int mode, int K);
 cudaError_t launch_qgemm(int bits, int mode, const GemmParams& p, int n_sm, cudaStream_t st);

@@ -62,6 +62,39 @@ EF_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
   return false;
 }
 
+// ---------------------------------------------------------------- flags shared with peer GPUs
+// A wait on a peer's flag ends after kPeerWaitNs of the GPU's global timer
+// or kPeerWaitPolls polls, whichever comes first: ranks may start a forward
+// seconds apart (host-side work between layers), a dead rank must not hang
+// the others.
+constexpr unsigned long long kPeerWaitNs = 20ull * 1000 * 1000 * 1000;
+constexpr uint32_t kPeerWaitPolls = 1u << 28;
+EF_DEV void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+EF_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait until *flag has reached `want` (flags only grow, mod 2^32);
+// false (error word set) when it never does or another wait already failed.
+EF_DEV unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+EF_DEV bool wait_flag_sys(const uint32_t* flag, uint32_t want) {
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 0; i < kPeerWaitPolls; ++i) {
+    if ((int)(ld_acquire_sys(flag) - want) >= 0) return true;
+    if ((i & 255u) == 255u && (ef_error_seen() || global_ns() - t0 > kPeerWaitNs)) break;
+    __nanosleep(i < 1024 ? 32 : 256);
+  }
+  if (!ef_error_seen()) ef_set_error(ef::kDevErrTimeoutPeer);
+  return false;
+}
+
 // ---------------------------------------------------------------- programmatic dependent launch
 // The kernels of one forward are launched with programmatic stream
 // serialisation: each waits for its predecessor's completion and memory

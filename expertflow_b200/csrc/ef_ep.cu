@@ -167,12 +167,6 @@ ef_status ef_ep_combine(const ef_moe_cfg* cfg, const float* back_rows, const int
 namespace ef {
 
 constexpr int kEpMaxRanks = EF_EP_MAX_RANKS;
-// A wait on a peer's flag ends after kPeerWaitNs of the GPU's global timer
-// or kPeerWaitPolls polls, whichever comes first: ranks may start a forward
-// seconds apart (host-side work between layers), a dead rank must not hang
-// the others.
-constexpr unsigned long long kPeerWaitNs = 20ull * 1000 * 1000 * 1000;
-constexpr uint32_t kPeerWaitPolls = 1u << 28;
 
 struct EpPeers {
   uint8_t* base[kEpMaxRanks];
@@ -187,31 +181,6 @@ struct EpGeom {
   uint32_t* ctr;    // [2] last-CTA counters of dispatch and return
 };
 
-EF_DEV void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-EF_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-// Bounded wait until *flag has reached `want` (flags only grow, mod 2^32);
-// false (error word set) when it never does or another wait already failed.
-EF_DEV unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-EF_DEV bool wait_flag_sys(const uint32_t* flag, uint32_t want) {
-  const unsigned long long t0 = global_ns();
-  for (uint32_t i = 0; i < kPeerWaitPolls; ++i) {
-    if ((int)(ld_acquire_sys(flag) - want) >= 0) return true;
-    if ((i & 255u) == 255u && (ef_error_seen() || global_ns() - t0 > kPeerWaitNs)) break;
-    __nanosleep(i < 1024 ? 32 : 256);
-  }
-  if (!ef_error_seen()) ef_set_error(kDevErrTimeoutPeer);
-  return false;
-}
 EF_DEV uint32_t* slot_u32(uint8_t* base, unsigned long long off, int i) {
   return reinterpret_cast<uint32_t*>(base + off + (size_t)i * 64);
 }
@@ -660,11 +629,13 @@ extern "C" ef_status ef_ep_forward(ef_ep_group* g, const void* x, int T, const v
                                       (const float*)w.f.yrows, (const int*)w.ret_rank, (const int*)w.ret_row,
                                       (const int*)w.n_rows, nr_max));
   }
-  EF_LAUNCH("ep_wait", launch_pdl(ef::ep_wait_kernel, 1, 64, 0, st, G, (const uint8_t*)g->base));
-  if (T > 0) {
+  if (T > 0) {  // the combine waits for every rank's done flag itself
     const float* back = reinterpret_cast<const float*>(g->base + G.off_back);
     EF_LAUNCH("combine", launch_combine(back, w.own.inv, wts, T, k, H, cfg->n_shared ? T * k : -1, y, out_dtype,
-                                        st));
+                                        st, reinterpret_cast<const uint32_t*>(g->base + G.off_done), g->P,
+                                        G.epoch));
+  } else {  // nothing to combine, but the next dispatch must follow every rank's return
+    EF_LAUNCH("ep_wait", launch_pdl(ef::ep_wait_kernel, 1, 64, 0, st, G, (const uint8_t*)g->base));
   }
   return EF_OK;
 }

@@ -215,10 +215,17 @@ __global__ void prep_act_kernel(const uint16_t* __restrict__ act, const int* __r
 // ---------------------------------------------------------------- combine
 // out[t, c] = sum_j wts[t, j] * rows[inv[t*k + j], c]  (+ rows[sh_base + t, c])
 // wts == nullptr means unit weights.  out dtype: 0 bf16, 1 fp16, 2 fp32.
-__global__ void combine_kernel(const float* __restrict__ rows, const int* __restrict__ inv,
-                               const float* __restrict__ wts, int T, int k, int H, int sh_base,
-                               void* __restrict__ out, int out_dtype) {
+// wait_flags (or null): the rows are written by peer GPUs; every CTA first
+// waits (bounded) until flags 0..n_wait-1 (64 bytes apart) reach *epoch.
+__global__ void combine_kernel(const float* rows, const int* __restrict__ inv, const float* __restrict__ wts, int T,
+                               int k, int H, int sh_base, void* __restrict__ out, int out_dtype,
+                               const uint32_t* wait_flags, int n_wait, const uint32_t* epoch) {
   pdl_wait();
+  if (wait_flags) {
+    const uint32_t ep = *reinterpret_cast<const volatile uint32_t*>(epoch);
+    if ((int)threadIdx.x < n_wait) wait_flag_sys(wait_flags + threadIdx.x * 16, ep);
+    __syncthreads();
+  }
   pdl_launch_next();
   const int t = blockIdx.y;
   const int c4 = blockIdx.x * blockDim.x + threadIdx.x;  // index of a 4-column quad
@@ -277,12 +284,15 @@ cudaError_t launch_prep_act(const uint16_t* act, const int* row_src, int is_bf16
 }
 
 cudaError_t launch_combine(const float* rows, const int* inv, const float* wts, int T, int k, int H, int sh_base,
-                           void* out, int out_dtype, cudaStream_t st) {
+                           void* out, int out_dtype, cudaStream_t st, const uint32_t* wait_flags, int n_wait,
+                           const uint32_t* epoch) {
   if (T == 0) return cudaSuccess;
   int quads = H / 4;
   int threads = quads < 256 ? ((quads + 31) / 32) * 32 : 256;
+  if (wait_flags && threads < n_wait) threads = ((n_wait + 31) / 32) * 32;
   dim3 grid((quads + threads - 1) / threads, T);
-  return launch_pdl(combine_kernel, grid, threads, 0, st, rows, inv, wts, T, k, H, sh_base, out, out_dtype);
+  return launch_pdl(combine_kernel, grid, threads, 0, st, rows, inv, wts, T, k, H, sh_base, out, out_dtype,
+                    wait_flags, n_wait, epoch);
 }
 
 }  // namespace ef
