@@ -95,6 +95,10 @@ class StoreInfo(ctypes.Structure):
                 ("n_readers", ctypes.c_int), ("direct", ctypes.c_int), ("reads", ctypes.c_longlong),
                 ("file_bytes", ctypes.c_double)]
 
+class KQWeight(ctypes.Structure):
+    _fields_ = [("blocks", ctypes.c_void_p), ("type", ctypes.c_int), ("expert_stride", ctypes.c_longlong)]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _SZ = ctypes.c_size_t
@@ -134,6 +138,9 @@ SIGNATURES = {
     "ef_ep_workspace_size": (_SZ, [_P, _I]),
     "ef_ep_forward": (_I, [_P, _P, _I, _P, _P, _QW, _QW, _QW, _QWP, _QWP, _QWP, _P, _I, _P, _P, _P, _SZ, _P]),
     "ef_ep_group_destroy": (_I, [_P]),
+    "ef_kquant_moe_workspace_size": (_SZ, [_CFGP, _I]),
+    "ef_kquant_moe_forward": (_I, [_CFGP, _P, _I, _P, _P, KQWeight, KQWeight, KQWeight, ctypes.POINTER(KQWeight),
+                                   ctypes.POINTER(KQWeight), ctypes.POINTER(KQWeight), _P, _P, _P, _P, _SZ, _P]),
     "ef_policy_create": (_I, [_I, _I, ctypes.c_double, _P]),
     "ef_policy_get": (_I, [_P, ctypes.c_longlong]),
     "ef_policy_put": (None, [_P, ctypes.c_longlong]),
@@ -152,6 +159,8 @@ SIGNATURES = {
     "ef_pool_decode_workspace_size": (_SZ, [_P, _I]),
     "ef_pool_decode_step": (_I, [_P, _P, _I, _P, _P, _I, ctypes.c_float, _P, _SZ, _P]),
     "ef_pool_resident": (_I, [_P, _I, _P, _I, ctypes.POINTER(_I)]),
+    "ef_pool_record_routing": (_I, [_P, _I]),
+    "ef_pool_routing_trace": (_I, [_P, _P, ctypes.c_longlong, _P, _P, ctypes.c_longlong, _P]),
     "ef_pool_get_stats": (_I, [_P, ctypes.POINTER(PoolStats)]),
     "ef_pool_reset_stats": (_I, [_P]),
     "ef_pool_destroy": (_I, [_P]),

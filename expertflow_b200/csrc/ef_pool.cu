@@ -385,6 +385,11 @@ struct ef_slot_pool {
   int32_t* h_slot = nullptr;
   int h_cap = 0;
   ef_pool_stats st{};
+  // routing trace (ef_pool_record_routing): (layer, expert) pairs in routing
+  // order and, per ended token, the number of pairs recorded up to its end
+  bool rec_on = false;
+  std::vector<int32_t> rec_pairs;
+  std::vector<long long> rec_tok_end;
   std::vector<ef::CopyTimer> timers;       // one per copy batch, folded into st.copy_ms on demand
   std::vector<ef::CopyTimer> spare;
   // host tier over a store: host_blobs then holds host_n blobs, replaced
@@ -940,6 +945,11 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
   cudaMemcpyAsync(P->h_inds, inds, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
   if (next_gate_w) cudaMemcpyAsync(P->h_pred, w.pinds, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
   if (cudaStreamSynchronize(st) != cudaSuccess) return fail(EF_ERR_CUDA, "routing failed: %s", cudaGetErrorString(cudaGetLastError()));
+  if (P->rec_on)  // the reference records each routed entry in (token, k) order (ef_engine.py:640-646)
+    for (int i = 0; i < n; ++i) {
+      P->rec_pairs.push_back(layer);
+      P->rec_pairs.push_back(P->h_inds[i]);
+    }
   const std::vector<int> need = distinct_sorted(P->h_inds, n, E);
   std::vector<char> keep(E, 0);
   for (int e : need) keep[e] = 1;
@@ -1117,6 +1127,30 @@ ef_status ef_pool_end_token(ef_slot_pool* P) {
     L.policy.end_token();  // trim, then end_token, as the reference's decode loop does
   }
   P->st.tokens++;
+  if (P->rec_on) P->rec_tok_end.push_back((long long)(P->rec_pairs.size() / 2));
+  return EF_OK;
+}
+
+ef_status ef_pool_record_routing(ef_slot_pool* P, int on) {
+  if (!P) return fail(EF_ERR_INVALID, "pool is NULL");
+  if (on && !P->rec_on) {
+    P->rec_pairs.clear();
+    P->rec_tok_end.clear();
+  }
+  P->rec_on = on != 0;
+  return EF_OK;
+}
+
+ef_status ef_pool_routing_trace(const ef_slot_pool* P, int32_t* pairs, long long pair_cap, long long* n_pairs,
+                                long long* token_ends, long long tok_cap, long long* n_tokens) {
+  if (!P) return fail(EF_ERR_INVALID, "pool is NULL");
+  const long long np = (long long)(P->rec_pairs.size() / 2), nt = (long long)P->rec_tok_end.size();
+  if (n_pairs) *n_pairs = np;
+  if (n_tokens) *n_tokens = nt;
+  if (pairs)
+    for (long long i = 0; i < std::min(np, pair_cap) * 2; ++i) pairs[i] = P->rec_pairs[(size_t)i];
+  if (token_ends)
+    for (long long i = 0; i < std::min(nt, tok_cap); ++i) token_ends[i] = P->rec_tok_end[(size_t)i];
   return EF_OK;
 }
 

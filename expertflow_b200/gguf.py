@@ -231,6 +231,28 @@ class GGUFExperts:
             raise KeyError(f"Expert {e} not found in layer {layer}, proj {proj}")
         return ExpertSlice(s.file, s.offset + e * s.expert_bytes, s.expert_bytes, s.dtype, s.shape)
 
+    def stacked(self, layer: int, proj: str) -> ExpertSlice:
+        """The stacked ``blk.{layer}.ffn_{proj}_exps`` tensor (expert 0's slice;
+        expert e at ``offset + e * expert_bytes``)."""
+        s = self._stacked.get((layer, proj))
+        if s is None:
+            raise KeyError(f"No stacked experts for layer {layer}, proj {proj}")
+        return s
+
+    def shared_slice(self, layer: int, proj: str) -> Optional[ExpertSlice]:
+        """The shared expert's matrix under the names GGUF conversions use
+        (``ffn_{proj}_shexp``, ``ffn_{proj}_shared``, ``ffn_{proj}``), as the
+        reference's ``load_shared_expert`` looks them up (ef_deepseek_mmap.py:611-639);
+        None when the layer has none."""
+        for name in (f"blk.{layer}.ffn_{proj}_shexp.weight", f"blk.{layer}.ffn_{proj}_shared.weight",
+                     f"blk.{layer}.ffn_{proj}.weight"):
+            t = self.tensors.get(name)
+            if t is not None:
+                fi = self.file_infos[t.file_idx]
+                return ExpertSlice(fi.path, fi.data_offset + t.offset, t.total_bytes, t.dtype, tuple(t.shape),
+                                   stacked=False)
+        return None
+
     def load_expert_raw(self, layer: int, e: int, proj: str = "gate"):
         """(raw bytes, dtype, shape) of one expert's matrix."""
         s = self.expert(layer, e, proj)

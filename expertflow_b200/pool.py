@@ -400,6 +400,29 @@ class ExpertSlotPool:
     def reset_stats(self) -> None:
         L.check(L.lib().ef_pool_reset_stats(self._h))
 
+    def record_routing(self, on: bool = True) -> None:
+        """Start (clearing the trace) or stop recording the routing trace."""
+        L.check(L.lib().ef_pool_record_routing(self._h, int(on)))
+
+    @property
+    def routing_trace(self) -> list:
+        """Per ended token, the (layer, expert) of every routed entry in
+        routing order -- the reference's ``expert_cache.routing_trace``
+        (ef_engine.py:222-229), the input of its Belady label computation."""
+        n_p, n_t = ctypes.c_longlong(), ctypes.c_longlong()
+        L.check(L.lib().ef_pool_routing_trace(self._h, None, 0, ctypes.byref(n_p), None, 0, ctypes.byref(n_t)))
+        pairs = (ctypes.c_int32 * max(1, 2 * n_p.value))()
+        ends = (ctypes.c_longlong * max(1, n_t.value))()
+        L.check(L.lib().ef_pool_routing_trace(self._h, ctypes.cast(pairs, ctypes.c_void_p), n_p.value,
+                                              ctypes.byref(n_p), ctypes.cast(ends, ctypes.c_void_p), n_t.value,
+                                              ctypes.byref(n_t)))
+        out, start = [], 0
+        for i in range(n_t.value):
+            end = int(ends[i])
+            out.append([(int(pairs[2 * j]), int(pairs[2 * j + 1])) for j in range(start, end)])
+            start = end
+        return out
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             L.lib().ef_pool_destroy(self._h)

@@ -33,6 +33,7 @@
  *   ef_slotpool_*         FrequencyWeightedCache get/put/trim              ef_engine.py:48-104
  *                         + mmap page-in of misses                        ef_engine.py:650-675
  *   ef_kquant_*           GGUF Q2_K/Q3_K/Q4_K decode (+ GEMV)              ef_deepseek_mmap.py:330-378,655-773
+ *   ef_kquant_moe_forward the MoE layer over GGUF K-quant experts          ef_deepseek_mmap.py:570-593,1563-1660
  *   ef_store_*            expert byte ranges read out of the checkpoint     ef_deepseek_mmap.py:431-570,
  *                         files on reader threads                          experiments/ef_v18_prefetch2.py:76-200
  */
@@ -382,6 +383,17 @@ ef_status ef_pool_decode_step(ef_slot_pool* pool, float* r, int T, const void* c
                               const float* const* e_bias, int lookahead, float eps, void* workspace,
                               size_t workspace_bytes, void* stream);
 ef_status ef_pool_resident(const ef_slot_pool* pool, int layer, int32_t* experts, int cap, int* n);
+/* Routing trace for offline training of the learned eviction predictor (the
+ * reference's record_routing / end_token / routing_trace, ef_engine.py:222-229,
+ * called at :643-646): while on, every ef_pool_moe_forward records (layer,
+ * expert) for each routed entry in (token, k) order and every
+ * ef_pool_end_token closes a token.  Turning it on clears the trace. */
+ef_status ef_pool_record_routing(ef_slot_pool* pool, int on);
+/* pairs [n_pairs][2] (layer, expert) in recording order; token_ends[i] = pairs
+ * recorded up to the end of token i.  Copies up to pair_cap pairs and tok_cap
+ * ends; n_pairs / n_tokens receive the full counts. */
+ef_status ef_pool_routing_trace(const ef_slot_pool* pool, int32_t* pairs, long long pair_cap, long long* n_pairs,
+                                long long* token_ends, long long tok_cap, long long* n_tokens);
 /* The learned policy's predictor for every layer of a pool created with
  * policy EF_POLICY_BELADY (same layout as ef_policy_set_predictor). */
 ef_status ef_pool_set_predictor(ef_slot_pool* pool, int hidden, const float* w1, const float* b1, const float* w2,
@@ -406,6 +418,31 @@ ef_status ef_kquant_dequantize(int type, const void* blocks, long long n_blocks,
 size_t ef_kquant_matmul_workspace_size(int T, int K);
 ef_status ef_kquant_matmul(const void* x, int act_dtype, int T, const void* blocks, int type, int N, int K, float* y,
                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* One stacked K-quant projection of a MoE layer: expert e's matrix (N rows of
+ * K/256 blocks, i.e. its slice of a GGML (K, N, E) tensor such as
+ * blk.{i}.ffn_gate_exps) starts at blocks + e * expert_stride bytes.  blocks
+ * and expert_stride 16-byte (Q4_K), 4-byte (Q2_K) or 2-byte (Q3_K) aligned. */
+typedef struct {
+  const void* blocks;
+  int type;                 /* EF_GGML_Q2_K / Q3_K / Q4_K */
+  long long expert_stride;  /* bytes; >= N * K / 256 * block bytes */
+} ef_kqweight;
+/* ef_moe_forward for experts stored as GGUF K-quant blocks (the reference's
+ * DeepSeek GGUF models): same router, permutation and combine; each routed
+ * (token, k) runs silu(x Wg^T) * (x Wu^T) Wd^T on the fp16 weights the
+ * reference's decoders give (ExpertMmapLoader.load_expert_dequantized,
+ * ef_deepseek_mmap.py:570-593; MoE forward :1563-1660), decoded inside the GEMV
+ * with fp32 accumulation.  cfg->bits / group_size are not used; hidden and
+ * inter must be multiples of 256; gate and up share one type, the shared
+ * expert's types match the routed ones.  Decode-size batches (the weights
+ * are streamed once per 8 routed rows of an expert). */
+size_t ef_kquant_moe_workspace_size(const ef_moe_cfg* cfg, int T);
+ef_status ef_kquant_moe_forward(const ef_moe_cfg* cfg, const void* x, int T, const void* gate_w,
+                                const float* e_bias, ef_kqweight gate, ef_kqweight up, ef_kqweight down,
+                                const ef_kqweight* shared_gate, const ef_kqweight* shared_up,
+                                const ef_kqweight* shared_down, void* y, int32_t* inds_out, float* wts_out,
+                                void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- cold tier: expert blobs read from the model files ----------------------------- */
 /* Expert e's copy of one stacked array (w, scales or biases of gate, up or

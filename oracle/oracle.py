@@ -493,3 +493,39 @@ def np_kquant_matmul(x: np.ndarray, raw, dtype: int, N: int, K: int) -> np.ndarr
     N * K / 256 K-quant blocks (row r = blocks [r K/256, (r+1) K/256))."""
     w = np_dequant_kquant(raw, dtype).astype(np.float64).reshape(N, K)
     return np.asarray(x, np.float64) @ w.T
+
+
+def np_kquant_moe_ffn(xf, inds, wts, gate, up, down, shared=None) -> np.ndarray:
+    """MoE FFN over K-quant experts: y [T, H] fp64 = sum_k wts[t, k] *
+    E_{inds[t, k]}(x[t]) (+ shared(x[t])) with E(v) = (silu(v Wg^T) * (v Wu^T)) Wd^T
+    on the fp16 matrices np_dequant_kquant decodes -- the reference's
+    load_expert_dequantized (ef_deepseek_mmap.py:570-593) feeding its MoE
+    forward (:1563-1660).  gate / up / down: (raw bytes of E stacked
+    matrices, GGML type, n_rows, n_cols); shared: the same triple for one
+    expert, or None."""
+    xf = np.asarray(xf, np.float64)
+    cache = {}
+
+    def mat(p, e):
+        raw, dt, rows, cols = p
+        key = (id(raw), e)
+        if key not in cache:
+            per = rows * (cols // 256) * KQ_BLOCK_BYTES[dt]
+            cache[key] = np_dequant_kquant(raw[e * per:(e + 1) * per], dt).astype(np.float64).reshape(rows, cols)
+        return cache[key]
+
+    def expert(mats, e, v):
+        g = v @ mat(mats[0], e).T
+        u = v @ mat(mats[1], e).T
+        h = g / (1.0 + np.exp(-g)) * u
+        return h @ mat(mats[2], e).T
+
+    T, k = inds.shape
+    y = np.zeros((T, xf.shape[1]), np.float64)
+    for t in range(T):
+        for j in range(k):
+            y[t] += float(wts[t, j]) * expert((gate, up, down), int(inds[t, j]), xf[t:t + 1])[0]
+        if shared is not None:
+            y[t] += expert(shared, 0, xf[t:t + 1])[0]
+    return y
+

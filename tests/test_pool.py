@@ -112,10 +112,13 @@ def test_pool_forward_matches_resident_layers_and_policy(P):
         m.gate = gates[layer]
         resident.append(m)
     pool = P.ExpertSlotPool(spec, host, budget=budget, headroom=spec.top_k)
+    pool.record_routing(True)
     ref_pol = [P.CachePolicy(budget, 0.95) for _ in range(n_layers)]
     acc = hits = 0
+    trace = []  # the reference's routing_trace: per token, (layer, expert) per routed entry
     for t in range(steps):
         x = synthetic.make_x_torch(spec, 1, seed=900 + t)
+        trace.append([])
         for layer in range(n_layers):
             inds = torch.empty((1, spec.top_k), dtype=torch.int32, device=dev)
             nxt = gates[layer + 1] if layer + 1 < n_layers else None
@@ -123,6 +126,7 @@ def test_pool_forward_matches_resident_layers_and_policy(P):
             y_ref = resident[layer](x, out_dtype=torch.float32)
             torch.cuda.synchronize()
             assert torch.equal(y, y_ref), (t, layer)
+            trace[-1].extend((layer, int(e)) for e in inds.flatten().tolist())
             for e in sorted(set(inds.flatten().tolist())):
                 acc += 1
                 if ref_pol[layer].get(e):
@@ -140,6 +144,8 @@ def test_pool_forward_matches_resident_layers_and_policy(P):
     eb = spec.expert_bytes()
     assert st["h2d_bytes"] == (st["copies_sync"] + st["copies_prefetch"]) * eb
     assert st["tokens"] == steps and st["copies_prefetch"] > 0 and st["copy_ms"] > 0
+    assert pool.routing_trace == trace
+    pool.record_routing(False)
     from expertflow_b200.moe import device_error
     assert device_error() == 0
     pool.close()
