@@ -34,8 +34,12 @@ def _kq_layer(spec, tg, td, seed):
     rng = np.random.default_rng(seed)
     E, H, I = spec.n_experts, spec.hidden, spec.inter
 
+    # super-block scales that give weights of about 0.02 in magnitude, as in
+    # real checkpoints (the code and sub-scale ranges differ per format)
+    d_scale = {Q2: 0.002, Q3: 0.0006, Q4: 0.0001}
+
     def proj(t, rows, cols, n):
-        return (G.random_kquant_blocks(t, n * rows * cols // 256, rng, d_scale=0.0005), t, rows, cols)
+        return (G.random_kquant_blocks(t, n * rows * cols // 256, rng, d_scale=d_scale[t]), t, rows, cols)
 
     layer = {"gate": proj(tg, I, H, E), "up": proj(tg, I, H, E), "down": proj(td, H, I, E),
              "gate_w": rng.normal(0, spec.gate_std, (E, H)).astype(np.float16),
