@@ -564,6 +564,80 @@ def section_kquant(args, dev, peaks):
                                   "bits_per_weight": round(8 * bb / 256, 3)})
         del w, wb
         torch.cuda.empty_cache()
+    out["moe"] = section_kquant_moe(args, dev, peaks)
+    return out
+
+
+def section_kquant_moe(args, dev, peaks):
+    """The whole DeepSeek-V3-shaped MoE layer over GGUF K-quant experts
+    (ef_kquant_moe_forward): 256 experts + shared, Q2_K gate/up and Q3_K down
+    (a common mix in the reference's DeepSeek GGUF models), seeded blocks.
+    Layer tokens/s (CUDA events around each forward) and the gate/up kernel's
+    GB/s over the blocks of the distinct experts it ran."""
+    import torch
+    from expertflow_b200 import gguf as G, kquant as KQ, moe, synthetic, _lib
+    from expertflow_b200.spec import DEEPSEEK_V3
+
+    spec = DEEPSEEK_V3
+    E, H, I = spec.n_experts, spec.hidden, spec.inter
+    tg, td = G.GGML_TYPE_Q2_K, G.GGML_TYPE_Q3_K
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+
+    def proj(t, rows, cols, n, d_scale):
+        bb = G.GGML_BLOCK_SIZES[t][1]
+        raw = torch.randint(0, 256, (n * rows * (cols // 256), bb), dtype=torch.uint8, device=dev, generator=g)
+        d = (torch.randn(raw.shape[0], device=dev, generator=g).abs() * d_scale).to(torch.float16)
+        off = {G.GGML_TYPE_Q2_K: (80, 82), G.GGML_TYPE_Q3_K: (108,)}[t]
+        for o in off:
+            raw[:, o:o + 2] = d.view(torch.uint8).view(-1, 2)
+        return KQ.KQuantProj(raw.reshape(-1), t, rows, cols, n)
+
+    sc = {tg: 0.002, td: 0.0006}
+    gate_w = (torch.randn((E, H), device=dev, generator=g) * spec.gate_std).to(torch.float16)
+    e_bias = (torch.randn(E, device=dev, generator=g) * 0.01).float()
+    gate = moe.MoEGate(gate_w, spec.top_k, spec.router, spec.norm_topk, spec.n_group, spec.topk_group,
+                       spec.routed_scaling, e_bias)
+    m = KQ.KQuantMoELayer(gate, proj(tg, I, H, E, sc[tg]), proj(tg, I, H, E, sc[tg]), proj(td, H, I, E, sc[td]),
+                          shared=(proj(tg, I, H, 1, sc[tg]), proj(tg, I, H, 1, sc[tg]), proj(td, H, I, 1, sc[td])))
+    gu_bytes = 2 * I * (H // 256) * G.GGML_BLOCK_SIZES[tg][1]
+    out = {"workload": "deepseek-v3 layer over GGUF K-quant experts (Q2_K gate/up, Q3_K down), 256 experts + "
+                       "shared", "layer_bytes": int(m.gate_proj.blocks.numel() * 2 + m.down_proj.blocks.numel()),
+           "points": []}
+    for T in (1, 8, 32):
+        # eight batches in rotation route to different experts, so a forward
+        # does not find the previous one's weights in L2
+        xs = [synthetic.make_x_torch(spec, T, seed=5 + i, device=dev) for i in range(8)]
+        x = xs[0]
+        inds = torch.empty((T, spec.top_k), dtype=torch.int32, device=dev)
+        m(x, inds_out=inds)
+        n_u = int(torch.unique(inds).numel())
+        for i in range(max(3, args.warmup)):
+            m(xs[i % 8])
+        torch.cuda.synchronize()
+        reps = max(16, args.steps)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            m(xs[i % 8])
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        m(xs[1])
+        _lib.trace_enable(True)
+        _lib.trace_read()
+        m(x)
+        torch.cuda.synchronize()
+        by = _by_kernel(_lib.trace_read())
+        _lib.trace_enable(False)
+        k_ms = by["kq_gate_up"][0]
+        gbs = (n_u + 1) * gu_bytes / (k_ms * 1e-3) / 1e9
+        out["points"].append({"tokens": T, "tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
+                              "unique_experts": n_u, "kq_gate_up_ms": round(k_ms, 4),
+                              "kq_gate_up_gbs": round(gbs, 1), "kq_gate_up_frac": round(gbs / peaks["hbm"], 4),
+                              "kernel_ms": {k: round(v[0], 4) for k, v in by.items()}})
+    del m
+    torch.cuda.empty_cache()
     return out
 
 
@@ -901,6 +975,9 @@ def _summary(line, sections):
     kq = sections.get("kq")
     if kq:
         out["kq"] = {f"{p['format']}_T{p['tokens']}": p["frac"] for p in kq["points"] if p["tokens"] == 1}
+        if kq.get("moe"):
+            out["kq_moe"] = {f"T{p['tokens']}": {"tok_s": p["tokens_per_s"], "gate_up_frac": p["kq_gate_up_frac"]}
+                             for p in kq["moe"]["points"]}
     return out
 
 

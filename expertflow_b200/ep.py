@@ -293,3 +293,36 @@ class CapturedEpForward:
             self.x.copy_(x.reshape(self.x.shape), non_blocking=True)
         self.graph.replay()
         return self.y
+
+
+def _main(argv=None) -> None:
+    """A one-rank peer-memory expert-parallel layer of the DeepSeek-V3 shape on
+    cuda:0 (every exchange kernel runs; the peer stores land in this GPU's own
+    buffer), for profiling:  python -m expertflow_b200.ep --tokens 32 --reps 5"""
+    import argparse
+
+    from . import synthetic
+    from .spec import DEEPSEEK_V3
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--tokens", type=int, default=32)
+    ap.add_argument("--reps", type=int, default=5)
+    a = ap.parse_args(argv)
+    spec = DEEPSEEK_V3
+    layer = synthetic.make_layer_torch(spec, seed=1, device="cuda")
+    m = PeerExpertParallelMoE(spec, shard_layer(spec, layer, 0, 1), max_tokens=a.tokens)
+    del layer
+    x = synthetic.make_x_torch(spec, a.tokens, seed=2, device="cuda")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(a.reps):
+        if i == a.reps - 1:
+            e0.record()
+        m(x)
+    e1.record()
+    torch.cuda.synchronize()
+    print(f"{a.tokens} tokens: last forward {e0.elapsed_time(e1) * 1e3:.1f} us")
+    m.close()
+
+
+if __name__ == "__main__":
+    _main()
