@@ -185,6 +185,23 @@ EF_DEV uint32_t* slot_u32(uint8_t* base, unsigned long long off, int i) {
   return reinterpret_cast<uint32_t*>(base + off + (size_t)i * 64);
 }
 
+// One warp copies n16 16-byte units src -> dst (dst may be a peer GPU's
+// memory): each lane issues kCopyBatch independent loads before its stores,
+// so a row's loads overlap instead of waiting one round trip each.
+constexpr int kCopyBatch = 8;
+constexpr int kRowParts = 4;  // warps per copied row
+EF_DEV void warp_copy16(uint4* dst, const uint4* src, int n16, int lane) {
+  for (int c0 = lane; c0 < n16; c0 += 32 * kCopyBatch) {
+    uint4 v[kCopyBatch];
+#pragma unroll
+    for (int u = 0; u < kCopyBatch; ++u)
+      if (c0 + 32 * u < n16) v[u] = src[c0 + 32 * u];
+#pragma unroll
+    for (int u = 0; u < kCopyBatch; ++u)
+      if (c0 + 32 * u < n16) dst[c0 + 32 * u] = v[u];
+  }
+}
+
 // The last CTA of a grid to get here returns true (all CTAs' earlier global
 // stores, peer stores included, are then visible system-wide); counter reset.
 EF_DEV bool last_cta(uint32_t* ctr, int* s_last) {
@@ -215,9 +232,12 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
   const int h16 = g.H / 8;
+  const int part16 = (h16 + kRowParts - 1) / kRowParts;  // 16-byte units per warp's part of a row
   const uint4* xs = reinterpret_cast<const uint4*>(x);
   const size_t row_bytes = (size_t)g.H * 2;
-  for (int p = blockIdx.x * wpb + warp; p < n; p += gridDim.x * wpb) {
+  // work unit = (sorted routed row p, part) and then (own token t, part)
+  for (int wu = blockIdx.x * wpb + warp; wu < n * kRowParts; wu += gridDim.x * wpb) {
+    const int p = wu / kRowParts, part = wu - p * kRowParts;
     int lo = 0, hi = E;  // the expert of sorted row p: s_off[lo] <= p < s_off[hi]
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
@@ -232,15 +252,19 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
     uint8_t* db = peers.base[d];
     uint4* dst = reinterpret_cast<uint4*>(db + g.off_rows + ((size_t)g.rank * g.rmax + q) * row_bytes);
     const uint4* src = xs + (size_t)__ldg(row_src + p) * h16;
-    for (int c = lane; c < h16; c += 32) dst[c] = src[c];
-    if (lane == 0) reinterpret_cast<int2*>(db + g.off_meta)[(size_t)g.rank * g.rmax + q] = make_int2(le, p);
+    const int c0 = part * part16;
+    warp_copy16(dst + c0, src + c0, min(part16, h16 - c0), lane);
+    if (lane == 0 && part == 0)
+      reinterpret_cast<int2*>(db + g.off_meta)[(size_t)g.rank * g.rmax + q] = make_int2(le, p);
   }
   if (g.has_shared) {  // this rank's own tokens, for its shared-expert bin
     uint8_t* ob = peers.base[g.rank];
-    for (int t = blockIdx.x * wpb + warp; t < g.T; t += gridDim.x * wpb) {
+    for (int wu = blockIdx.x * wpb + warp; wu < g.T * kRowParts; wu += gridDim.x * wpb) {
+      const int t = wu / kRowParts, part = wu - t * kRowParts;
       uint4* dst = reinterpret_cast<uint4*>(ob + g.off_rows + ((size_t)g.P * g.rmax + t) * row_bytes);
       const uint4* src = xs + (size_t)t * h16;
-      for (int c = lane; c < h16; c += 32) dst[c] = src[c];
+      const int c0 = part * part16;
+      warp_copy16(dst + c0, src + c0, min(part16, h16 - c0), lane);
     }
   }
   if (!last_cta(&g.ctr[0], &s_last)) return;
@@ -331,14 +355,17 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const __grid_constant__ 
   const uint32_t ep = *reinterpret_cast<const volatile uint32_t*>(g.epoch);
   const int n = min(max(*n_rows_dev, 0), max_rows);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
-  const int h4 = g.H / 4;
+  const int h16 = g.H / 4;  // 16-byte units of an fp32 row
+  const int part16 = (h16 + kRowParts - 1) / kRowParts;
   const int back_rows = g.max_tokens * g.k + g.max_tokens;
-  for (int q = blockIdx.x * wpb + warp; q < n; q += gridDim.x * wpb) {
+  for (int wu = blockIdx.x * wpb + warp; wu < n * kRowParts; wu += gridDim.x * wpb) {
+    const int q = wu / kRowParts, part = wu - q * kRowParts;
     const int s = __ldg(ret_rank + q), p = __ldg(ret_row + q);
     if (s < 0 || s >= g.P || p < 0 || p >= back_rows) continue;  // recorded by ep_recv_kernel
-    float4* dst = reinterpret_cast<float4*>(peers.base[s] + g.off_back + (size_t)p * g.H * 4);
-    const float4* src = reinterpret_cast<const float4*>(yrows + (size_t)q * g.H);
-    for (int c = lane; c < h4; c += 32) dst[c] = src[c];
+    uint4* dst = reinterpret_cast<uint4*>(peers.base[s] + g.off_back + (size_t)p * g.H * 4);
+    const uint4* src = reinterpret_cast<const uint4*>(yrows + (size_t)q * g.H);
+    const int c0 = part * part16;
+    warp_copy16(dst + c0, src + c0, min(part16, h16 - c0), lane);
   }
   if (!last_cta(&g.ctr[1], &s_last)) return;
   if (threadIdx.x < g.P) st_release_sys(slot_u32(peers.base[threadIdx.x], g.off_done, g.rank), ep);
@@ -598,7 +625,7 @@ extern "C" ef_status ef_ep_forward(ef_ep_group* g, const void* x, int T, const v
   }
   {
     const int rows = T * k + (cfg->n_shared ? T : 0);
-    const int blocks = std::max(1, std::min((rows + 7) / 8, 2 * nsm));
+    const int blocks = std::max(1, std::min((rows * ef::kRowParts + 7) / 8, 4 * nsm));
     EF_LAUNCH("ep_dispatch", launch_pdl(ef::ep_dispatch_kernel, blocks, 256, 0, st, g->peers, G,
                                         static_cast<const uint16_t*>(x), (const int*)w.own.row_src,
                                         (const int*)w.own.offsets));
@@ -624,7 +651,7 @@ extern "C" ef_status ef_ep_forward(ef_ep_group* g, const void* x, int T, const v
     return s;
   }
   {
-    const int blocks = std::max(1, std::min((nr_max + 7) / 8, 2 * nsm));
+    const int blocks = std::max(1, std::min((nr_max * ef::kRowParts + 7) / 8, 4 * nsm));
     EF_LAUNCH("ep_return", launch_pdl(ef::ep_return_kernel, blocks, 256, 0, st, g->peers, G,
                                       (const float*)w.f.yrows, (const int*)w.ret_rank, (const int*)w.ret_row,
                                       (const int*)w.n_rows, nr_max));
