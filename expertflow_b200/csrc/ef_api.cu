@@ -606,7 +606,7 @@ static ef_status moe_tail(const ef_moe_cfg* cfg, const void* x, int T, const int
   const bool bf = cfg->act_dtype == EF_DT_BF16;
   const int n_sh = cfg->n_shared ? T : 0;
   const bool gemm = use_gemm(cfg, T * k + n_sh, T * k);
-  EF_LAUNCH("permute", launch_permute(inds, T * k, k, E, n_sh, gemm ? kGemmSegRows : kTokChunk, f.pb, st));
+  EF_LAUNCH("permute", launch_permute(inds, T * k, k, E, n_sh, gemm ? kGemmSegRows : kSegRows, f.pb, st));
   EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), f.pb.row_src, bf, T * k + n_sh, H, cfg->bits,
                                         f.x16, f.xsum, st));
   if (gemm) {
@@ -710,7 +710,7 @@ ef_status ef_moe_experts_forward(const ef_moe_cfg* cfg, const void* x_rows, int 
   carve_ffn(c, N, cfg->n_experts + 1, N, cfg->hidden, cfg->inter, f);
   const bool bf = cfg->act_dtype == EF_DT_BF16;
   const bool gemm = use_gemm(cfg, N, N);
-  EF_LAUNCH("permute", launch_permute(row_expert, N, 1, cfg->n_experts, 0, gemm ? kGemmSegRows : kTokChunk, f.pb, st));
+  EF_LAUNCH("permute", launch_permute(row_expert, N, 1, cfg->n_experts, 0, gemm ? kGemmSegRows : kSegRows, f.pb, st));
   EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x_rows), f.pb.row_src, bf, N, cfg->hidden,
                                         cfg->bits, f.x16, f.xsum, st));
   if (gemm) {
@@ -795,7 +795,7 @@ ef_status ef_quantized_matmul(const void* x, int act_dtype, int M, const uint32_
   qmm_ws(M, 1, 1, out_dim, in_dim, c, f, M);
   int* ids = f.ids;
   EF_CUDA(cudaMemsetAsync(ids, 0, sizeof(int) * (size_t)M, st));
-  EF_LAUNCH("permute", launch_permute(ids, M, 1, 1, 0, kTokChunk, f.pb, st));
+  EF_LAUNCH("permute", launch_permute(ids, M, 1, 1, 0, kSegRows, f.pb, st));
   EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), f.pb.row_src, act_dtype == EF_DT_BF16, M,
                                         in_dim, bits, f.x16, f.xsum, st));
   if ((s = run_single_matrix(q, 1, out_dim, in_dim, bits, f, M, st))) return s;
@@ -826,7 +826,7 @@ ef_status ef_gather_qmm(const void* x, int act_dtype, int T, const int32_t* indi
   Carver c{static_cast<uint8_t*>(workspace)};
   FfnBufs f;
   qmm_ws(T, k, n_experts, out_dim, in_dim, c, f, T);
-  EF_LAUNCH("permute", launch_permute(indices, T * k, k, n_experts, 0, kTokChunk, f.pb, st));
+  EF_LAUNCH("permute", launch_permute(indices, T * k, k, n_experts, 0, kSegRows, f.pb, st));
   EF_LAUNCH("prep_act", launch_prep_act(static_cast<const uint16_t*>(x), f.pb.row_src, act_dtype == EF_DT_BF16,
                                         T * k, in_dim, bits, f.x16, f.xsum, st));
   if ((s = run_single_matrix(w, n_experts, out_dim, in_dim, bits, f, T * k, st))) return s;

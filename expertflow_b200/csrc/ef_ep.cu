@@ -636,7 +636,7 @@ extern "C" ef_status ef_ep_forward(ef_ep_group* g, const void* x, int T, const v
     EF_LAUNCH("ep_recv", (set_max_smem_once(ef::ep_recv_kernel, 160 * 1024, attr_set) != cudaSuccess
                               ? cudaGetLastError()
                               : launch_pdl(ef::ep_recv_kernel, 1, ef::kPermThreads, smem, st, G,
-                                           (const uint8_t*)g->base, gemm ? kGemmSegRows : kTokChunk, w.f.pb,
+                                           (const uint8_t*)g->base, gemm ? kGemmSegRows : kSegRows, w.f.pb,
                                            w.ret_rank, w.ret_row, w.n_rows)));
   }
   const uint16_t* recv_rows = reinterpret_cast<const uint16_t*>(g->base + G.off_rows);

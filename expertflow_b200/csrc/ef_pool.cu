@@ -358,6 +358,24 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
 
 }  // namespace ef
 
+namespace ef {
+// The routed (and predicted) expert ids of a pool step -> mapped pinned host
+// memory, then `seq` into the host flag once they are visible there.
+__global__ void publish_ids_kernel(const int* __restrict__ inds, const int* __restrict__ pred, int n,
+                                   int* h_inds, int* h_pred, uint32_t* h_flag, uint32_t seq) {
+  pdl_wait();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    h_inds[i] = inds[i];
+    if (pred) h_pred[i] = pred[i];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    st_release_sys(h_flag, seq);
+  }
+}
+}  // namespace ef
+
 struct ef_slot_pool {
   ef_moe_cfg cfg;
   ef_pool_cfg pc;
@@ -380,9 +398,12 @@ struct ef_slot_pool {
   ef::ScatterParams scat{};                // blob layout, copied into each lane's batch
   std::vector<ef::LayerSlots> layers;
   uint8_t* dev_mem = nullptr;
-  int32_t* h_inds = nullptr;               // pinned staging: routed ids, predicted ids, slot ids
+  int32_t* h_inds = nullptr;               // mapped pinned staging: routed ids, predicted ids, slot ids, flag
   int32_t* h_pred = nullptr;
   int32_t* h_slot = nullptr;
+  int32_t* d_inds = nullptr;               // the same staging as the device addresses it
+  uint32_t* h_flag = nullptr;              // sequence number of the last published routing
+  uint32_t h_seq = 0;
   int h_cap = 0;
   ef_pool_stats st{};
   // routing trace (ef_pool_record_routing): (layer, expert) pairs in routing
@@ -658,6 +679,26 @@ size_t pool_ws(const ef_slot_pool* P, int T, Carver& c, PoolWs& w) {
 
 // Routes x through gate gw (and, when gw2, the next layer's gate gw2 in the same
 // two launches: that routing is the lookahead prediction).
+// Polls the host flag until the routing of step `seq` is published (bounded:
+// the stream's errors are checked every millisecond or so, and 30 s without
+// the flag is an error).
+ef_status wait_published(const uint32_t* flag, uint32_t seq, cudaStream_t st) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (uint32_t i = 0;; ++i) {
+    if ((int)(*reinterpret_cast<const volatile uint32_t*>(flag) - seq) >= 0) break;
+    if ((i & 4095u) == 4095u) {
+      const cudaError_t e = cudaStreamQuery(st);
+      if (e != cudaSuccess && e != cudaErrorNotReady) return fail(EF_ERR_CUDA, "routing failed: %s", cudaGetErrorString(e));
+      if (e == cudaSuccess && (int)(*reinterpret_cast<const volatile uint32_t*>(flag) - seq) < 0)
+        return fail(EF_ERR_CUDA, "routing finished without publishing its ids");
+      if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(30))
+        return fail(EF_ERR_TIMEOUT, "routing ids not published within 30 s");
+    }
+  }
+  std::atomic_thread_fence(std::memory_order_acquire);
+  return EF_OK;
+}
+
 ef_status pool_route(const ef_moe_cfg& cfg, const void* x, int T, const void* gw, const float* eb, float* logits, int* inds,
                      float* wts, const void* gw2, const float* eb2, float* logits2, int* inds2, float* wts2,
                      cudaStream_t st) {
@@ -932,19 +973,33 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
                       w.pwts, st)))
     return s;
   if (n > P->h_cap) {
-    if (P->h_inds) cudaFreeHost(P->h_inds);
+    if (P->h_inds) {
+      cudaStreamSynchronize(st);  // no earlier layer still reads the old staging
+      cudaFreeHost(P->h_inds);
+    }
     P->h_cap = std::max(n, 256);
-    if (cudaMallocHost(&P->h_inds, 3 * sizeof(int32_t) * P->h_cap) != cudaSuccess) {
+    if (cudaHostAlloc(reinterpret_cast<void**>(&P->h_inds), 3 * sizeof(int32_t) * P->h_cap + 64,
+                      cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer(reinterpret_cast<void**>(&P->d_inds), P->h_inds, 0) != cudaSuccess) {
+      if (P->h_inds) cudaFreeHost(P->h_inds);
       P->h_inds = nullptr;
       P->h_cap = 0;
-      return fail(EF_ERR_CUDA, "pinned staging allocation failed");
+      return fail(EF_ERR_CUDA, "mapped pinned staging allocation failed");
     }
+    P->h_flag = reinterpret_cast<uint32_t*>(P->h_inds + 3 * P->h_cap);
+    *reinterpret_cast<volatile uint32_t*>(P->h_flag) = P->h_seq;
   }
   P->h_pred = P->h_inds + P->h_cap;
   P->h_slot = P->h_inds + 2 * P->h_cap;
-  cudaMemcpyAsync(P->h_inds, inds, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
-  if (next_gate_w) cudaMemcpyAsync(P->h_pred, w.pinds, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
-  if (cudaStreamSynchronize(st) != cudaSuccess) return fail(EF_ERR_CUDA, "routing failed: %s", cudaGetErrorString(cudaGetLastError()));
+  // the routing reaches the host through the mapped staging: a one-CTA kernel
+  // stores the ids there and then the step's sequence number, which this
+  // thread polls (no copy launch, no stream synchronisation)
+  const uint32_t seq = ++P->h_seq;
+  EF_LAUNCH("publish_ids", launch_pdl(ef::publish_ids_kernel, 1, 256, 0, st, (const int*)inds,
+                                      (const int*)(next_gate_w ? w.pinds : nullptr), n, P->d_inds,
+                                      P->d_inds + P->h_cap, reinterpret_cast<uint32_t*>(P->d_inds + 3 * P->h_cap),
+                                      seq));
+  if ((s = wait_published(P->h_flag, seq, st))) return s;
   if (P->rec_on)  // the reference records each routed entry in (token, k) order (ef_engine.py:640-646)
     for (int i = 0; i < n; ++i) {
       P->rec_pairs.push_back(layer);

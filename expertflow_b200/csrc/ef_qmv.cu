@@ -4,7 +4,9 @@
 // (gate, up, silu*up, down) for small token counts, where the layer is bound by
 // HBM bandwidth on the packed weights.
 //
-// Work item = (segment of <= 8 rows routed to one expert) x (64 weight rows).
+// Work item = (segment of <= 16 rows routed to one expert) x (64 weight rows);
+// a segment of more than 8 rows is two MMA n-tiles that share every unpacked
+// code, so the expert's weights pass through the SM once for up to 16 tokens.
 // A CTA has 4 compute warps (16 rows each), a TMA producer warp and a scale
 // producer warp, and loops over work items (persistent; two CTAs per SM).
 //  * The TMA warp streams, per 256-column (4-bit) / 128-column (8-bit) stage,
@@ -53,8 +55,9 @@ struct QmvShape {
   static constexpr int NMAT = MODE == 1 ? 1 : 2;
   static constexpr int ITEM_ROWS = MODE == 2 ? 2 * kRowTile : kRowTile;  // weight rows per work item
   static constexpr int CODE_BYTES = NMAT * kRowTile * ROWB;
-  static constexpr int ACT_BOX = kTokChunk * 128;     // one 64-column group of 8 activation rows
-  static constexpr int ACT_BYTES = GPS * ACT_BOX;
+  static constexpr int ACT_BOX = kTokChunk * 128;     // one 64-column group of 8 activation rows (a TMA box)
+  static constexpr int ACT_GROUP = kSegRows * 128;    // a group's rows of both n-tiles
+  static constexpr int ACT_BYTES = GPS * ACT_GROUP;
   static constexpr int STAGE_BYTES = ((CODE_BYTES + ACT_BYTES) + 1023) / 1024 * 1024;
 };
 constexpr float kQ = 1024.0f;
@@ -71,12 +74,12 @@ __host__ __device__ constexpr int row_of_lane(int g) {
 
 // ---- scale slots
 // Chunked: [2 * NMAT arrays][64 rows][32 groups] fp16 in the TMA's 64-byte
-// swizzle (a 4 KB box per array), then the group sums [8 tokens][36] fp32
-// (pitch padded against bank conflicts).  Whole item: [2 * NMAT][64][K / 64]
-// fp16 and [8][sum_ld(K)] fp32, both as contiguous copies.
+// swizzle (a 4 KB box per array), then the group sums [16 tokens][32] fp32.
+// Whole item: [2 * NMAT][64][K / 64] fp16 and [16][sum_ld(K)] fp32, both as
+// contiguous copies.
 constexpr int kSbChunk = 32;                          // groups per chunk
 constexpr int kSbBox = kRowTile * kSbChunk * 2;       // bytes of one array's box
-constexpr int kXsPitchChunk = kSbChunk + 4;           // floats
+constexpr int kXsPitchChunk = kSbChunk;               // floats (unpadded: the smem budget has no room for a pad)
 
 template <int BITS, int MODE>
 __host__ __device__ inline size_t qmv_slot_bytes(int K, bool chunked) {
@@ -84,26 +87,31 @@ __host__ __device__ inline size_t qmv_slot_bytes(int K, bool chunked) {
   size_t sb, xs;
   if (chunked) {
     sb = (size_t)2 * NM * kSbBox;
-    xs = (size_t)kTokChunk * kXsPitchChunk * 4;
+    xs = (size_t)kSegRows * kXsPitchChunk * 4;
   } else {
     sb = (size_t)2 * NM * kRowTile * (K / 64) * 2;
-    xs = (size_t)kTokChunk * sum_ld(K) * 4;
+    xs = (size_t)kSegRows * sum_ld(K) * 4;
   }
   const size_t b = (sb + 127) / 128 * 128 + (xs + 127) / 128 * 128;
   return (b + 1023) / 1024 * 1024;  // slots stay 1024-byte aligned (swizzle atoms)
 }
 
-// Shared memory: `ns` pipeline stages, `nq` scale slots, the double-buffered
-// h staging tile and its per-warp sums, and the barriers.
+// Shared memory: `ns` pipeline stages, `nq` scale slots, in mode 0 the
+// double-buffered h staging tile and its per-warp sums, and the barriers.
+// The dynamic shared memory starts 1024-byte aligned (checked by the kernel),
+// so no alignment slack is reserved: three 24 KB stages must fit beside the
+// scale slots in the 113 KB a CTA has at two CTAs per SM.
 template <int BITS, int MODE>
 __host__ __device__ inline size_t qmv_smem_bytes(int K, int ns, int nq, bool chunked) {
   using S = QmvShape<BITS, MODE>;
-  size_t b = 1024;  // alignment slack
+  size_t b = 0;
   b += (size_t)ns * S::STAGE_BYTES;
   b += (size_t)nq * qmv_slot_bytes<BITS, MODE>(K, chunked);
-  b += (size_t)2 * kTokChunk * kRowTile * 2;       // h staging (mode 0)
-  b += (size_t)2 * kComputeWarps * kTokChunk * 4;  // h sums
-  b += 256;                                        // barriers: 2 ns + 2 nq + 4
+  if (MODE == 0) {
+    b += (size_t)2 * kSegRows * kRowTile * 2;       // h staging
+    b += (size_t)2 * kComputeWarps * kSegRows * 4;  // h sums
+  }
+  b += 256;                                         // barriers: 2 ns + 2 nq + 4
   return b;
 }
 
@@ -200,12 +208,17 @@ EF_DEV GroupCodes<BITS> load_group_codes(const uint8_t* cm, int G, int rA, int r
 }
 
 // Dot products of one 64-column group for rows rA, rB of matrix m and the
-// segment's 8 tokens; folds the group's affine scale into y (sA, sB: scales;
-// bA, bB: bias - 1024 * scale; x0, x1: the group sums of tokens 2t, 2t + 1).
-template <int BITS, int MODE>
-EF_DEV void qmv_group_regs(const GroupCodes<BITS>& cw, const uint4 (&blk)[2], float sA, float sB, float bA, float bB,
-                           float x0, float x1, float (&y)[4]) {
+// segment's tokens 0..7 (blk) and, when `two`, its tokens 8..15 (blk2): the
+// codes are unpacked once and feed both n-tiles.  Folds the group's affine
+// scale into y / y2 (sA, sB: scales; bA, bB: bias - 1024 * scale; x0, x1: the
+// group sums of tokens 2t, 2t + 1; x2, x3: of tokens 8 + 2t, 9 + 2t).  `two`
+// is uniform across the warp.
+template <int BITS>
+EF_DEV void qmv_group_regs(const GroupCodes<BITS>& cw, const uint4 (&blk)[2], const uint4 (&blk2)[2], bool two,
+                           float sA, float sB, float bA, float bB, float x0, float x1, float x2, float x3,
+                           float (&y)[4], float (&y2)[4]) {
   float D[4] = {0.f, 0.f, 0.f, 0.f};
+  float E[4] = {0.f, 0.f, 0.f, 0.f};
   if constexpr (BITS == 4) {
     const uint2 va = make_uint2(cw.a.x, cw.a.y), vb = make_uint2(cw.b.x, cw.b.y);
 #pragma unroll
@@ -218,6 +231,10 @@ EF_DEV void qmv_group_regs(const GroupCodes<BITS>& cw, const uint4 (&blk)[2], fl
                               mag(wb >> 12, 0x000F000Fu)};
       mma_16816(D, a0, blk[h].x, blk[h].y);
       mma_16816(D, a1, blk[h].z, blk[h].w);
+      if (two) {
+        mma_16816(E, a0, blk2[h].x, blk2[h].y);
+        mma_16816(E, a1, blk2[h].z, blk2[h].w);
+      }
     }
   } else {
     const uint4 va = cw.a, vb = cw.b;
@@ -231,12 +248,34 @@ EF_DEV void qmv_group_regs(const GroupCodes<BITS>& cw, const uint4 (&blk)[2], fl
       const uint32_t a1[4] = {mag8(wa0, 0x4341u), mag8(wb0, 0x4341u), mag8(wa1, 0x4341u), mag8(wb1, 0x4341u)};
       mma_16816(D, a0, blk[h].x, blk[h].y);
       mma_16816(D, a1, blk[h].z, blk[h].w);
+      if (two) {
+        mma_16816(E, a0, blk2[h].x, blk2[h].y);
+        mma_16816(E, a1, blk2[h].z, blk2[h].w);
+      }
     }
   }
   y[0] = fmaf(sA, D[0], fmaf(bA, x0, y[0]));
   y[1] = fmaf(sA, D[1], fmaf(bA, x1, y[1]));
   y[2] = fmaf(sB, D[2], fmaf(bB, x0, y[2]));
   y[3] = fmaf(sB, D[3], fmaf(bB, x1, y[3]));
+  if (two) {
+    y2[0] = fmaf(sA, E[0], fmaf(bA, x2, y2[0]));
+    y2[1] = fmaf(sA, E[1], fmaf(bA, x3, y2[1]));
+    y2[2] = fmaf(sB, E[2], fmaf(bB, x2, y2[2]));
+    y2[3] = fmaf(sB, E[3], fmaf(bB, x3, y2[3]));
+  }
+}
+
+// fp16 word G of N packed consecutive fp16 values (N = 4: a uint2; N = 2: in .x)
+template <int N>
+EF_DEV uint16_t h16_at(const uint2& v, int G) {
+  const uint32_t w = (N == 4 && G >= 2) ? v.y : v.x;
+  return (uint16_t)(w >> ((G & 1) * 16));
+}
+template <int N>
+EF_DEV uint2 load_h16_pack(const uint16_t* p) {
+  if constexpr (N == 4) return *reinterpret_cast<const uint2*>(p);
+  else return make_uint2(*reinterpret_cast<const uint32_t*>(p), 0u);
 }
 
 // Scale warp, mode 0: copy item e's staged h tile to h_out and its per-token
@@ -250,8 +289,8 @@ EF_DEV bool qmv_h_out(const QmvParams& p, const QmvSmem& sm, const WorkItem& it,
   if (lane == 0) ok = mbar_wait(&sm.h_ready[b], (e >> 1) & 1u, kDevErrTimeoutFull);
   ok = __shfl_sync(0xffffffffu, ok, 0);
   if (!ok) return false;
-  const uint16_t* s_h = sm.s_h + (size_t)b * kTokChunk * kRowTile;
-  const float* s_hs = sm.hsum + (size_t)b * kComputeWarps * kTokChunk;
+  const uint16_t* s_h = sm.s_h + (size_t)b * kSegRows * kRowTile;
+  const float* s_hs = sm.hsum + (size_t)b * kComputeWarps * kSegRows;
   const int R = p.R, row0 = it.rt * kRowTile;
   for (int c = lane; c < it.nrows * 8; c += 32) {
     const int tok = c >> 3, part = c & 7;
@@ -261,7 +300,7 @@ EF_DEV bool qmv_h_out(const QmvParams& p, const QmvSmem& sm, const WorkItem& it,
   if (lane < it.nrows) {
     float s = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kComputeWarps; ++w) s += s_hs[w * kTokChunk + lane];
+    for (int w = 0; w < kComputeWarps; ++w) s += s_hs[w * kSegRows + lane];
     p.hsum_out[(size_t)(it.row0_seg + lane) * sum_ld(R) + it.rt] = s;
   }
   __syncwarp();
@@ -287,7 +326,9 @@ EF_DEV SbGeom sb_geom(const QmvParams& p, int nstages) {
 }
 
 // One work item for one compute warp; `cc` counts the scale chunks consumed.
-// Returns false after a failed wait.
+// A segment of more than 8 rows runs its tokens 8..15 as a second n-tile on
+// the same unpacked codes (`two`, uniform across the CTA).  Returns false after
+// a failed wait.
 template <int BITS, int MODE>
 EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, uint32_t item, uint32_t fill_base,
                      uint32_t& cc, int ns, int nq) {
@@ -304,18 +345,20 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
       geo.chunked ? (size_t)2 * S::NMAT * kSbBox : ((size_t)2 * S::NMAT * arr_words * 2 + 127) / 128 * 128;
   const int rA = cw * 16 + row_of_lane<BITS>(g), rB = rA + 8;
   const bool vec_ok = geo.chunked || (ng & 3) == 0;  // a stage's groups aligned in the scale rows
+  const bool two = it.nrows > kTokChunk;
 
-  float y[S::NMAT][4];
+  float y[S::NMAT][4], y2[S::NMAT][4];
 #pragma unroll
   for (int m = 0; m < S::NMAT; ++m)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) y[m][i] = 0.0f;
+    for (int i = 0; i < 4; ++i) y[m][i] = y2[m][i] = 0.0f;
 
   const uint16_t* s_sb = nullptr;
   const float* s_xs = nullptr;
   int q = 0, sc = 0, cg0 = 0;  // slot, stage within the chunk, first group of the chunk
   int slot_i = (int)(fill_base % (uint32_t)ns);
   uint32_t phase = (fill_base / (uint32_t)ns) & 1u;
+  const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
   for (int st = 0; st < nstages; ++st) {
     if (sc == 0) {  // a new scale chunk
       q = (int)(cc % (uint32_t)nq);
@@ -327,23 +370,24 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
     }
     if (!mbar_wait(&sm.full[slot_i], phase, kDevErrTimeoutFull)) return false;
     const uint8_t* codes = sm.stage_base + (size_t)slot_i * S::STAGE_BYTES;
-    // activation box of group G: [8 rows][128 B], 16-byte chunk c of row r at chunk c ^ r
+    // activation rows of group G: [16 rows][128 B] (rows 8..15 loaded only for
+    // two n-tiles), 16-byte chunk c of row r at chunk c ^ (r % 8)
     const uint8_t* act = codes + S::CODE_BYTES + (size_t)g * 128;
+    const uint8_t* act2 = act + (size_t)kTokChunk * 128;
     const int gvalid = min(GPS, ng - st * GPS);  // last stage may be partial
     const int gc = st * GPS - cg0;               // slot-relative first group of the stage
-    if (gvalid == GPS && vec_ok) {
-      // ---- full stage: all loads of the stage issued up front, groups unguarded
+    if (gvalid == GPS && vec_ok && !two) {
+      // ---- full stage, one n-tile: every load of the stage issued up front
+      // (their shared-memory latencies overlap), groups unguarded
       float xa[GPS], xb[GPS];
       load_f32s<GPS>(s_xs + (2 * t) * geo.xp + gc, xa);
       load_f32s<GPS>(s_xs + (2 * t + 1) * geo.xp + gc, xb);
       uint4 blk[GPS][2];
 #pragma unroll
       for (int G = 0; G < GPS; ++G) {
-        blk[G][0] = *reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t) ^ g) << 4));
-        blk[G][1] = *reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t + 1) ^ g) << 4));
+        blk[G][0] = *reinterpret_cast<const uint4*>(act + G * S::ACT_GROUP + (((2 * t) ^ g) << 4));
+        blk[G][1] = *reinterpret_cast<const uint4*>(act + G * S::ACT_GROUP + (((2 * t + 1) ^ g) << 4));
       }
-      // every code word of the stage up front: the shared-memory latencies
-      // overlap instead of serialising group by group
       GroupCodes<BITS> cwd[S::NMAT][GPS];
 #pragma unroll
       for (int m = 0; m < S::NMAT; ++m)
@@ -351,6 +395,7 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
         for (int G = 0; G < GPS; ++G)
           cwd[m][G] = load_group_codes<BITS>(codes + (size_t)m * kRowTile * S::ROWB, G, rA, rB, t);
       const int wA = sb_word(geo.chunked, rA, gc, geo.row_len), wB = sb_word(geo.chunked, rB, gc, geo.row_len);
+      const uint4 none[2] = {zero4, zero4};
 #pragma unroll
       for (int m = 0; m < S::NMAT; ++m) {
         const uint16_t* ms = s_sb + (size_t)m * 2 * arr_words;
@@ -363,16 +408,64 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
 #pragma unroll
         for (int G = 0; G < GPS; ++G) {
           const float sA = h16_to_f32(hsA[G]), sB = h16_to_f32(hsB[G]);
-          qmv_group_regs<BITS, MODE>(cwd[m][G], blk[G], sA, sB, fmaf(-kQ, sA, h16_to_f32(hbA[G])),
-                                     fmaf(-kQ, sB, h16_to_f32(hbB[G])), xa[G], xb[G], y[m]);
+          qmv_group_regs<BITS>(cwd[m][G], blk[G], none, false, sA, sB, fmaf(-kQ, sA, h16_to_f32(hbA[G])),
+                               fmaf(-kQ, sB, h16_to_f32(hbB[G])), xa[G], xb[G], 0.0f, 0.0f, y[m], y2[m]);
+        }
+      }
+    } else if (gvalid == GPS && vec_ok) {
+      // ---- full stage, two n-tiles: sums, code words and scales of the stage
+      // up front, each group's activation rows of both n-tiles as the group
+      // comes up (fewer live registers), groups unguarded
+      float xa[GPS], xb[GPS], xc[GPS], xd[GPS];
+      load_f32s<GPS>(s_xs + (2 * t) * geo.xp + gc, xa);
+      load_f32s<GPS>(s_xs + (2 * t + 1) * geo.xp + gc, xb);
+      load_f32s<GPS>(s_xs + (kTokChunk + 2 * t) * geo.xp + gc, xc);
+      load_f32s<GPS>(s_xs + (kTokChunk + 2 * t + 1) * geo.xp + gc, xd);
+      GroupCodes<BITS> cwd[S::NMAT][GPS];
+#pragma unroll
+      for (int m = 0; m < S::NMAT; ++m)
+#pragma unroll
+        for (int G = 0; G < GPS; ++G)
+          cwd[m][G] = load_group_codes<BITS>(codes + (size_t)m * kRowTile * S::ROWB, G, rA, rB, t);
+      const int wA = sb_word(geo.chunked, rA, gc, geo.row_len), wB = sb_word(geo.chunked, rB, gc, geo.row_len);
+      uint2 hsA[S::NMAT], hsB[S::NMAT], hbA[S::NMAT], hbB[S::NMAT];  // fp16 scales / biases of the GPS groups
+#pragma unroll
+      for (int m = 0; m < S::NMAT; ++m) {
+        const uint16_t* ms = s_sb + (size_t)m * 2 * arr_words;
+        const uint16_t* mb = ms + arr_words;
+        hsA[m] = load_h16_pack<GPS>(ms + wA);
+        hsB[m] = load_h16_pack<GPS>(ms + wB);
+        hbA[m] = load_h16_pack<GPS>(mb + wA);
+        hbB[m] = load_h16_pack<GPS>(mb + wB);
+      }
+#pragma unroll
+      for (int G = 0; G < GPS; ++G) {
+        const uint4 blk[2] = {*reinterpret_cast<const uint4*>(act + G * S::ACT_GROUP + (((2 * t) ^ g) << 4)),
+                              *reinterpret_cast<const uint4*>(act + G * S::ACT_GROUP + (((2 * t + 1) ^ g) << 4))};
+        const uint4 blk2[2] = {*reinterpret_cast<const uint4*>(act2 + G * S::ACT_GROUP + (((2 * t) ^ g) << 4)),
+                               *reinterpret_cast<const uint4*>(act2 + G * S::ACT_GROUP + (((2 * t + 1) ^ g) << 4))};
+#pragma unroll
+        for (int m = 0; m < S::NMAT; ++m) {
+          const float sA = h16_to_f32(h16_at<GPS>(hsA[m], G)), sB = h16_to_f32(h16_at<GPS>(hsB[m], G));
+          qmv_group_regs<BITS>(cwd[m][G], blk, blk2, true, sA, sB, fmaf(-kQ, sA, h16_to_f32(h16_at<GPS>(hbA[m], G))),
+                               fmaf(-kQ, sB, h16_to_f32(h16_at<GPS>(hbB[m], G))), xa[G], xb[G], xc[G], xd[G], y[m],
+                               y2[m]);
         }
       }
     } else {
 #pragma unroll
       for (int G = 0; G < GPS; ++G) {
         if (G < gvalid) {
-          const uint4 blk[2] = {*reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t) ^ g) << 4)),
-                                *reinterpret_cast<const uint4*>(act + G * S::ACT_BOX + (((2 * t + 1) ^ g) << 4))};
+          const uint4 blk[2] = {*reinterpret_cast<const uint4*>(act + G * S::ACT_GROUP + (((2 * t) ^ g) << 4)),
+                                *reinterpret_cast<const uint4*>(act + G * S::ACT_GROUP + (((2 * t + 1) ^ g) << 4))};
+          uint4 blk2[2] = {zero4, zero4};
+          float x2 = 0.0f, x3 = 0.0f;
+          if (two) {
+            blk2[0] = *reinterpret_cast<const uint4*>(act2 + G * S::ACT_GROUP + (((2 * t) ^ g) << 4));
+            blk2[1] = *reinterpret_cast<const uint4*>(act2 + G * S::ACT_GROUP + (((2 * t + 1) ^ g) << 4));
+            x2 = s_xs[(kTokChunk + 2 * t) * geo.xp + gc + G];
+            x3 = s_xs[(kTokChunk + 2 * t + 1) * geo.xp + gc + G];
+          }
           const float x0 = s_xs[(2 * t) * geo.xp + gc + G], x1 = s_xs[(2 * t + 1) * geo.xp + gc + G];
           const int wA = sb_word(geo.chunked, rA, gc + G, geo.row_len);
           const int wB = sb_word(geo.chunked, rB, gc + G, geo.row_len);
@@ -382,8 +475,8 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
             const uint16_t* mb = ms + arr_words;
             const float sA = h16_to_f32(ms[wA]), sB = h16_to_f32(ms[wB]);
             const float bA = fmaf(-kQ, sA, h16_to_f32(mb[wA])), bB = fmaf(-kQ, sB, h16_to_f32(mb[wB]));
-            qmv_group_regs<BITS, MODE>(load_group_codes<BITS>(codes + (size_t)m * kRowTile * S::ROWB, G, rA, rB, t),
-                                       blk, sA, sB, bA, bB, x0, x1, y[m]);
+            qmv_group_regs<BITS>(load_group_codes<BITS>(codes + (size_t)m * kRowTile * S::ROWB, G, rA, rB, t), blk,
+                                 blk2, two, sA, sB, bA, bB, x0, x1, x2, x3, y[m], y2[m]);
           }
         }
       }
@@ -402,51 +495,58 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
   }
 
   if constexpr (MODE == 0) {
-    const int row0 = it.rt * kRowTile;
-    // h = silu(g) * u -> fp16 staging [8][64] in the activation layout, and
+    // h = silu(g) * u -> fp16 staging [16][64] in the activation layout, and
     // each token's sum of the 64 rounded h values (the group sum the down
     // projection folds its biases with): per thread over rows rA, rB, over the
     // 8 lane groups by shuffles, over the warps by the scale warp, which also
     // copies the tile out.  Staging and sums are double-buffered by item
     // parity; a buffer is rewritten (item + 2) only after its copy-out.
     const uint32_t hb_i = item & 1u;
-    uint16_t* s_h = sm.s_h + (size_t)hb_i * kTokChunk * kRowTile;
-    float* s_hs = sm.hsum + (size_t)hb_i * kComputeWarps * kTokChunk;
+    uint16_t* s_h = sm.s_h + (size_t)hb_i * kSegRows * kRowTile;
+    float* s_hs = sm.hsum + (size_t)hb_i * kComputeWarps * kSegRows;
     if (item >= 2 && !mbar_wait(&sm.h_free[hb_i], ((item >> 1) - 1) & 1u, kDevErrTimeoutFull)) return false;
-    float part[2] = {0.0f, 0.0f};
+    float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = (i < 2) ? rA : rB;
-      const int tok = 2 * t + (i & 1);
-      const float gv = y[0][i], uv = y[1][i];
-      const float h = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
-      const uint16_t hb = f32_to_h16_sat(h);
-      s_h[tok * kRowTile + (r & ~7) + act_pos(r & 7, BITS)] = hb;
-      part[i & 1] += h16_to_f32(hb);
-    }
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
-      part[1] += __shfl_xor_sync(0xffffffffu, part[1], o);
-    }
-    if (g == 0) {
-      s_hs[cw * kTokChunk + 2 * t] = part[0];
-      s_hs[cw * kTokChunk + 2 * t + 1] = part[1];
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.h_ready[hb_i]);
-    (void)row0;
-  } else {
-    const int R = p.R;
-#pragma unroll
-    for (int m = 0; m < S::NMAT; ++m)
+    for (int n = 0; n < 2; ++n) {
+      if (n == 1 && !two) break;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int r = (i < 2) ? rA : rB;
-        const int tok = 2 * t + (i & 1);
-        const int row = it.rt * S::ITEM_ROWS + m * kRowTile + r;
-        if (tok < it.nrows) p.y_out[(size_t)(it.row0_seg + tok) * R + row] = y[m][i];
+        const int tok = n * kTokChunk + 2 * t + (i & 1);
+        const float gv = n ? y2[0][i] : y[0][i], uv = n ? y2[1][i] : y[1][i];
+        const float h = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
+        const uint16_t hb = f32_to_h16_sat(h);
+        s_h[tok * kRowTile + (r & ~7) + act_pos(r & 7, BITS)] = hb;
+        part[2 * n + (i & 1)] += h16_to_f32(hb);
       }
+    }
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) part[j] += __shfl_xor_sync(0xffffffffu, part[j], o);
+    if (g == 0) {
+      s_hs[cw * kSegRows + 2 * t] = part[0];
+      s_hs[cw * kSegRows + 2 * t + 1] = part[1];
+      s_hs[cw * kSegRows + kTokChunk + 2 * t] = part[2];
+      s_hs[cw * kSegRows + kTokChunk + 2 * t + 1] = part[3];
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.h_ready[hb_i]);
+  } else {
+    const int R = p.R;
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      if (n == 1 && !two) break;
+#pragma unroll
+      for (int m = 0; m < S::NMAT; ++m)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = (i < 2) ? rA : rB;
+          const int tok = n * kTokChunk + 2 * t + (i & 1);
+          const int row = it.rt * S::ITEM_ROWS + m * kRowTile + r;
+          if (tok < it.nrows) p.y_out[(size_t)(it.row0_seg + tok) * R + row] = n ? y2[m][i] : y[m][i];
+        }
+    }
   }
   return true;
 }
@@ -454,8 +554,15 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
 template <int BITS, int MODE>
 __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_constant__ QmvParams p) {
   using S = QmvShape<BITS, MODE>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // the 128-byte swizzle of the stage tiles needs 1024-byte aligned stages and
+  // the launch reserves no slack for aligning up: a base that is not aligned
+  // ends the kernel before any shared-memory access, with an error recorded
+  if (smem_u32(smem_raw) & 1023u) {
+    if (threadIdx.x == 0) ef_set_error(kDevErrSmemAlign);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   const int ns = p.n_stages, nq = p.n_slots;
   const int ng = p.K / 64;
   const int nstages = (p.K + S::KT - 1) / S::KT;
@@ -465,8 +572,8 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
   sm.stage_base = smem;
   sm.slot_base = sm.stage_base + (size_t)ns * S::STAGE_BYTES;
   sm.s_h = reinterpret_cast<uint16_t*>(sm.slot_base + (size_t)nq * slot_bytes);
-  sm.hsum = reinterpret_cast<float*>(sm.s_h + (size_t)2 * kTokChunk * kRowTile);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm.hsum + (size_t)2 * kComputeWarps * kTokChunk);
+  sm.hsum = reinterpret_cast<float*>(sm.s_h + (MODE == 0 ? (size_t)2 * kSegRows * kRowTile : 0));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm.hsum + (MODE == 0 ? (size_t)2 * kComputeWarps * kSegRows : 0));
   sm.full = bars;
   sm.empty = bars + ns;
   sm.sb_full = bars + 2 * ns;
@@ -526,13 +633,17 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
         uint8_t* dst = sm.stage_base + (size_t)slot * S::STAGE_BYTES;
         // partial last stage: the code box past the row end is zero-filled by TMA
         const int gv = min(S::GPS, ng - st * S::GPS);
-        mbar_arrive_expect_tx(&sm.full[slot], S::CODE_BYTES + gv * S::ACT_BOX);
+        // the segment's rows 8..15 only when it has them (a second n-tile)
+        const int n_boxes = it.nrows > kTokChunk ? 2 : 1;
+        mbar_arrive_expect_tx(&sm.full[slot], S::CODE_BYTES + gv * n_boxes * S::ACT_BOX);
         const int kw = st * (S::KT * BITS / 32);
         tma_load_2d(dst, m0, kw, rowg, &sm.full[slot]);
         if (S::NMAT == 2) tma_load_2d(dst + kRowTile * S::ROWB, m1, kw, rowg1, &sm.full[slot]);
         uint8_t* adst = dst + S::CODE_BYTES;
         for (int G = 0; G < gv; ++G)
-          tma_load_2d(adst + G * S::ACT_BOX, &p.tm_act, st * S::KT + 64 * G, it.row0_seg, &sm.full[slot]);
+          for (int bx = 0; bx < n_boxes; ++bx)
+            tma_load_2d(adst + G * S::ACT_GROUP + bx * S::ACT_BOX, &p.tm_act, st * S::KT + 64 * G,
+                        it.row0_seg + bx * kTokChunk, &sm.full[slot]);
       }
     }
     // drain: wait (bounded) for the copies issued last

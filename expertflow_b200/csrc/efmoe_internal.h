@@ -8,7 +8,8 @@ namespace ef {
 
 // ---- quantised grouped GEMV (decode path) ----
 constexpr int kRowTile = 64;        // weight rows per work item (4 warps x 16 rows)
-constexpr int kTokChunk = 8;        // rows (tokens) per segment: one n-tile of 8
+constexpr int kTokChunk = 8;        // rows (tokens) of one MMA n-tile / activation box
+constexpr int kSegRows = 16;        // rows per decode-GEMV segment: up to two n-tiles share each weight pass
 #ifndef EF_GEMM_NMAX
 #define EF_GEMM_NMAX 192
 #endif
@@ -26,6 +27,7 @@ constexpr int kDevErrTimeoutEmpty = 1002;
 constexpr int kDevErrTimeoutScales = 1003;
 constexpr int kDevErrRange = 2001;
 constexpr int kDevErrTimeoutTc = 1004;
+constexpr int kDevErrSmemAlign = 2003;  // dynamic shared memory not 1024-byte aligned
 constexpr int kDevErrTimeoutPeer = 1005;  // a peer rank's flag never arrived
 constexpr int kDevErrRecvOverflow = 2002; // more rows received than the exchange holds
 
