@@ -339,10 +339,23 @@ QmvParams make_params_common() {
   return p;
 }
 
-// gate/up (mode 0) then down (mode 1) over permuted rows already described by f.pb.
+// Where the down projection of an expert-parallel forward stores its rows
+// (see QmvParams::ret_rank).
+struct EpReturn {
+  const int* rank;
+  const int* row;
+  float* const* base;
+  uint32_t* const* flag;
+  const uint32_t* epoch;
+  uint32_t* ctr;
+  int ranks, rows;
+};
+
+// gate/up (mode 0) then down (mode 1) over permuted rows already described by
+// f.pb; with `ret`, the down rows go to the expert-parallel return regions.
 ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, const ef_qweight& gate,
                       const ef_qweight& up, const ef_qweight& down, const ef_qweight* sg, const ef_qweight* su,
-                      const ef_qweight* sd, cudaStream_t st) {
+                      const ef_qweight* sd, cudaStream_t st, const EpReturn* ret = nullptr) {
   const int H = c->hidden, I = c->inter, E = c->n_experts, bits = c->bits;
   const int nsm = sm_count();
   ef_status s;
@@ -385,6 +398,16 @@ ef_status run_experts(const ef_moe_cfg* c, const FfnBufs& f, int n_rows, const e
   p1.K = I; p1.R = H; p1.n_experts = E;
   set_scale_maps(p1, (long long)E * H, sd ? H : (long long)E * H);
   p1.y_out = f.yrows;
+  if (ret) {
+    p1.ret_rank = ret->rank;
+    p1.ret_row = ret->row;
+    p1.ret_base = ret->base;
+    p1.ret_flag = ret->flag;
+    p1.ep_epoch = ret->epoch;
+    p1.ep_ctr = ret->ctr;
+    p1.ep_ranks = ret->ranks;
+    p1.ret_rows = ret->rows;
+  }
   // each expert with rows makes at least one segment
   const int min_segs = std::min(n_rows, E + (sd ? 1 : 0));
   EF_LAUNCH("qmv_down", launch_qmv(bits, 1, p1, nsm, st, min_segs));

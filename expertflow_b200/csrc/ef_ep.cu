@@ -394,6 +394,7 @@ struct ef_ep_group {
 namespace {
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+constexpr size_t kEpLocalTables = 64;  // offset of the pointer tables in the local area
 
 // Layout of an exchange buffer: flags, done flags and counts (64 bytes per
 // source rank), the receive metadata and rows ([P][rmax], then this rank's own
@@ -414,8 +415,8 @@ size_t ep_layout(ef::EpGeom& g) {
   o = align256(o + ((size_t)g.P * g.rmax + g.max_tokens) * g.H * 2);
   g.off_back = o;
   o = align256(o + ((size_t)g.max_tokens * g.k + g.max_tokens) * g.H * 4);
-  g.off_local = o;
-  o = align256(o + 256);
+  g.off_local = o;  // epoch, 3 last-CTA counters, then the return-region and done-flag tables
+  o = align256(o + kEpLocalTables + 2 * kEpMaxRanks * sizeof(void*));
   return o;
 }
 
@@ -507,7 +508,7 @@ ef_status ef_ep_group_create(const ef_moe_cfg* cfg, int rank, int n_ranks, int m
     return fail(EF_ERR_CUDA, "exchange buffer (%zu bytes): %s", bytes, cudaGetErrorString(e));
   }
   G.epoch = reinterpret_cast<uint32_t*>(g->base + G.off_local);
-  G.ctr = G.epoch + 1;
+  G.ctr = G.epoch + 1;  // [0] dispatch, [1] return kernel, [2] the down GEMV's fused return
   g->peers.base[rank] = g->base;
   *out = g;
   return EF_OK;
@@ -544,6 +545,16 @@ ef_status ef_ep_group_open(ef_ep_group* g, const void* handles) {
     g->mapped[s] = static_cast<uint8_t*>(p);
     g->peers.base[s] = g->mapped[s];
   }
+  // tables the down GEMV's fused return reads: every rank's return region and
+  // this rank's done flag in every rank's buffer
+  std::vector<uintptr_t> tab(2 * (size_t)g->P);
+  for (int s = 0; s < g->P; ++s) {
+    tab[s] = reinterpret_cast<uintptr_t>(g->peers.base[s] + g->geom.off_back);
+    tab[g->P + s] = reinterpret_cast<uintptr_t>(g->peers.base[s] + g->geom.off_done + (size_t)g->rank * 64);
+  }
+  const cudaError_t e = cudaMemcpy(g->base + g->geom.off_local + kEpLocalTables, tab.data(),
+                                   tab.size() * sizeof(uintptr_t), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return fail(EF_ERR_CUDA, "return tables: %s", cudaGetErrorString(e));
   g->opened = true;
   return EF_OK;
 }
@@ -647,14 +658,24 @@ extern "C" ef_status ef_ep_forward(ef_ep_group* g, const void* x, int T, const v
   const ef_qweight* lsd = cfg->n_shared ? sd : nullptr;
   if (gemm) {
     if ((s = run_experts_gemm(&lc, w.f, nr_max, gate, up, down, lsg, lsu, lsd, st))) return s;
-  } else if ((s = run_experts(&lc, w.f, nr_max, gate, up, down, lsg, lsu, lsd, st))) {
-    return s;
-  }
-  {
     const int blocks = std::max(1, std::min((nr_max * ef::kRowParts + 7) / 8, 4 * nsm));
     EF_LAUNCH("ep_return", launch_pdl(ef::ep_return_kernel, blocks, 256, 0, st, g->peers, G,
                                       (const float*)w.f.yrows, (const int*)w.ret_rank, (const int*)w.ret_row,
                                       (const int*)w.n_rows, nr_max));
+  } else {
+    // the down GEMV stores each output row into its source rank's return
+    // region itself and its last CTA releases the done flags
+    uint8_t* tabs = g->base + G.off_local + kEpLocalTables;
+    EpReturn er;
+    er.rank = w.ret_rank;
+    er.row = w.ret_row;
+    er.base = reinterpret_cast<float* const*>(tabs);
+    er.flag = reinterpret_cast<uint32_t* const*>(tabs + (size_t)g->P * sizeof(void*));
+    er.epoch = G.epoch;
+    er.ctr = G.ctr + 2;
+    er.ranks = g->P;
+    er.rows = g->max_tokens * k + g->max_tokens;
+    if ((s = run_experts(&lc, w.f, nr_max, gate, up, down, lsg, lsu, lsd, st, &er))) return s;
   }
   if (T > 0) {  // the combine waits for every rank's done flag itself
     const float* back = reinterpret_cast<const float*>(g->base + G.off_back);

@@ -538,14 +538,25 @@ EF_DEV bool qmv_item(const QmvParams& p, const WorkItem& it, const QmvSmem& sm, 
     for (int n = 0; n < 2; ++n) {
       if (n == 1 && !two) break;
 #pragma unroll
-      for (int m = 0; m < S::NMAT; ++m)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = (i < 2) ? rA : rB;
-          const int tok = n * kTokChunk + 2 * t + (i & 1);
-          const int row = it.rt * S::ITEM_ROWS + m * kRowTile + r;
-          if (tok < it.nrows) p.y_out[(size_t)(it.row0_seg + tok) * R + row] = n ? y2[m][i] : y[m][i];
+      for (int tb = 0; tb < 2; ++tb) {  // tokens 2t, 2t + 1 of n-tile n
+        const int tok = n * kTokChunk + 2 * t + tb;
+        if (tok >= it.nrows) continue;
+        const int q = it.row0_seg + tok;
+        float* yrow = p.y_out + (size_t)q * R;
+        if (p.ret_rank) {  // straight into the source rank's return region
+          const int rk = __ldg(p.ret_rank + q), rr = __ldg(p.ret_row + q);
+          if (rk < 0 || rk >= p.ep_ranks || rr < 0 || rr >= p.ret_rows) continue;  // recorded by the receiver
+          yrow = p.ret_base[rk] + (size_t)rr * R;
         }
+#pragma unroll
+        for (int m = 0; m < S::NMAT; ++m)
+#pragma unroll
+          for (int i = tb; i < 4; i += 2) {
+            const int r = (i < 2) ? rA : rB;
+            const int row = it.rt * S::ITEM_ROWS + m * kRowTile + r;
+            yrow[row] = n ? y2[m][i] : y[m][i];
+          }
+      }
     }
   }
   return true;
@@ -724,8 +735,23 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const __grid_consta
   for (; w < n_work; w += gridDim.x, ++item) {
     const WorkItem it = nxt;
     if (w + (int)gridDim.x < n_work) nxt = decode_work(p, w + gridDim.x, n_rt);
-    if (!qmv_item<BITS, MODE>(p, it, sm, item, fill_base, cc, ns, nq)) return;
+    if (!qmv_item<BITS, MODE>(p, it, sm, item, fill_base, cc, ns, nq)) break;
     fill_base += nstages;
+  }
+  if (MODE != 0 && p.ret_rank) {
+    // expert-parallel return: every compute warp of the CTA has stored its
+    // rows; the grid's last CTA releases the done flags (also after a failed
+    // wait, recorded in the error word, so that no peer waits for a dead rank)
+    asm volatile("bar.sync 1, %0;" ::"r"(kComputeWarps * 32) : "memory");
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      if (atomicAdd(p.ep_ctr, 1u) == gridDim.x - 1) {
+        __threadfence_system();
+        const uint32_t ep = *reinterpret_cast<const volatile uint32_t*>(p.ep_epoch);
+        for (int r = 0; r < p.ep_ranks; ++r) st_release_sys(p.ret_flag[r], ep);
+        *p.ep_ctr = 0;
+      }
+    }
   }
 }
 

@@ -242,12 +242,14 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const flo
     __syncwarp();
   }
   // top-k over sc by (value desc, index asc); each lane keeps the keys of its
-  // elements e = lane + 32 r, a taken element's key drops to 0
-  int sel[16];
+  // elements e = lane + 32 r, a taken element's key drops to 0.  Lane j < k
+  // keeps the j-th pick (no per-thread arrays indexed by j: they would live
+  // in local memory).
   constexpr int kPerLane = kMaxE / 32;
   uint32_t keys[kPerLane];
 #pragma unroll
   for (int r = 0; r < kPerLane; ++r) keys[r] = lane + 32 * r < E ? order_key(sc[lane + 32 * r]) : 0u;
+  int my_sel = 0;
   for (int j = 0; j < k; ++j) {
     uint32_t bk = 0u;
     int bi = 0x7fffffff;
@@ -258,44 +260,40 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const flo
         bi = lane + 32 * r;
       }
     const int win = warp_argmax_key(bk, bi);
-    sel[j] = win;
-    if ((win & 31) == lane) {
+    if (lane == j) my_sel = win;
+    const bool own = (win & 31) == lane;
+    const int wr = win >> 5;
 #pragma unroll
-      for (int r = 0; r < kPerLane; ++r)
-        if (r == (win >> 5)) keys[r] = 0u;
-    }
+    for (int r = 0; r < kPerLane; ++r) keys[r] = (own && r == wr) ? 0u : keys[r];
   }
-  // weights (every lane computes the same values; lane 0 writes)
-  float w[16];
+  // weights of the picks, lane j for pick j; sums over the picks run in j
+  // order (shuffles bring the values to every lane), as the oracle adds them
+  const bool mine = lane < k;
+  float w = 0.0f;
   if (cfg.mode == 0) {
-    const float m = kv[sel[0]];
+    const float m = kv[__shfl_sync(0xffffffffu, my_sel, 0)];
     if (cfg.norm_topk) {
-      float s = 0.0f;
-      for (int j = 0; j < k; ++j) { w[j] = det_expf(__fsub_rn(kv[sel[j]], m)); s = (j == 0) ? w[j] : __fadd_rn(s, w[j]); }
-      for (int j = 0; j < k; ++j) w[j] = __fdiv_rn(w[j], s);
+      w = mine ? det_expf(__fsub_rn(kv[my_sel], m)) : 0.0f;
+      float s = __shfl_sync(0xffffffffu, w, 0);
+      for (int j = 1; j < k; ++j) s = __fadd_rn(s, __shfl_sync(0xffffffffu, w, j));
+      w = __fdiv_rn(w, s);
     } else {
       float z = 0.0f;
       for (int e = lane; e < E; e += 32) z = __fadd_rn(z, det_expf(__fsub_rn(kv[e], m)));
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) z = __fadd_rn(z, __shfl_xor_sync(0xffffffffu, z, off));
-      for (int j = 0; j < k; ++j) w[j] = __fdiv_rn(det_expf(__fsub_rn(kv[sel[j]], m)), z);
+      w = mine ? __fdiv_rn(det_expf(__fsub_rn(kv[my_sel], m)), z) : 0.0f;
     }
   } else {
-    float s = 0.0f;
-    for (int j = 0; j < k; ++j) { w[j] = kv[sel[j]]; s = (j == 0) ? w[j] : __fadd_rn(s, w[j]); }
-    for (int j = 0; j < k; ++j) {
-      float v = w[j];
-      if (cfg.norm_topk && k > 1) v = __fdiv_rn(v, s);
-      w[j] = __fmul_rn(v, cfg.scaling);
-    }
+    w = mine ? kv[my_sel] : 0.0f;
+    float s = __shfl_sync(0xffffffffu, w, 0);
+    for (int j = 1; j < k; ++j) s = __fadd_rn(s, __shfl_sync(0xffffffffu, w, j));
+    if (cfg.norm_topk && k > 1) w = __fdiv_rn(w, s);
+    w = __fmul_rn(w, cfg.scaling);
   }
-  if (lane < k) {
-    int sj = 0;
-    float wj = 0.0f;
-    for (int j = 0; j < k; ++j)
-      if (j == lane) { sj = sel[j]; wj = w[j]; }
-    inds[(size_t)t * k + lane] = sj;
-    wts[(size_t)t * k + lane] = wj;
+  if (mine) {
+    inds[(size_t)t * k + lane] = my_sel;
+    wts[(size_t)t * k + lane] = w;
   }
 }
 

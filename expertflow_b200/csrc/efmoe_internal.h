@@ -78,6 +78,18 @@ struct QmvParams {
   int sb_chunked;           // 1: scales streamed in 32-group chunks through tm_sc (K / 64 a multiple of 8)
   int n_stages;             // TMA ring depth (set by the launcher)
   int n_slots;              // scale slots (set by the launcher)
+  // expert-parallel return (modes 1 / 2, ret_rank non-null): output row q goes
+  // to rank ret_rank[q]'s return region at row ret_row[q] (peer stores), and
+  // the grid's last CTA releases this rank's done flag in every rank's buffer
+  // (value *ep_epoch) once every row is written
+  const int* ret_rank;
+  const int* ret_row;
+  float* const* ret_base;      // device [ep_ranks]: each rank's return region
+  uint32_t* const* ret_flag;   // device [ep_ranks]: this rank's done flag in each rank's buffer
+  const uint32_t* ep_epoch;
+  uint32_t* ep_ctr;            // last-CTA counter (zero between launches)
+  int ep_ranks;
+  int ret_rows;                // rows of a return region (bound of ret_row)
 };
 
 }  // namespace ef
