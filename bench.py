@@ -66,7 +66,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except Exception:
@@ -230,7 +230,24 @@ class _EpLayers:
             self.layers.append(ExpertParallelMoE(spec, ops))
 
 
-def _time_layers(L, T, steps, warmup, pg, dev, trace=False, x_seed=7, graphs=False):
+def _keep_loaded(fwd, n, e0, e1, steps, hold):
+    """After the timed steps (e0..e1, already enqueued), keep replaying the same
+    forwards, untimed, until about `hold` seconds have passed, so that a clock
+    sampler running around the timed region sees the GPU under that load."""
+    import torch
+
+    if hold <= 0:
+        torch.cuda.synchronize()
+        return
+    e1.synchronize()
+    per = max(e0.elapsed_time(e1) / max(steps, 1), 1e-3)  # ms per step
+    extra = int(min(20000, hold * 1e3 / per))
+    for s in range(extra):
+        fwd[s % n]()
+    torch.cuda.synchronize()
+
+
+def _time_layers(L, T, steps, warmup, pg, dev, trace=False, x_seed=7, graphs=False, hold=0.0):
     """CUDA-event time of `steps` forwards (max over ranks), the distinct
     experts per step (from the routing indices) and, with trace, the per-launch
     kernel times of a separate (eager) pass.  graphs: each layer copy's forward
@@ -262,7 +279,7 @@ def _time_layers(L, T, steps, warmup, pg, dev, trace=False, x_seed=7, graphs=Fal
     for s in range(steps):
         fwd[s % L.n]()
     e1.record(st)
-    torch.cuda.synchronize()
+    _keep_loaded(fwd, L.n, e0, e1, steps, hold)
     ms = e0.elapsed_time(e1) / steps
     if pg:
         t = torch.tensor([ms], device=dev)
@@ -671,7 +688,7 @@ class _PeerEpLayers:
             m.close()
 
 
-def _time_ep(L, T, steps, warmup, pg, dev, x_seed, rank, graphs=True, trace=False):
+def _time_ep(L, T, steps, warmup, pg, dev, x_seed, rank, graphs=True, trace=False, hold=0.0):
     """CUDA-event time per step (max over ranks) of T tokens per rank through
     the rotated expert-parallel copies; with trace, the per-launch times of a
     separate eager pass (kernel name -> mean ms, max over ranks)."""
@@ -698,6 +715,13 @@ def _time_ep(L, T, steps, warmup, pg, dev, x_seed, rank, graphs=True, trace=Fals
     for s in range(steps):
         fwd[s % L.n]()
     e1.record(st)
+    if hold > 0:
+        # every rank replays the same number of extra forwards (the exchange pairs them up)
+        e1.synchronize()
+        per = torch.tensor([max(e0.elapsed_time(e1) / max(steps, 1), 1e-3)], device=dev)
+        pg.all_reduce(per, op=pg.ReduceOp.MAX)
+        for s in range(int(min(20000, hold * 1e3 / float(per.item())))):
+            fwd[s % L.n]()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     t = torch.tensor([ms], device=dev)
@@ -761,7 +785,7 @@ def bench_ep(args, pg, dev, rank, ws, local, peaks):
     n_local = int(torch.unique(ai[(ai >= rank * el) & (ai < (rank + 1) * el)]).numel())
 
     with ClockSampler(local) as clk:
-        ms, _, _ = _time_ep(L, Tl, args.steps, args.warmup, pg, dev, 7, rank)
+        ms, _, _ = _time_ep(L, Tl, args.steps, args.warmup, pg, dev, 7, rank, hold=0.3)
     clocks = clk.summary()
     value = Tg / (ms * 1e-3)
     _, phases, _ = _time_ep(L, Tl, 2, 1, pg, dev, 7, rank, graphs=False, trace=True)
@@ -1019,7 +1043,7 @@ def bench_ours(args):
     L = _Layers(spec, dev, rank)
     T = args.tokens
     with ClockSampler(local) as clk:
-        ms, ub, _, _ = _time_layers(L, T, args.steps, args.warmup, pg, dev, graphs=True)
+        ms, ub, _, _ = _time_layers(L, T, args.steps, args.warmup, pg, dev, graphs=True, hold=0.3)
     clocks = clk.summary()
     ms_eager, _, _, _ = _time_layers(L, T, args.steps, args.warmup, pg, dev)
     ms_tr, ub_tr, recs, _ = _time_layers(L, T, args.steps, 1, pg, dev, trace=True)
