@@ -302,7 +302,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const flo
 cudaError_t launch_router_logits(const uint16_t* x, int x_bf16, const uint16_t* wg, int w_bf16, int T, int E,
                                  int H, float* logits, cudaStream_t st, const uint16_t* wg2, float* logits2) {
   const int nz = wg2 ? 2 : 1;
-  if (T >= 16) {
+  if (T >= 64) {
     dim3 grid((T + 7) / 8, (E + 7) / 8, nz);
     return launch_pdl(router_logits_kernel<8, 8>, grid, 128, 0, st, x, x_bf16, wg, w_bf16, T, E, H, logits, wg2,
                       logits2);
