@@ -438,6 +438,9 @@ def section_stream(name, spec, args, dev):
     del res
     torch.cuda.empty_cache()
     out = {"workload": name, "layers": NL, "steps": steps, "slots_per_layer": budget + spec.top_k,
+           "slots_note": f"the policy keeps {budget} of {spec.n_experts} experts per layer (25 %) across tokens; "
+                         f"{spec.top_k} more slots hold one token's misses until the per-token trim, as the "
+                         f"reference trims once per token",
            "loop": "ef_pool_decode_step (per layer: residual add + RMS norm, routed MoE on HBM slots)",
            "budget_per_layer": budget, "policy": "FrequencyWeightedCache (decay 0.95)",
            "resident_tokens_per_s": round(steps / (ms_res * 1e-3), 2)}
