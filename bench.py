@@ -402,7 +402,8 @@ def section_prefill(name, spec, T, args, pg, dev, rank, ws, peaks):
 
 def section_stream(name, spec, args, dev):
     """48 stacked layers, experts streamed from pinned host memory into HBM
-    slots (25% per layer) with one-layer lookahead; single-token decode."""
+    slots (25% per layer) without lookahead and with one- and two-layer
+    lookahead; single-token decode."""
     import numpy as np
     import torch
     from expertflow_b200 import moe, synthetic, pool as P
@@ -431,9 +432,10 @@ def section_stream(name, spec, args, dev):
         return e0.elapsed_time(e1)
 
     res = P.ExpertSlotPool(spec, host, budget=spec.n_experts, headroom=spec.top_k)
-    run(res, False, steps)  # every expert the run touches becomes resident
+    run(res, 0, steps)  # every expert the run touches becomes resident
     res.reset_stats()
-    ms_res = run(res, False, steps)
+    ms_res = run(res, 0, steps)
+    st_res = res.stats()
     res.close()
     del res
     torch.cuda.empty_cache()
@@ -443,8 +445,10 @@ def section_stream(name, spec, args, dev):
                          f"reference trims once per token",
            "loop": "ef_pool_decode_step (per layer: residual add + RMS norm, routed MoE on HBM slots)",
            "budget_per_layer": budget, "policy": "FrequencyWeightedCache (decay 0.95)",
-           "resident_tokens_per_s": round(steps / (ms_res * 1e-3), 2)}
-    for la in (False, True):
+           "resident_tokens_per_s": round(steps / (ms_res * 1e-3), 2),
+           "resident_host_route_wait_ms_per_token": round(st_res["route_wait_ms"] / steps, 4),
+           "resident_host_other_ms_per_token": round(st_res["host_ms"] / steps, 4)}
+    for la in (0, 1, 2):
         pl = P.ExpertSlotPool(spec, host, budget=budget, headroom=spec.top_k)
         run(pl, la, min(16, steps))
         pl.reset_stats()
@@ -459,8 +463,11 @@ def section_stream(name, spec, args, dev):
              "exposed_copy_ms": round(exposed, 1),
              "h2d_overlap": round(1.0 - exposed / st["copy_ms"], 4) if st["copy_ms"] > 0 else None,
              "copies_prefetch": st["copies_prefetch"], "prefetch_used": st["prefetch_used"],
-             "copies_sync": st["copies_sync"]}
-        out["lookahead" if la else "no_lookahead"] = d
+             "copies_sync": st["copies_sync"],
+             "stall_on_copies_ms_per_token": round(st["copy_wait_ms"] / steps, 4),
+             "host_route_wait_ms_per_token": round(st["route_wait_ms"] / steps, 4),
+             "host_other_ms_per_token": round(st["host_ms"] / steps, 4)}
+        out[("no_lookahead", "lookahead", "lookahead2")[la]] = d
     if args.stream_files != "off":
         out["files"] = stream_from_files(spec, host, gates, run, steps, budget, ms_res, args)
     del host
@@ -997,7 +1004,9 @@ def _summary(line, sections):
     c3 = sections.get("c3")
     if c3:
         la = c3.get("lookahead", {})
+        la2 = c3.get("lookahead2", {})
         out["c3"] = {"tok_s": la.get("tokens_per_s"), "h2d_overlap": la.get("h2d_overlap"),
+                     "tok_s_lookahead2": la2.get("tokens_per_s"), "h2d_overlap_lookahead2": la2.get("h2d_overlap"),
                      "resident_tok_s": c3.get("resident_tokens_per_s")}
     kq = sections.get("kq")
     if kq:

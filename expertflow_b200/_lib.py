@@ -76,7 +76,8 @@ class PoolStats(ctypes.Structure):
                 ("tokens", ctypes.c_longlong), ("h2d_bytes", ctypes.c_double), ("copy_ms", ctypes.c_double),
                 ("host_hits", ctypes.c_longlong), ("host_reads", ctypes.c_longlong),
                 ("host_reads_ahead", ctypes.c_longlong), ("host_evictions", ctypes.c_longlong),
-                ("read_wait_ms", ctypes.c_double)]
+                ("read_wait_ms", ctypes.c_double), ("copy_wait_ms", ctypes.c_double),
+                ("route_wait_ms", ctypes.c_double), ("host_ms", ctypes.c_double)]
 
     def as_dict(self) -> dict:
         return {name: getattr(self, name) for name, _ in self._fields_}

@@ -18,12 +18,14 @@
 namespace ef {
 cudaError_t launch_router_logits(const uint16_t* x, int x_bf16, const uint16_t* wg, int w_bf16, int T, int E, int H,
                                  float* logits, cudaStream_t st,
-                                 const uint16_t* wg2 = nullptr, float* logits2 = nullptr);
+                                 const uint16_t* wg2 = nullptr, float* logits2 = nullptr,
+                                 const uint16_t* wg3 = nullptr, float* logits3 = nullptr);
 cudaError_t launch_router_select(const float* logits, const float* e_bias, int T, int E, int k, int mode,
                                  int norm_topk, int n_group, int topk_group, float scaling, int* inds, float* wts,
                                  cudaStream_t st,
                                  const float* logits2 = nullptr, const float* e_bias2 = nullptr,
-                                 int* inds2 = nullptr, float* wts2 = nullptr);
+                                 int* inds2 = nullptr, float* wts2 = nullptr, const float* logits3 = nullptr,
+                                 const float* e_bias3 = nullptr, int* inds3 = nullptr, float* wts3 = nullptr);
 cudaError_t launch_permute(const int* entries, int n_ent, int k, int n_exp, int n_sh, int seg_chunk,
                            const PermBufs& pb, cudaStream_t st);
 cudaError_t launch_prep_act(const uint16_t* act, const int* row_src, int is_bf16, int n, int K, int bits,

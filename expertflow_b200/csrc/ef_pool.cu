@@ -290,6 +290,7 @@ struct LayerSlots {
 
 struct CopyTimer {
   cudaEvent_t a = nullptr, b = nullptr;
+  bool stall = false;  // a compute-stream stall on copies, not a copy interval
 };
 
 // Staged blobs -> slot arrays.  Blob layout: for each projection j, w then
@@ -361,12 +362,14 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
 namespace ef {
 // The routed (and predicted) expert ids of a pool step -> mapped pinned host
 // memory, then `seq` into the host flag once they are visible there.
-__global__ void publish_ids_kernel(const int* __restrict__ inds, const int* __restrict__ pred, int n,
-                                   int* h_inds, int* h_pred, uint32_t* h_flag, uint32_t seq) {
+__global__ void publish_ids_kernel(const int* __restrict__ inds, const int* __restrict__ pred,
+                                   const int* __restrict__ pred2, int n, int* h_inds, int* h_pred, int* h_pred2,
+                                   uint32_t* h_flag, uint32_t seq) {
   pdl_wait();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     h_inds[i] = inds[i];
     if (pred) h_pred[i] = pred[i];
+    if (pred2) h_pred2[i] = pred2[i];
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -401,6 +404,21 @@ struct ef_slot_pool {
   int32_t* h_inds = nullptr;               // mapped pinned staging: routed ids, predicted ids, slot ids, flag
   int32_t* h_pred = nullptr;
   int32_t* h_slot = nullptr;
+  int32_t* h_pred2 = nullptr;
+  // the expert kernels of a layer step (permute .. combine) as CUDA graphs,
+  // one per (layer, tokens, buffers); run eagerly the first time, captured
+  // on cap_stream the second, replayed from then on
+  struct TailGraph {
+    int layer, T, out_f32;
+    const void* x;
+    const void* y;
+    const void* wts;
+    const void* ws;
+    int uses;
+    cudaGraphExec_t exec;
+  };
+  std::vector<TailGraph> tails;
+  cudaStream_t cap_stream = nullptr;
   int32_t* d_inds = nullptr;               // the same staging as the device addresses it
   uint32_t* h_flag = nullptr;              // sequence number of the last published routing
   uint32_t h_seq = 0;
@@ -465,7 +483,7 @@ void fold_timers(ef_slot_pool* P, bool all) {
     }
     if (all) cudaEventSynchronize(t.b);
     float ms = 0.f;
-    if (cudaEventElapsedTime(&ms, t.a, t.b) == cudaSuccess) P->st.copy_ms += ms;
+    if (cudaEventElapsedTime(&ms, t.a, t.b) == cudaSuccess) (t.stall ? P->st.copy_wait_ms : P->st.copy_ms) += ms;
     P->spare.push_back(t);
     keep_from = i + 1;
   }
@@ -482,6 +500,7 @@ CopyTimer timer_begin(ef_slot_pool* P, cudaStream_t cs) {
     cudaEventCreate(&t.a);
     cudaEventCreate(&t.b);
   }
+  t.stall = false;
   cudaEventRecord(t.a, cs);
   return t;
 }
@@ -535,14 +554,15 @@ ef_status copy_expert(ef_slot_pool* P, int ln, int l, int e, int s, int h) {
 }
 
 // A free slot of layer l, else the slot of a staged (prefetched, unused)
-// expert not in `keep`; -1 when neither exists.
-int take_slot(ef_slot_pool* P, int l, const std::vector<char>& keep) {
+// expert not in `keep` (then *from_staged is set); -1 when neither exists.
+int take_slot(ef_slot_pool* P, int l, const std::vector<char>& keep, bool* from_staged = nullptr) {
   LayerSlots& L = P->layers[l];
   for (int s = 0; s < P->n_slots; ++s)
     if (L.slot_expert[s] < 0) return s;
   for (int s = 0; s < P->n_slots; ++s) {
     const int e = L.slot_expert[s];
     if (L.staged[e] && !keep[e]) {
+      if (from_staged) *from_staged = true;
       L.staged[e] = 0;
       L.expert_slot[e] = -1;
       L.slot_expert[s] = -1;
@@ -658,9 +678,9 @@ struct PoolWs {
   float* logits;
   int* inds;
   float* wts;
-  float* plogits;
-  int* pinds;
-  float* pwts;
+  float* plogits[2];  // lookahead predictions: the next layer, the one after it
+  int* pinds[2];
+  float* pwts[2];
   FfnBufs f;
 };
 size_t pool_ws(const ef_slot_pool* P, int T, Carver& c, PoolWs& w) {
@@ -670,15 +690,17 @@ size_t pool_ws(const ef_slot_pool* P, int T, Carver& c, PoolWs& w) {
   w.logits = c.take<float>((size_t)T * E);
   w.inds = c.take<int>((size_t)n_ent);
   w.wts = c.take<float>((size_t)n_ent);
-  w.plogits = c.take<float>((size_t)T * E);
-  w.pinds = c.take<int>((size_t)n_ent);
-  w.pwts = c.take<float>((size_t)n_ent);
+  for (int a = 0; a < 2; ++a) {
+    w.plogits[a] = c.take<float>((size_t)T * E);
+    w.pinds[a] = c.take<int>((size_t)n_ent);
+    w.pwts[a] = c.take<float>((size_t)n_ent);
+  }
   carve_ffn(c, n_ent, P->n_slots + 1, n_rows, cfg.hidden, cfg.inter, w.f);
   return c.off;
 }
 
-// Routes x through gate gw (and, when gw2, the next layer's gate gw2 in the same
-// two launches: that routing is the lookahead prediction).
+// Routes x through gate gw (and, when gw2 / gw3, the next layers' gates in the
+// same two launches: those routings are the lookahead predictions).
 // Polls the host flag until the routing of step `seq` is published (bounded:
 // the stream's errors are checked every millisecond or so, and 30 s without
 // the flag is an error).
@@ -701,16 +723,17 @@ ef_status wait_published(const uint32_t* flag, uint32_t seq, cudaStream_t st) {
 
 ef_status pool_route(const ef_moe_cfg& cfg, const void* x, int T, const void* gw, const float* eb, float* logits, int* inds,
                      float* wts, const void* gw2, const float* eb2, float* logits2, int* inds2, float* wts2,
-                     cudaStream_t st) {
+                     const void* gw3, const float* eb3, float* logits3, int* inds3, float* wts3, cudaStream_t st) {
   const bool bf = cfg.act_dtype == EF_DT_BF16;
   EF_LAUNCH("router_logits", launch_router_logits(static_cast<const uint16_t*>(x), bf, static_cast<const uint16_t*>(gw),
                                                   cfg.gate_dtype == EF_DT_BF16, T, cfg.n_experts, cfg.hidden, logits, st,
-                                                  static_cast<const uint16_t*>(gw2), gw2 ? logits2 : nullptr));
+                                                  static_cast<const uint16_t*>(gw2), gw2 ? logits2 : nullptr,
+                                                  static_cast<const uint16_t*>(gw3), gw3 ? logits3 : nullptr));
   EF_LAUNCH("router_select",
             launch_router_select(logits, eb, T, cfg.n_experts, cfg.top_k, cfg.router_mode, cfg.norm_topk,
                                  cfg.router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg.n_group : 1, cfg.topk_group,
                                  cfg.router_mode == EF_ROUTER_SIGMOID_GROUP ? cfg.routed_scaling : 1.0f, inds, wts, st,
-                                 gw2 ? logits2 : nullptr, eb2, inds2, wts2));
+                                 gw2 ? logits2 : nullptr, eb2, inds2, wts2, gw3 ? logits3 : nullptr, eb3, inds3, wts3));
   return EF_OK;
 }
 
@@ -944,41 +967,136 @@ size_t ef_pool_workspace_size(const ef_slot_pool* P, int T) {
   return pool_ws(P, T, c, w) + 256;
 }
 
-ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, const void* gate_w,
-                              const float* e_bias, const void* next_gate_w, const float* next_e_bias, void* y,
-                              int out_f32, int32_t* inds_out, float* wts_out, void* workspace, size_t ws_bytes,
-                              void* stream) {
-  if (!P) return fail(EF_ERR_INVALID, "pool is NULL");
-  if (layer < 0 || layer >= P->pc.n_layers) return fail(EF_ERR_RANGE, "layer %d out of range", layer);
-  if (T < 0) return fail(EF_ERR_INVALID, "T < 0");
-  if (T == 0) return EF_OK;
-  if (!x || !gate_w || !y) return fail(EF_ERR_INVALID, "null pointer");
-  if (!aligned16(x) || !aligned16(gate_w) || !aligned16(y)) return fail(EF_ERR_INVALID, "x/gate_w/y must be 16-byte aligned");
-  if (next_gate_w && layer + 1 >= P->pc.n_layers) return fail(EF_ERR_RANGE, "no layer after %d to predict", layer);
-  if (ws_bytes < ef_pool_workspace_size(P, T) || !workspace) return fail(EF_ERR_WORKSPACE, "workspace too small");
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev != P->dev) return fail(EF_ERR_INVALID, "pool belongs to device %d, current device is %d", P->dev, dev);
+namespace {
+void drop_tail_graphs(ef_slot_pool* P) {
+  for (auto& g : P->tails)
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+  P->tails.clear();
+}
+
+// The layer step's expert kernels on the slot arrays (slot ids in the pinned
+// staging, which the host rewrites before each launch): replayed from a CUDA
+// graph once the same layer has run with the same buffers, so the host issues
+// one launch instead of five kernel launches and their tensor-map encodes.
+ef_status run_tail(ef_slot_pool* P, int layer, const ef_moe_cfg& sc, const void* x, int T, const float* wts,
+                   const ef_qweight& qg, const ef_qweight& qu, const ef_qweight& qd, const FfnBufs& f, void* y,
+                   const void* ws, cudaStream_t st) {
+  if (g_trace_on)  // traced launches record events per kernel: run them eagerly
+    return moe_tail(&sc, x, T, P->h_slot, wts, qg, qu, qd, nullptr, nullptr, nullptr, f, y, st);
+  ef_slot_pool::TailGraph* g = nullptr;
+  for (auto& t : P->tails)
+    if (t.layer == layer && t.T == T && t.out_f32 == sc.out_f32 && t.x == x && t.y == y && t.wts == wts && t.ws == ws) {
+      g = &t;
+      break;
+    }
+  if (!g) {
+    if (P->tails.size() >= 4096) drop_tail_graphs(P);  // buffers keep changing: start over
+    P->tails.push_back({layer, T, sc.out_f32, x, y, wts, ws, 0, nullptr});
+    g = &P->tails.back();
+  }
+  if (!g->exec && g->uses++ == 0)
+    return moe_tail(&sc, x, T, P->h_slot, wts, qg, qu, qd, nullptr, nullptr, nullptr, f, y, st);
+  if (!g->exec) {
+    if (!P->cap_stream && cudaStreamCreateWithFlags(&P->cap_stream, cudaStreamNonBlocking) != cudaSuccess)
+      return fail(EF_ERR_CUDA, "slot pool: capture stream creation failed");
+    if (cudaStreamBeginCapture(P->cap_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+      return fail(EF_ERR_CUDA, "slot pool: stream capture failed to start");
+    const ef_status s = moe_tail(&sc, x, T, P->h_slot, wts, qg, qu, qd, nullptr, nullptr, nullptr, f, y, P->cap_stream);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(P->cap_stream, &graph);
+    if (s) {
+      if (graph) cudaGraphDestroy(graph);
+      return s;
+    }
+    if (e != cudaSuccess || !graph) return fail(EF_ERR_CUDA, "slot pool: capture failed: %s", cudaGetErrorString(e));
+    const cudaError_t ei = cudaGraphInstantiate(&g->exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ei != cudaSuccess) {
+      g->exec = nullptr;
+      return fail(EF_ERR_CUDA, "slot pool: graph instantiation failed: %s", cudaGetErrorString(ei));
+    }
+  }
+  if (cudaGraphLaunch(g->exec, st) != cudaSuccess)
+    return fail(EF_ERR_CUDA, "slot pool: graph launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return EF_OK;
+}
+
+// Copies ahead the experts predicted for layer nl that are not in its slots
+// (staged: they enter the policy only when a step uses them).  In a pool over
+// a store, an expert not yet in the host tier has its read started instead,
+// and is copied when a later prediction or its layer finds it there.
+ef_status stage_ahead(ef_slot_pool* P, int nl, const int32_t* pred_ids, int n) {
+  const int E = P->cfg.n_experts;
+  LayerSlots& N = P->layers[nl];
+  const std::vector<int> pred = distinct_sorted(pred_ids, n, E);
+  std::vector<char> nkeep(E, 0);
+  for (int e : pred) nkeep[e] = 1;
+  bool any = false;
+  CopyTimer t{};
+  ef_status s;
+  for (int e : pred) {
+    if (N.expert_slot[e] >= 0) continue;
+    int h = -1;
+    if (P->store) {
+      h = host_find(P, nl, e);
+      if (h < 0) {
+        host_fetch(P, nl, e, true);  // -1 (no blob to replace): the prediction is only a hint
+        continue;
+      }
+      if (!ef::store_done(&P->host_ticket[h]) || P->host_ticket[h].err.load()) continue;
+      host_touch(P, h);
+      P->st.host_hits++;
+    }
+    const int sl = take_slot(P, nl, nkeep);
+    if (sl < 0) break;  // no free slot: the prediction is only a hint
+    if (!any) {
+      copies_begin(P, 1, N);
+      t = timer_begin(P, P->lane[1].stream);
+      any = true;
+    }
+    if ((s = copy_expert(P, 1, nl, e, sl, h))) return s;
+    N.staged[e] = 1;
+    P->st.copies_prefetch++;
+  }
+  if (any) {
+    if ((s = flush_stage(P, 1))) return s;
+    cudaEventRecord(t.b, P->lane[1].stream);
+    P->timers.push_back(t);
+    cudaEventRecord(N.ready[1], P->lane[1].stream);
+    N.has_ready[1] = true;
+  }
+  return EF_OK;
+}
+
+// One streamed layer.  ahead_w / ahead_b: the gates of the next n_ahead
+// layers (0..2), routed on this layer's input as the lookahead predictions.
+ef_status pool_layer(ef_slot_pool* P, int layer, const void* x, int T, const void* gate_w, const float* e_bias,
+                     int n_ahead, const void* const* ahead_w, const float* const* ahead_b, void* y, int out_f32,
+                     int32_t* inds_out, float* wts_out, void* workspace, cudaStream_t st) {
+  using clk = std::chrono::steady_clock;
+  const auto h0 = clk::now();
   const ef_moe_cfg& cfg = P->cfg;
   const int E = cfg.n_experts, k = cfg.top_k, n = T * k;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   Carver c{static_cast<uint8_t*>(workspace)};
   PoolWs w;
   pool_ws(P, T, c, w);
   ef_status s;
   int* inds = inds_out ? inds_out : w.inds;
   float* wts = wts_out ? wts_out : w.wts;
-  // 1. route this layer, and predict the next layer's experts from the same input
-  if ((s = pool_route(cfg, x, T, gate_w, e_bias, w.logits, inds, wts, next_gate_w, next_e_bias, w.plogits, w.pinds,
-                      w.pwts, st)))
+  const void* gw[2] = {n_ahead > 0 ? ahead_w[0] : nullptr, n_ahead > 1 ? ahead_w[1] : nullptr};
+  const float* gb[2] = {n_ahead > 0 && ahead_b ? ahead_b[0] : nullptr, n_ahead > 1 && ahead_b ? ahead_b[1] : nullptr};
+  // 1. route this layer, and predict the next layers' experts from the same input
+  if ((s = pool_route(cfg, x, T, gate_w, e_bias, w.logits, inds, wts, gw[0], gb[0], w.plogits[0], w.pinds[0],
+                      w.pwts[0], gw[1], gb[1], w.plogits[1], w.pinds[1], w.pwts[1], st)))
     return s;
   if (n > P->h_cap) {
     if (P->h_inds) {
       cudaStreamSynchronize(st);  // no earlier layer still reads the old staging
       cudaFreeHost(P->h_inds);
     }
+    drop_tail_graphs(P);  // they read the old slot-id staging
     P->h_cap = std::max(n, 256);
-    if (cudaHostAlloc(reinterpret_cast<void**>(&P->h_inds), 3 * sizeof(int32_t) * P->h_cap + 64,
+    if (cudaHostAlloc(reinterpret_cast<void**>(&P->h_inds), 4 * sizeof(int32_t) * P->h_cap + 64,
                       cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer(reinterpret_cast<void**>(&P->d_inds), P->h_inds, 0) != cudaSuccess) {
       if (P->h_inds) cudaFreeHost(P->h_inds);
@@ -986,20 +1104,26 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
       P->h_cap = 0;
       return fail(EF_ERR_CUDA, "mapped pinned staging allocation failed");
     }
-    P->h_flag = reinterpret_cast<uint32_t*>(P->h_inds + 3 * P->h_cap);
+    P->h_flag = reinterpret_cast<uint32_t*>(P->h_inds + 4 * P->h_cap);
     *reinterpret_cast<volatile uint32_t*>(P->h_flag) = P->h_seq;
   }
   P->h_pred = P->h_inds + P->h_cap;
   P->h_slot = P->h_inds + 2 * P->h_cap;
+  P->h_pred2 = P->h_inds + 3 * P->h_cap;
   // the routing reaches the host through the mapped staging: a one-CTA kernel
   // stores the ids there and then the step's sequence number, which this
   // thread polls (no copy launch, no stream synchronisation)
   const uint32_t seq = ++P->h_seq;
   EF_LAUNCH("publish_ids", launch_pdl(ef::publish_ids_kernel, 1, 256, 0, st, (const int*)inds,
-                                      (const int*)(next_gate_w ? w.pinds : nullptr), n, P->d_inds,
-                                      P->d_inds + P->h_cap, reinterpret_cast<uint32_t*>(P->d_inds + 3 * P->h_cap),
+                                      (const int*)(gw[0] ? w.pinds[0] : nullptr),
+                                      (const int*)(gw[1] ? w.pinds[1] : nullptr), n, P->d_inds, P->d_inds + P->h_cap,
+                                      P->d_inds + 3 * P->h_cap, reinterpret_cast<uint32_t*>(P->d_inds + 4 * P->h_cap),
                                       seq));
+  const auto h1 = clk::now();
   if ((s = wait_published(P->h_flag, seq, st))) return s;
+  const auto h2 = clk::now();
+  P->st.route_wait_ms += std::chrono::duration<double, std::milli>(h2 - h1).count();
+  P->st.host_ms += std::chrono::duration<double, std::milli>(h1 - h0).count();
   if (P->rec_on)  // the reference records each routed entry in (token, k) order (ef_engine.py:640-646)
     for (int i = 0; i < n; ++i) {
       P->rec_pairs.push_back(layer);
@@ -1043,7 +1167,8 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
       L.staged[e] = 0;
       continue;
     }
-    int sl = take_slot(P, layer, keep);
+    bool from_staged = false;
+    int sl = take_slot(P, layer, keep, &from_staged);
     if (sl < 0) {  // full: evict now the lowest-priority resident expert this step does not use
       const long long v = L.policy.victim_excluding(keep);
       if (v < 0) return fail(EF_ERR_SLOT_MISS, "layer %d: no slot for expert %d (raise headroom)", layer, e);
@@ -1058,6 +1183,9 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
       t = timer_begin(P, P->lane[0].stream);
       any = true;
     }
+    // a slot taken from an unused prefetch may still be written by the
+    // prefetch lane: this lane's scatter into it goes after that lane's
+    if (from_staged && L.has_ready[1]) cudaStreamWaitEvent(P->lane[0].stream, L.ready[1], 0);
     if ((s = copy_expert(P, 0, layer, e, sl, P->store ? host_find(P, layer, e) : -1))) return s;
     P->st.copies_sync++;
   }
@@ -1068,9 +1196,18 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
     cudaEventRecord(L.ready[0], P->lane[0].stream);
     L.has_ready[0] = true;
   }
-  // this layer's experts wait for both lanes' copies into its slots
-  for (int ln = 0; ln < 2; ++ln)
-    if (L.has_ready[ln]) cudaStreamWaitEvent(st, L.ready[ln], 0);
+  // this layer's experts wait for both lanes' copies into its slots (the
+  // stall is timed on the compute stream)
+  bool pending[2];
+  for (int ln = 0; ln < 2; ++ln) pending[ln] = L.has_ready[ln] && cudaEventQuery(L.ready[ln]) != cudaSuccess;
+  if (pending[0] || pending[1]) {
+    CopyTimer wt = timer_begin(P, st);
+    wt.stall = true;
+    for (int ln = 0; ln < 2; ++ln)
+      if (pending[ln]) cudaStreamWaitEvent(st, L.ready[ln], 0);
+    cudaEventRecord(wt.b, st);
+    P->timers.push_back(wt);
+  }
   // 3. experts on slot ids
   // slot ids stay in pinned memory: the permute kernel reads them over the
   // link (n ints) instead of a copy that would queue behind the expert copies
@@ -1082,55 +1219,38 @@ ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, 
   const ef_qweight qg{reinterpret_cast<uint32_t*>(v.w[0]), reinterpret_cast<uint16_t*>(v.s[0]), reinterpret_cast<uint16_t*>(v.b[0])};
   const ef_qweight qu{reinterpret_cast<uint32_t*>(v.w[1]), reinterpret_cast<uint16_t*>(v.s[1]), reinterpret_cast<uint16_t*>(v.b[1])};
   const ef_qweight qd{reinterpret_cast<uint32_t*>(v.w[2]), reinterpret_cast<uint16_t*>(v.s[2]), reinterpret_cast<uint16_t*>(v.b[2])};
-  if ((s = moe_tail(&sc, x, T, P->h_slot, wts, qg, qu, qd, nullptr, nullptr, nullptr, w.f, y, st))) return s;
+  if ((s = run_tail(P, layer, sc, x, T, wts, qg, qu, qd, w.f, y, workspace, st))) return s;
   cudaEventRecord(L.last_use, st);
   L.has_use = true;
-  // 4. lookahead copies for the next layer, issued after this layer's expert
+  // 4. lookahead copies for the next layers, issued after this layer's expert
   //    kernels so that the host work and the copies overlap them (the step
   //    synchronised once, for the routing; host time before the launches is
-  //    idle GPU time); in a pool over a store, an expert not yet in the host
-  //    tier has its read started instead, and is copied when its layer runs
-  if (next_gate_w) {
-    const int nl = layer + 1;
-    LayerSlots& N = P->layers[nl];
-    const std::vector<int> pred = distinct_sorted(P->h_pred, n, E);
-    std::vector<char> nkeep(E, 0);
-    for (int e : pred) nkeep[e] = 1;
-    bool any = false;
-    CopyTimer t{};
-    for (int e : pred) {
-      if (N.expert_slot[e] >= 0) continue;
-      int h = -1;
-      if (P->store) {
-        h = host_find(P, nl, e);
-        if (h < 0) {
-          host_fetch(P, nl, e, true);  // -1 (no blob to replace): the prediction is only a hint
-          continue;
-        }
-        if (!ef::store_done(&P->host_ticket[h]) || P->host_ticket[h].err.load()) continue;
-        host_touch(P, h);
-        P->st.host_hits++;
-      }
-      const int sl = take_slot(P, nl, nkeep);
-      if (sl < 0) break;  // no free slot: the prediction is only a hint
-      if (!any) {
-        copies_begin(P, 1, N);
-        t = timer_begin(P, P->lane[1].stream);
-        any = true;
-      }
-      if ((s = copy_expert(P, 1, nl, e, sl, h))) return s;
-      N.staged[e] = 1;
-      P->st.copies_prefetch++;
-    }
-    if (any) {
-      if ((s = flush_stage(P, 1))) return s;
-      cudaEventRecord(t.b, P->lane[1].stream);
-      P->timers.push_back(t);
-      cudaEventRecord(N.ready[1], P->lane[1].stream);
-      N.has_ready[1] = true;
-    }
-  }
+  //    idle GPU time); the nearer layer's copies are queued first
+  for (int a = 0; a < n_ahead; ++a)
+    if ((s = stage_ahead(P, layer + 1 + a, a ? P->h_pred2 : P->h_pred, n))) return s;
+  P->st.host_ms += std::chrono::duration<double, std::milli>(clk::now() - h2).count();
   return EF_OK;
+}
+}  // namespace
+
+ef_status ef_pool_moe_forward(ef_slot_pool* P, int layer, const void* x, int T, const void* gate_w,
+                              const float* e_bias, const void* next_gate_w, const float* next_e_bias, void* y,
+                              int out_f32, int32_t* inds_out, float* wts_out, void* workspace, size_t ws_bytes,
+                              void* stream) {
+  if (!P) return fail(EF_ERR_INVALID, "pool is NULL");
+  if (layer < 0 || layer >= P->pc.n_layers) return fail(EF_ERR_RANGE, "layer %d out of range", layer);
+  if (T < 0) return fail(EF_ERR_INVALID, "T < 0");
+  if (T == 0) return EF_OK;
+  if (!x || !gate_w || !y) return fail(EF_ERR_INVALID, "null pointer");
+  if (!aligned16(x) || !aligned16(gate_w) || !aligned16(y)) return fail(EF_ERR_INVALID, "x/gate_w/y must be 16-byte aligned");
+  if (next_gate_w && layer + 1 >= P->pc.n_layers) return fail(EF_ERR_RANGE, "no layer after %d to predict", layer);
+  if (ws_bytes < ef_pool_workspace_size(P, T) || !workspace) return fail(EF_ERR_WORKSPACE, "workspace too small");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != P->dev) return fail(EF_ERR_INVALID, "pool belongs to device %d, current device is %d", P->dev, dev);
+  const float* nb = next_e_bias;
+  return pool_layer(P, layer, x, T, gate_w, e_bias, next_gate_w ? 1 : 0, &next_gate_w, &nb, y, out_f32, inds_out,
+                    wts_out, workspace, static_cast<cudaStream_t>(stream));
 }
 
 size_t ef_pool_decode_workspace_size(const ef_slot_pool* P, int T) {
@@ -1147,9 +1267,15 @@ ef_status ef_pool_decode_step(ef_slot_pool* P, float* r, int T, const void* cons
   if (T < 0) return fail(EF_ERR_INVALID, "T < 0");
   if (T == 0) return EF_OK;
   if (!r || !gate_w) return fail(EF_ERR_INVALID, "null pointer");
+  if (lookahead < 0 || lookahead > 2) return fail(EF_ERR_INVALID, "lookahead must be 0, 1 or 2 layers");
   if (ws_bytes < ef_pool_decode_workspace_size(P, T) || !workspace) return fail(EF_ERR_WORKSPACE, "workspace too small");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int H = P->cfg.hidden, L = P->pc.n_layers;
+  for (int l = 0; l < L; ++l)
+    if (!gate_w[l] || !aligned16(gate_w[l])) return fail(EF_ERR_INVALID, "gate_w[%d] null or not 16-byte aligned", l);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != P->dev) return fail(EF_ERR_INVALID, "pool belongs to device %d, current device is %d", P->dev, dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int bf = P->cfg.act_dtype == EF_DT_BF16;
   Carver c{static_cast<uint8_t*>(workspace)};
   uint16_t* x = c.take<uint16_t>((size_t)T * H);
@@ -1160,9 +1286,9 @@ ef_status ef_pool_decode_step(ef_slot_pool* P, float* r, int T, const void* cons
   for (int l = 0; l < L; ++l) {
     EF_LAUNCH("add_rmsnorm", launch_pdl(ef::add_rmsnorm_kernel, T, ef::kNormThreads, 0, st, r,
                                             l ? static_cast<const float*>(y) : nullptr, H, eps, bf, x));
-    const bool la = lookahead && l + 1 < L;
-    if ((s = ef_pool_moe_forward(P, l, x, T, gate_w[l], e_bias ? e_bias[l] : nullptr, la ? gate_w[l + 1] : nullptr,
-                                 la && e_bias ? e_bias[l + 1] : nullptr, y, 1, nullptr, nullptr, fws, fws_bytes, st)))
+    const int n_ahead = std::min(lookahead, L - 1 - l);
+    if ((s = pool_layer(P, l, x, T, gate_w[l], e_bias ? e_bias[l] : nullptr, n_ahead, gate_w + l + 1,
+                        e_bias ? e_bias + l + 1 : nullptr, y, 1, nullptr, nullptr, fws, st)))
       return s;
   }
   EF_LAUNCH("add_rmsnorm", launch_pdl(ef::add_rmsnorm_kernel, T, ef::kNormThreads, 0, st, r,
@@ -1255,6 +1381,8 @@ ef_status ef_pool_destroy(ef_slot_pool* P) {
     cudaEventDestroy(t.a);
     cudaEventDestroy(t.b);
   }
+  drop_tail_graphs(P);
+  if (P->cap_stream) cudaStreamDestroy(P->cap_stream);
   for (auto& L : P->layers) {
     cudaEventDestroy(L.ready[0]);
     cudaEventDestroy(L.ready[1]);

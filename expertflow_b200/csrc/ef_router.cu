@@ -69,19 +69,25 @@ EF_DEV void cvt8(const uint4& v, int is_bf16, float (&f)[8]) {
 }
 
 // CTA = 4 warps computes logits for TT tokens x TE experts.  blockIdx.z = 1
-// takes a second gate (wg2 -> logits2) over the same tokens, so a layer's
-// routing and the next layer's prediction share one launch.
+// and 2 take a second and third gate (wg2 -> logits2, wg3 -> logits3) over the
+// same tokens, so a layer's routing and the predictions of the next layers
+// share one launch.
 template <int TT, int TE>
 __global__ void __launch_bounds__(128) router_logits_kernel(const uint16_t* __restrict__ x, int x_bf16,
                                                             const uint16_t* __restrict__ wg, int w_bf16,
                                                             int T, int E, int H, float* __restrict__ logits,
                                                             const uint16_t* __restrict__ wg2,
-                                                            float* __restrict__ logits2) {
+                                                            float* __restrict__ logits2,
+                                                            const uint16_t* __restrict__ wg3,
+                                                            float* __restrict__ logits3) {
   pdl_wait();
   pdl_launch_next();
-  if (blockIdx.z) {
+  if (blockIdx.z == 1) {
     wg = wg2;
     logits = logits2;
+  } else if (blockIdx.z == 2) {
+    wg = wg3;
+    logits = logits3;
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * TT, e0 = blockIdx.y * TE;
@@ -173,7 +179,8 @@ constexpr int kMaxE = 512;
 constexpr int kSelWarps = 4;
 
 // One warp per token.  Scores live in shared memory (E <= 512).  blockIdx.y = 1
-// selects the second gate's logits / bias / outputs (see router_logits_kernel).
+// and 2 select the second and third gate's logits / bias / outputs (see
+// router_logits_kernel).
 __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const float* __restrict__ logits,
                                                                        const float* __restrict__ e_bias, int T,
                                                                        SelCfg cfg, int* __restrict__ inds,
@@ -181,14 +188,23 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const flo
                                                                        const float* __restrict__ logits2,
                                                                        const float* __restrict__ e_bias2,
                                                                        int* __restrict__ inds2,
-                                                                       float* __restrict__ wts2) {
+                                                                       float* __restrict__ wts2,
+                                                                       const float* __restrict__ logits3,
+                                                                       const float* __restrict__ e_bias3,
+                                                                       int* __restrict__ inds3,
+                                                                       float* __restrict__ wts3) {
   pdl_wait();
   pdl_launch_next();
-  if (blockIdx.y) {
+  if (blockIdx.y == 1) {
     logits = logits2;
     e_bias = e_bias2;
     inds = inds2;
     wts = wts2;
+  } else if (blockIdx.y == 2) {
+    logits = logits3;
+    e_bias = e_bias3;
+    inds = inds3;
+    wts = wts3;
   }
   __shared__ float s_score[kSelWarps][kMaxE];  // selection score
   __shared__ float s_keep[kSelWarps][kMaxE];   // sigmoid value / logit for weights
@@ -298,27 +314,29 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const flo
 }
 
 // ---------------------------------------------------------------- launchers
-// wg2 / logits2 (optional): a second gate routed in the same launch.
+// wg2 / logits2, wg3 / logits3 (optional, wg3 only with wg2): further gates
+// routed over the same tokens in the same launch.
 cudaError_t launch_router_logits(const uint16_t* x, int x_bf16, const uint16_t* wg, int w_bf16, int T, int E,
-                                 int H, float* logits, cudaStream_t st, const uint16_t* wg2, float* logits2) {
-  const int nz = wg2 ? 2 : 1;
+                                 int H, float* logits, cudaStream_t st, const uint16_t* wg2, float* logits2,
+                                 const uint16_t* wg3, float* logits3) {
+  const int nz = wg2 ? (wg3 ? 3 : 2) : 1;
   if (T >= 64) {
     dim3 grid((T + 7) / 8, (E + 7) / 8, nz);
     return launch_pdl(router_logits_kernel<8, 8>, grid, 128, 0, st, x, x_bf16, wg, w_bf16, T, E, H, logits, wg2,
-                      logits2);
+                      logits2, wg3, logits3);
   } else if (T >= 4) {
     dim3 grid((T + 3) / 4, (E + 3) / 4, nz);
     return launch_pdl(router_logits_kernel<4, 4>, grid, 128, 0, st, x, x_bf16, wg, w_bf16, T, E, H, logits, wg2,
-                      logits2);
+                      logits2, wg3, logits3);
   } else {
     int te = (E >= 256) ? 2 : 1;
     dim3 grid(T, (E + te - 1) / te, nz);
     if (te == 2)
       return launch_pdl(router_logits_kernel<1, 2>, grid, 128, 0, st, x, x_bf16, wg, w_bf16, T, E, H, logits, wg2,
-                        logits2);
+                        logits2, wg3, logits3);
     else
       return launch_pdl(router_logits_kernel<1, 1>, grid, 128, 0, st, x, x_bf16, wg, w_bf16, T, E, H, logits, wg2,
-                        logits2);
+                        logits2, wg3, logits3);
   }
   return cudaGetLastError();
 }
@@ -326,11 +344,11 @@ cudaError_t launch_router_logits(const uint16_t* x, int x_bf16, const uint16_t* 
 cudaError_t launch_router_select(const float* logits, const float* e_bias, int T, int E, int k, int mode,
                                  int norm_topk, int n_group, int topk_group, float scaling, int* inds, float* wts,
                                  cudaStream_t st, const float* logits2, const float* e_bias2, int* inds2,
-                                 float* wts2) {
+                                 float* wts2, const float* logits3, const float* e_bias3, int* inds3, float* wts3) {
   SelCfg c{E, k, mode, norm_topk, n_group, topk_group, scaling};
-  dim3 grid((T + kSelWarps - 1) / kSelWarps, logits2 ? 2 : 1);
+  dim3 grid((T + kSelWarps - 1) / kSelWarps, logits2 ? (logits3 ? 3 : 2) : 1);
   return launch_pdl(router_select_kernel, grid, kSelWarps * 32, 0, st, logits, e_bias, T, c, inds, wts, logits2, e_bias2,
-                    inds2, wts2);
+                    inds2, wts2, logits3, e_bias3, inds3, wts3);
 }
 
 }  // namespace ef

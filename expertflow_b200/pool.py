@@ -352,11 +352,16 @@ class ExpertSlotPool:
             wts_out.data_ptr() if wts_out is not None else None, ws.data_ptr(), ws.numel(), _stream_ptr(xf.device)))
         return y.reshape(x.shape)
 
-    def decode_step(self, r: torch.Tensor, gates: Sequence[MoEGate], lookahead: bool = True,
+    def decode_step(self, r: torch.Tensor, gates: Sequence[MoEGate], lookahead: int = 1,
                     eps: float = 1e-6) -> torch.Tensor:
         """One decode step through all layers in the library (ef_pool_decode_step):
         per layer r += y, x = rmsnorm(r), y = MoE_layer(x); then r += y and the
-        per-token trim.  r: fp32 [T, H] residual stream, updated in place."""
+        per-token trim.  r: fp32 [T, H] residual stream, updated in place.
+        lookahead: how many following layers (0, 1 or 2; True is 1) have their
+        experts predicted from each layer's input and copied ahead."""
+        lookahead = int(lookahead)
+        if not 0 <= lookahead <= 2:
+            raise ValueError("lookahead must be 0, 1 or 2 layers")
         if r.dtype != torch.float32 or not r.is_cuda or not r.is_contiguous():
             raise ValueError("r must be a contiguous fp32 CUDA tensor")
         if len(gates) != self.n_layers:
@@ -450,8 +455,8 @@ def make_host_layers(spec: MoESpec, n_layers: int, seed: int = 0, device="cuda")
 
 def _main(argv=None) -> None:
     """A streamed decode for profiling: `layers` Qwen3-30B-A3B-shaped layers,
-    25 % of each layer's experts in HBM, Zipf(1.1)-biased routing, one-layer
-    lookahead; prints the time per token.
+    25 % of each layer's experts in HBM, Zipf(1.1)-biased routing, lookahead
+    over --lookahead layers (default 1); prints the time per token.
     python -m expertflow_b200.pool --layers 8 --steps 24"""
     import argparse
 
@@ -480,7 +485,7 @@ def _main(argv=None) -> None:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for r in rs:
-        pl.decode_step(r, gates, lookahead=bool(a.lookahead))
+        pl.decode_step(r, gates, lookahead=a.lookahead)
     e1.record()
     torch.cuda.synchronize()
     st = pl.stats()

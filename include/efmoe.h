@@ -352,6 +352,9 @@ typedef struct {
   long long host_reads_ahead;/* of those, reads started by the lookahead */
   long long host_evictions;  /* host-tier blobs replaced */
   double read_wait_ms;       /* host time the pool waited for file reads */
+  double copy_wait_ms;       /* compute-stream time stalled on copies into a layer's slots */
+  double route_wait_ms;      /* host time spent waiting for the routing to be published */
+  double host_ms;            /* other host time in the pool's layer steps (decisions, launches) */
 } ef_pool_stats;
 typedef struct ef_slot_pool ef_slot_pool;
 /* cfg: the layer configuration (n_shared must be 0); host_*: n_layers entries of
@@ -375,8 +378,9 @@ ef_status ef_pool_end_token(ef_slot_pool* pool); /* trim + decay every layer (on
 /* One decode step through all n_layers pooled layers: for each layer,
  * r += y (from the previous layer), x = r / sqrt(mean(r^2) + eps) in the
  * activation dtype (the pre-MoE norm), y = ef_pool_moe_forward(layer, x) with
- * the next layer's gate as lookahead when `lookahead`; finally r += y and
- * ef_pool_end_token.  r [T, H] fp32 (the residual stream) is updated in place;
+ * the gates of the next `lookahead` layers (0, 1 or 2) routed on x as the
+ * lookahead predictions (the nearer layer's copies are queued first); finally
+ * r += y and ef_pool_end_token.  r [T, H] fp32 (the residual stream) is updated in place;
  * gate_w / e_bias: n_layers device pointers (e_bias may be NULL, or hold NULLs). */
 size_t ef_pool_decode_workspace_size(const ef_slot_pool* pool, int T);
 ef_status ef_pool_decode_step(ef_slot_pool* pool, float* r, int T, const void* const* gate_w,

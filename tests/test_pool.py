@@ -164,9 +164,10 @@ def test_pool_rejects_device_arrays(P):
 
 @pytest.mark.gpu
 def test_pool_decode_step_independent_of_residency(P):
-    """The in-library multi-layer decode step: a pool with 6 of 32 experts per
-    layer in HBM and one holding every expert produce bit-identical residual
-    streams (residency changes where weights come from, never the result)."""
+    """The in-library multi-layer decode step: pools with 6 of 32 experts per
+    layer in HBM (one- and two-layer lookahead) and one holding every expert
+    produce bit-identical residual streams (residency changes where weights
+    come from, never the result)."""
     import torch
     from expertflow_b200 import moe, synthetic
 
@@ -182,7 +183,7 @@ def test_pool_decode_step_independent_of_residency(P):
         gw = (torch.randn((spec.n_experts, spec.hidden), generator=g, device=dev) * 0.02).to(torch.float16)
         gates.append(moe.MoEGate(gw, spec.top_k, "softmax", True, e_score_correction_bias=bias[layer].contiguous()))
     out = []
-    for budget, la in ((6, True), (spec.n_experts, False)):
+    for budget, la in ((6, 1), (6, 2), (spec.n_experts, 0)):
         pl = P.ExpertSlotPool(spec, host, budget=budget, headroom=spec.top_k)
         rs = []
         for t in range(steps):
@@ -192,10 +193,15 @@ def test_pool_decode_step_independent_of_residency(P):
         torch.cuda.synchronize()
         out.append((torch.stack(rs), pl.stats()))
         pl.close()
-    (ra, sa), (rb, sb) = out
-    assert torch.isfinite(ra).all() and torch.equal(ra, rb)
+    (ra, sa), (r2, s2), (rb, sb) = out
+    assert torch.isfinite(ra).all() and torch.equal(ra, rb) and torch.equal(r2, rb)
     assert sa["tokens"] == steps and sa["copies_prefetch"] > 0
+    assert s2["copies_prefetch"] > 0
     assert sb["copies_sync"] <= spec.n_experts * n_layers
+    pl = P.ExpertSlotPool(spec, host, budget=6, headroom=spec.top_k)
+    with pytest.raises(ValueError):
+        pl.decode_step(synthetic.make_x_torch(spec, 1, seed=1).float().contiguous(), gates, lookahead=3)
+    pl.close()
     assert moe.device_error() == 0
 
 
