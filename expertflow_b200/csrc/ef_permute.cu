@@ -231,6 +231,8 @@ __global__ void combine_kernel(const float* rows, const int* __restrict__ inv, c
   const int c4 = blockIdx.x * blockDim.x + threadIdx.x;  // index of a 4-column quad
   if (t >= T || c4 * 4 >= H) return;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  // unrolled so that several rows' loads are in flight (the sum stays in j order)
+#pragma unroll 4
   for (int j = 0; j < k; ++j) {
     int r = inv[(size_t)t * k + j];
     float w = wts ? wts[(size_t)t * k + j] : 1.0f;

@@ -100,6 +100,9 @@ __global__ void __launch_bounds__(128) router_logits_kernel(const uint16_t* __re
 
   const uint4* xv = reinterpret_cast<const uint4*>(x);
   const uint4* wv = reinterpret_cast<const uint4*>(wg);
+  // small tiles: several iterations' loads in flight per thread (a thread's
+  // FMA order over c is unchanged)
+#pragma unroll(TT * TE <= 4 ? 4 : 1)
   for (int c = warp * 32 + lane; c < nch; c += 128) {
     float xf[TT][8], wf[TE][8];
 #pragma unroll
