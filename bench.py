@@ -465,6 +465,7 @@ def section_stream(name, spec, args, dev):
              "copies_prefetch": st["copies_prefetch"], "prefetch_used": st["prefetch_used"],
              "copies_sync": st["copies_sync"],
              "stall_on_copies_ms_per_token": round(st["copy_wait_ms"] / steps, 4),
+             "copy_hidden_frac_device": round(1.0 - st["copy_wait_ms"] / st["copy_ms"], 4) if st["copy_ms"] > 0 else None,
              "host_route_wait_ms_per_token": round(st["route_wait_ms"] / steps, 4),
              "host_other_ms_per_token": round(st["host_ms"] / steps, 4)}
         out[("no_lookahead", "lookahead", "lookahead2")[la]] = d
@@ -1005,9 +1006,9 @@ def _summary(line, sections):
     if c3:
         la = c3.get("lookahead", {})
         la2 = c3.get("lookahead2", {})
-        out["c3"] = {"tok_s": la.get("tokens_per_s"), "h2d_overlap": la.get("h2d_overlap"),
-                     "tok_s_lookahead2": la2.get("tokens_per_s"), "h2d_overlap_lookahead2": la2.get("h2d_overlap"),
-                     "resident_tok_s": c3.get("resident_tokens_per_s")}
+        out["c3"] = {"tok_s": la2.get("tokens_per_s"), "lookahead_layers": 2, "h2d_overlap": la2.get("h2d_overlap"),
+                     "copy_hidden_frac_device": la2.get("copy_hidden_frac_device"),
+                     "tok_s_lookahead1": la.get("tokens_per_s"), "resident_tok_s": c3.get("resident_tokens_per_s")}
     kq = sections.get("kq")
     if kq:
         out["kq"] = {f"{p['format']}_T{p['tokens']}": p["frac"] for p in kq["points"] if p["tokens"] == 1}
