@@ -21,7 +21,13 @@
 //
 // GEMV (decode): mma.sync m16n8k16 with fp32 accumulation.  A warp owns 16
 // rows; lane (g = lane/4, c = lane%4) decodes rows g and g+8 straight into its
-// A fragments.  Within each 256-element block the reduction index is permuted
+// A fragments.  Q2_K and Q3_K fragments are the reference's fp16 weights
+// (RN16 of the exact value); Q4_K codes go into the MMA exactly, as the fp16
+// values 1024 + q (one LOP3 per pair), each MMA's 16 reduction indices inside
+// one 32-element sub-block, and the sub-block's scale and min are folded in
+// fp32 afterwards:  y += A D - (1024 A + B) X,  D = sum (1024 + q) x,  X = sum x
+// (A = d sc, B = dmin mn), which is sum (A q - B) x without the fp16 rounding of
+// each weight.  Within each 256-element block the reduction index is permuted
 // so that lane c's 64 elements of a row sit in whole code words of the block
 // (the order depends on the format); the activations are permuted the same
 // way by kquant_prep_kernel, so every MMA pairs matching weights and inputs.
@@ -47,8 +53,11 @@ __host__ __device__ inline int kq_elem(int type, int c, int j, int t) {
     const int h = j >> 3, s = (j >> 1) & 3, u = j & 1;
     return 128 * h + 32 * s + 8 * c + 4 * u + t;
   }
-  const int w = j >> 1, v = j & 1;
-  return (t >= 2 ? 128 : 0) + 32 * c + 4 * w + 2 * v + (t & 1);
+  // Q4_K: MMA j = 4J + 2h + u takes the low (h = 0: sub-block J) or high
+  // (h = 1: sub-block 4 + J) nibbles of qs word 32J + 8c + 4u; slots t0, t1
+  // are its bytes 0 and 2, t2, t3 its bytes 1 and 3
+  const int J = j >> 2, h = (j >> 1) & 1, u = j & 1;
+  return 32 * (J + 4 * h) + 8 * c + 4 * u + ((t & 1) << 1) + (t >> 1);
 }
 
 EF_DEV float kq_f16(const uint8_t* p) {  // fp16 field (2-byte aligned)
@@ -168,65 +177,57 @@ struct KqRow<kKqQ3> {
 
 template <>
 struct KqRow<kKqQ4> {
-  uint4 q0, q1;    // qs bytes 32c .. 32c+31
+  uint2 qw[4];     // [J]: qs bytes 32J + 8c .. 32J + 8c + 7
   uint32_t s[3];   // scales[12]
   uint32_t dd;     // d | dmin << 16
-  // after prep(): A of the low (sub-block c) and high (4 + c) nibbles times
-  // 2^-p for the bit position p each code is read at, and the two mins
-  float al[4], ah[4], bl, bh;
+  float A[2], C[2];  // after prep(): sub-blocks 2c, 2c + 1: A = d sc, C = 1024 A + dmin mn
   EF_DEV void load(const uint8_t* blk, int c) {
-    const uint4* q = reinterpret_cast<const uint4*>(blk + 16 + 32 * c);
-    q0 = __ldg(q);
-    q1 = __ldg(q + 1);
+#pragma unroll
+    for (int J = 0; J < 4; ++J) qw[J] = __ldg(reinterpret_cast<const uint2*>(blk + 16 + 32 * J + 8 * c));
     const uint32_t* w = reinterpret_cast<const uint32_t*>(blk);
     dd = __ldg(w);
     s[0] = __ldg(w + 1);
     s[1] = __ldg(w + 2);
     s[2] = __ldg(w + 3);
   }
+  // the same words from a block staged in shared memory
+  EF_DEV void load_shared(const uint8_t* blk, int c) {
+#pragma unroll
+    for (int J = 0; J < 4; ++J) qw[J] = *reinterpret_cast<const uint2*>(blk + 16 + 32 * J + 8 * c);
+    const uint4 h = *reinterpret_cast<const uint4*>(blk);
+    dd = h.x;
+    s[0] = h.y;
+    s[1] = h.z;
+    s[2] = h.w;
+  }
+  // byte i of scales[12] (i is lane-dependent: selects, not an indexed load,
+  // keep the words in registers)
+  EF_DEV uint32_t sbyte(int i) const {
+    const uint32_t w = i < 4 ? s[0] : (i < 8 ? s[1] : s[2]);
+    return (w >> (8 * (i & 3))) & 0xffu;
+  }
+  // sub-block j: sc = s[j] & 63; mn = s[8 + j] & 63 (j < 4), else
+  // (s[j - 4] >> 6) | ((s[j + 4] >> 2) & 0x30) (the reference's decode)
   EF_DEV void prep(int c) {
     const float d = __half2float(__ushort_as_half((uint16_t)dd));
     const float m = __half2float(__ushort_as_half((uint16_t)(dd >> 16)));
-    const uint32_t sc_lo = (s[0] >> (8 * c)) & 0xffu;  // byte c
-    const uint32_t sc_hi = (s[1] >> (8 * c)) & 0xffu;  // byte 4 + c
-    const uint32_t mn_b = (s[2] >> (8 * c)) & 0xffu;   // byte 8 + c
-    const float Alo = d * (float)(sc_lo & 63u), Ahi = d * (float)(sc_hi & 63u);
-    bl = m * (float)(mn_b & 63u);
-    bh = m * (float)((sc_lo >> 6) | ((mn_b >> 2) & 0x30u));
-    // positions: low nibbles at 0, 8, 16 (word) and 12 (word >> 12);
-    //            high nibbles at 4, 12 (word) and 8, 16 (word >> 12)
-    al[0] = Alo;
-    al[1] = Alo * 0x1p-8f;
-    al[2] = Alo * 0x1p-16f;
-    al[3] = Alo * 0x1p-12f;
-    ah[0] = Ahi * 0x1p-4f;
-    ah[1] = Ahi * 0x1p-12f;
-    ah[2] = Ahi * 0x1p-8f;
-    ah[3] = Ahi * 0x1p-16f;
-  }
-  // MMAs j = 4QQ .. 4QQ+3 (j = 2w + v: word w of the lane's 32 bytes, bytes
-  // 2v, 2v+1; t0, t1 their low nibbles, t2, t3 their high nibbles).  A code
-  // at bit position p is read as the float q 2^p (its bits OR'ed into the
-  // mantissa of 2^23, minus 2^23) and scaled by A 2^-p: the same exact A q.
-  template <int QQ>
-  EF_DEV void frags(int, uint32_t (&lo)[4], uint32_t (&hi)[4]) const {
-    const uint4 qq = QQ < 2 ? q0 : q1;
-    const uint32_t ws[2] = {(QQ & 1) ? qq.z : qq.x, (QQ & 1) ? qq.w : qq.y};
 #pragma unroll
-    for (int w = 0; w < 2; ++w) {
-      const uint32_t W = ws[w], Wh = W >> 12;
-      lo[2 * w] = pack_h2(fmaf(al[0], code_f32(W & 0xFu), -bl), fmaf(al[1], code_f32(W & 0xF00u), -bl));
-      hi[2 * w] = pack_h2(fmaf(ah[0], code_f32(W & 0xF0u), -bh), fmaf(ah[1], code_f32(W & 0xF000u), -bh));
-      lo[2 * w + 1] = pack_h2(fmaf(al[2], code_f32(W & 0xF0000u), -bl), fmaf(al[3], code_f32(Wh & 0xF000u), -bl));
-      hi[2 * w + 1] = pack_h2(fmaf(ah[2], code_f32(Wh & 0xF00u), -bh), fmaf(ah[3], code_f32(Wh & 0xF0000u), -bh));
+    for (int i = 0; i < 2; ++i) {
+      const int j = 2 * c + i;
+      const uint32_t sc = sbyte(j) & 63u;
+      const uint32_t mn = j < 4 ? (sbyte(8 + j) & 63u) : ((sbyte(j - 4) >> 6) | ((sbyte(j + 4) >> 2) & 0x30u));
+      A[i] = d * (float)sc;
+      C[i] = fmaf(1024.0f, A[i], m * (float)mn);
     }
   }
 };
 
-// Permute and convert the activations: xp fp16 [n_tok8][K] (tokens >= T zero).
+// Permute and convert the activations: xp fp16 [n_tok8][K] (tokens >= T zero);
+// Q4_K also the sums of each 32-element sub-block of the rounded values, xs
+// fp32 [n_tok8][K / 32], in element order.
 template <int TYPE>
 __global__ void kquant_prep_kernel(const uint16_t* __restrict__ x, int act_bf16, int T, int K, int n_tok8,
-                                   uint16_t* __restrict__ xp) {
+                                   uint16_t* __restrict__ xp, float* __restrict__ xs) {
   const long long total = (long long)n_tok8 * K;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -241,6 +242,19 @@ __global__ void kquant_prep_kernel(const uint16_t* __restrict__ x, int act_bf16,
       out = __half_as_ushort(__float2half_rn(v));
     }
     xp[i] = out;
+  }
+  if (TYPE == kKqQ4) {
+    const int nsb = K >> 5;
+    const long long tsum = (long long)n_tok8 * nsb;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < tsum;
+         i += (long long)gridDim.x * blockDim.x) {
+      const int tok = (int)(i / nsb), sb = (int)(i % nsb);
+      float sum = 0.0f;
+      if (tok < T)
+        for (int e = 0; e < 32; ++e)
+          sum += __half2float(__float2half_rn(act_to_f32(x[(size_t)tok * K + 32 * sb + e], act_bf16)));
+      xs[i] = sum;
+    }
   }
 }
 
@@ -282,6 +296,52 @@ EF_DEV void kq_block_mma(KqRow<TYPE>& r0, KqRow<TYPE>& r1, int c, const uint16_t
   kq_quarter_mma<TYPE, NT, 3>(r0, r1, c, xrow, tok_off, acc);
 }
 
+// Q4_K: one block of both rows.  Per sub-block: two MMAs on the exact codes
+// into a fresh accumulator, then the fold with the sub-block's A and C of each
+// row (decoded by the quad's lane that owns the sub-block, passed by shuffle)
+// and the tokens' sub-block sums.  xs_blk: the sums of this block (xs + 8 kb);
+// xs_off[n][i]: the row offset of token 8n + 2c + i in xs.
+template <int NT>
+EF_DEV void kq_block_q4(KqRow<kKqQ4>& r0, KqRow<kKqQ4>& r1, int c, const uint16_t* __restrict__ xrow,
+                        const size_t (&tok_off)[NT], const float* __restrict__ xs_blk,
+                        const size_t (&xs_off)[NT][2], float (&acc)[NT][4]) {
+  r0.prep(c);
+  r1.prep(c);
+  const int qbase = (threadIdx.x & 31) & ~3;
+#pragma unroll
+  for (int J = 0; J < 4; ++J)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int sb = J + 4 * h;
+      uint32_t a[2][4];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint32_t w0 = u ? r0.qw[J].y : r0.qw[J].x, w1 = u ? r1.qw[J].y : r1.qw[J].x;
+        a[u][0] = lop3_and_or(w0 >> (4 * h), 0x000F000Fu, 0x64006400u);
+        a[u][1] = lop3_and_or(w1 >> (4 * h), 0x000F000Fu, 0x64006400u);
+        a[u][2] = lop3_and_or(w0 >> (8 + 4 * h), 0x000F000Fu, 0x64006400u);
+        a[u][3] = lop3_and_or(w1 >> (8 + 4 * h), 0x000F000Fu, 0x64006400u);
+      }
+      const int src = qbase + (sb >> 1);
+      const float A0 = __shfl_sync(0xffffffffu, r0.A[sb & 1], src);
+      const float C0 = __shfl_sync(0xffffffffu, r0.C[sb & 1], src);
+      const float A1 = __shfl_sync(0xffffffffu, r1.A[sb & 1], src);
+      const float C1 = __shfl_sync(0xffffffffu, r1.C[sb & 1], src);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const uint4 b = __ldg(reinterpret_cast<const uint4*>(xrow + tok_off[n] + 64 * J + 32 * h));
+        float D[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_16816(D, a[0], b.x, b.y);
+        mma_16816(D, a[1], b.z, b.w);
+        const float X0 = __ldg(xs_blk + xs_off[n][0] + sb), X1 = __ldg(xs_blk + xs_off[n][1] + sb);
+        acc[n][0] = fmaf(A0, D[0], fmaf(-C0, X0, acc[n][0]));
+        acc[n][1] = fmaf(A0, D[1], fmaf(-C0, X1, acc[n][1]));
+        acc[n][2] = fmaf(A1, D[2], fmaf(-C1, X0, acc[n][2]));
+        acc[n][3] = fmaf(A1, D[3], fmaf(-C1, X1, acc[n][3]));
+      }
+    }
+}
+
 // Blocks in flight per warp (register ring depth).  Deeper rings cost
 // occupancy and measured slower.
 constexpr int kKqDepth = 2;
@@ -290,7 +350,8 @@ constexpr int kKqDepth = 2;
 // `split` warps share a tile (each a contiguous range of blocks).
 template <int TYPE, int NT>
 __global__ void __launch_bounds__(kKqWarps * 32, (NT == 1 && TYPE == kKqQ2) ? 3 : 2) kquant_gemv_kernel(const uint8_t* __restrict__ w,
-                                                                   const uint16_t* __restrict__ xp, int T, int N,
+                                                                   const uint16_t* __restrict__ xp,
+                                                                   const float* __restrict__ xs, int T, int N,
                                                                    int K, int split, float* __restrict__ y) {
   constexpr int BB = kq_block_bytes(TYPE);
   __shared__ float red[kKqWarps][32][NT * 4];
@@ -316,6 +377,13 @@ __global__ void __launch_bounds__(kKqWarps * 32, (NT == 1 && TYPE == kKqQ2) ? 3 
     size_t tok_off[NT];
 #pragma unroll
     for (int n = 0; n < NT; ++n) tok_off[n] = (size_t)(8 * n + g < T ? 8 * n + g : T) * tok_stride;
+    // Q4_K sub-block sums of the accumulator's tokens 8n + 2c, 8n + 2c + 1
+    // (rows past T hold zeros)
+    size_t xs_off[NT][2];
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) xs_off[n][i] = (size_t)(8 * n + 2 * c + i) * (size_t)(K >> 5);
     // ring of D blocks in flight per warp: the load of block kb + D is issued
     // as soon as block kb has been consumed
     constexpr int D = kKqDepth;
@@ -330,7 +398,11 @@ __global__ void __launch_bounds__(kKqWarps * 32, (NT == 1 && TYPE == kKqQ2) ? 3 
 #pragma unroll
       for (int i = 0; i < D; ++i) {
         if (kb + i < kb1) {
-          kq_block_mma<TYPE, NT>(b0[i], b1[i], c, xl + (size_t)(kb + i) * 256, tok_off, acc);
+          if constexpr (TYPE == kKqQ4)
+            kq_block_q4<NT>(b0[i], b1[i], c, xl + (size_t)(kb + i) * 256, tok_off, xs + (size_t)(kb + i) * 8, xs_off,
+                            acc);
+          else
+            kq_block_mma<TYPE, NT>(b0[i], b1[i], c, xl + (size_t)(kb + i) * 256, tok_off, acc);
           if (kb + i + D < kb1) {
             b0[i].load(row0 + (size_t)(kb + i + D) * BB, c);
             b1[i].load(row1 + (size_t)(kb + i + D) * BB, c);
@@ -414,14 +486,14 @@ __global__ void kquant_dequant_kernel(const uint8_t* __restrict__ blocks, long l
 }
 
 template <int TYPE>
-cudaError_t launch_kquant_gemv_t(const uint8_t* w, const uint16_t* xp, int T, int N, int K, int split, float* y,
-                                 cudaStream_t st) {
+cudaError_t launch_kquant_gemv_t(const uint8_t* w, const uint16_t* xp, const float* xs, int T, int N, int K,
+                                 int split, float* y, cudaStream_t st) {
   const int n_tiles = N >> 4, tiles_per_cta = kKqWarps / split;
   const int grid = (n_tiles + tiles_per_cta - 1) / tiles_per_cta;
   const int nt = (T + 7) / 8;
-  if (nt == 1) kquant_gemv_kernel<TYPE, 1><<<grid, kKqWarps * 32, 0, st>>>(w, xp, T, N, K, split, y);
-  else if (nt == 2) kquant_gemv_kernel<TYPE, 2><<<grid, kKqWarps * 32, 0, st>>>(w, xp, T, N, K, split, y);
-  else kquant_gemv_kernel<TYPE, 4><<<grid, kKqWarps * 32, 0, st>>>(w, xp, T, N, K, split, y);
+  if (nt == 1) kquant_gemv_kernel<TYPE, 1><<<grid, kKqWarps * 32, 0, st>>>(w, xp, xs, T, N, K, split, y);
+  else if (nt == 2) kquant_gemv_kernel<TYPE, 2><<<grid, kKqWarps * 32, 0, st>>>(w, xp, xs, T, N, K, split, y);
+  else kquant_gemv_kernel<TYPE, 4><<<grid, kKqWarps * 32, 0, st>>>(w, xp, xs, T, N, K, split, y);
   return cudaGetLastError();
 }
 
@@ -474,7 +546,8 @@ ef_status ef_kquant_dequantize(int type, const void* blocks, long long n_blocks,
 size_t ef_kquant_matmul_workspace_size(int T, int K) {
   if (T < 0 || K < 0) return 0;
   const int nt = (T + 7) / 8;
-  return (size_t)(nt <= 2 ? nt : 4) * 8 * K * 2 + 256;  // token groups the kernel reads: 1, 2 or 4
+  const size_t rows = (size_t)(nt <= 2 ? nt : 4) * 8;  // token groups the kernel reads: 1, 2 or 4
+  return (rows * K * 2 + 255) / 256 * 256 + rows * (K / 32) * 4 + 256;  // permuted rows, Q4_K sub-block sums
 }
 
 ef_status ef_kquant_matmul(const void* x, int act_dtype, int T, const void* blocks, int type, int N, int K, float* y,
@@ -494,20 +567,21 @@ ef_status ef_kquant_matmul(const void* x, int act_dtype, int T, const void* bloc
   const int nt = (T + 7) / 8;
   const int n_tok_k = (nt <= 2 ? nt : 4) * 8;  // token rows the kernel reads (zero beyond T)
   uint16_t* xp = static_cast<uint16_t*>(workspace);
+  float* xsum = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((size_t)n_tok_k * K * 2 + 255) / 256 * 256);
   const int n_sm = sm_count();
   const int pgrid = (int)std::min<long long>(((long long)n_tok_k * K + 255) / 256, (long long)n_sm * 16);
   const uint16_t* xs = static_cast<const uint16_t*>(x);
   const int bf = act_dtype == EF_DT_BF16;
-  if (type == ef::kKqQ2) ef::kquant_prep_kernel<ef::kKqQ2><<<pgrid, 256, 0, st>>>(xs, bf, T, K, n_tok_k, xp);
-  else if (type == ef::kKqQ3) ef::kquant_prep_kernel<ef::kKqQ3><<<pgrid, 256, 0, st>>>(xs, bf, T, K, n_tok_k, xp);
-  else ef::kquant_prep_kernel<ef::kKqQ4><<<pgrid, 256, 0, st>>>(xs, bf, T, K, n_tok_k, xp);
+  if (type == ef::kKqQ2) ef::kquant_prep_kernel<ef::kKqQ2><<<pgrid, 256, 0, st>>>(xs, bf, T, K, n_tok_k, xp, xsum);
+  else if (type == ef::kKqQ3) ef::kquant_prep_kernel<ef::kKqQ3><<<pgrid, 256, 0, st>>>(xs, bf, T, K, n_tok_k, xp, xsum);
+  else ef::kquant_prep_kernel<ef::kKqQ4><<<pgrid, 256, 0, st>>>(xs, bf, T, K, n_tok_k, xp, xsum);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(EF_ERR_CUDA, "kquant_prep: %s", cudaGetErrorString(e));
   const int split = kq_split(N, K, n_sm);
   const uint8_t* w = static_cast<const uint8_t*>(blocks);
-  if (type == ef::kKqQ2) e = ef::launch_kquant_gemv_t<ef::kKqQ2>(w, xp, T, N, K, split, y, st);
-  else if (type == ef::kKqQ3) e = ef::launch_kquant_gemv_t<ef::kKqQ3>(w, xp, T, N, K, split, y, st);
-  else e = ef::launch_kquant_gemv_t<ef::kKqQ4>(w, xp, T, N, K, split, y, st);
+  if (type == ef::kKqQ2) e = ef::launch_kquant_gemv_t<ef::kKqQ2>(w, xp, xsum, T, N, K, split, y, st);
+  else if (type == ef::kKqQ3) e = ef::launch_kquant_gemv_t<ef::kKqQ3>(w, xp, xsum, T, N, K, split, y, st);
+  else e = ef::launch_kquant_gemv_t<ef::kKqQ4>(w, xp, xsum, T, N, K, split, y, st);
   if (e != cudaSuccess) return fail(EF_ERR_CUDA, "kquant_gemv: %s", cudaGetErrorString(e));
   return EF_OK;
 }

@@ -21,9 +21,12 @@ namespace ef {
 // out[r][K] fp16 in the K-quant GEMV's permuted order for TYPE (see
 // kquant_prep_kernel) = in[row_src[r]] (or in[r]); in: bf16 / fp16 / fp32 rows
 // of K values (in_dtype EF_DT_*).  n_dev (or null): row count on the device.
+// Q4_K also the sums of each 32-element sub-block of the rounded values, xs
+// fp32 [n][K / 32], in element order.
 template <int TYPE>
 __global__ void kq_rows_prep_kernel(const void* __restrict__ in, int in_dtype, const int* __restrict__ row_src,
-                                    int n, const int* __restrict__ n_dev, int K, uint16_t* __restrict__ out) {
+                                    int n, const int* __restrict__ n_dev, int K, uint16_t* __restrict__ out,
+                                    float* __restrict__ xs) {
   pdl_wait();
   if (n_dev) n = min(n, max(0, *n_dev));
   const long long total = (long long)n * K;
@@ -43,6 +46,23 @@ __global__ void kq_rows_prep_kernel(const void* __restrict__ in, int in_dtype, c
     if (!(fabsf(v) <= 65504.0f)) ef_set_error(kDevErrRange);
     out[i] = f32_to_h16_sat(v);
   }
+  if (TYPE == kKqQ4) {
+    const int nsb = K >> 5;
+    const long long tsum = (long long)n * nsb;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < tsum;
+         i += (long long)gridDim.x * blockDim.x) {
+      const int r = (int)(i / nsb), sb = (int)(i % nsb);
+      const long long sr = row_src ? __ldg(row_src + r) : r;
+      float sum = 0.0f;
+      for (int e = 0; e < 32; ++e) {
+        const size_t o = (size_t)sr * K + 32 * sb + e;
+        const float v = in_dtype == 2 ? static_cast<const float*>(in)[o]
+                                      : act_to_f32(static_cast<const uint16_t*>(in)[o], in_dtype == 0);
+        sum += h16_to_f32(f32_to_h16_sat(v));
+      }
+      xs[i] = sum;
+    }
+  }
 }
 
 struct KqMoeParams {
@@ -53,6 +73,7 @@ struct KqMoeParams {
   const uint8_t* sw0;  // the shared expert's matrices (expert id == n_experts)
   const uint8_t* sw1;
   const uint16_t* xp;  // permuted fp16 activation rows [n_rows][K]
+  const float* xs;     // Q4_K: their sub-block sums [n_rows][K / 32]
   const int* seg_expert;
   const int* seg_row0;
   const int* seg_nrows;
@@ -88,6 +109,9 @@ __global__ void __launch_bounds__(kKqWarps * 32, MODE == 0 ? 1 : 2) kq_moe_kerne
     // lane g's token column: a row of the segment (rows past its end repeat
     // the last one; their outputs are not stored)
     const size_t tok_off[1] = {(size_t)(row0 + min(g, nrows - 1)) * p.K};
+    // Q4_K sub-block sums of the accumulator's tokens 2c, 2c + 1 (the same repeat)
+    const size_t xs_off[1][2] = {{(size_t)(row0 + min(2 * c, nrows - 1)) * (size_t)(p.K >> 5),
+                                  (size_t)(row0 + min(2 * c + 1, nrows - 1)) * (size_t)(p.K >> 5)}};
     const uint16_t* xl = p.xp + 8 * c;
     float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
     float accu[1][4] = {{0.f, 0.f, 0.f, 0.f}};
@@ -100,12 +124,18 @@ __global__ void __launch_bounds__(kKqWarps * 32, MODE == 0 ? 1 : 2) kq_moe_kerne
         na.load(g0 + (size_t)(kb + 1) * BB, c);
         nbr.load(g1 + (size_t)(kb + 1) * BB, c);
       }
-      kq_block_mma<TYPE, 1>(ra, rb, c, xl + (size_t)kb * 256, tok_off, acc);
+      if constexpr (TYPE == kKqQ4)
+        kq_block_q4<1>(ra, rb, c, xl + (size_t)kb * 256, tok_off, p.xs + (size_t)kb * 8, xs_off, acc);
+      else
+        kq_block_mma<TYPE, 1>(ra, rb, c, xl + (size_t)kb * 256, tok_off, acc);
       if (MODE == 0) {
         KqRow<TYPE> ua, ub;
         ua.load(u0 + (size_t)kb * BB, c);
         ub.load(u1 + (size_t)kb * BB, c);
-        kq_block_mma<TYPE, 1>(ua, ub, c, xl + (size_t)kb * 256, tok_off, accu);
+        if constexpr (TYPE == kKqQ4)
+          kq_block_q4<1>(ua, ub, c, xl + (size_t)kb * 256, tok_off, p.xs + (size_t)kb * 8, xs_off, accu);
+        else
+          kq_block_mma<TYPE, 1>(ua, ub, c, xl + (size_t)kb * 256, tok_off, accu);
       }
       if (kb + 1 < nb) {
         ra = na;
@@ -128,18 +158,18 @@ __global__ void __launch_bounds__(kKqWarps * 32, MODE == 0 ? 1 : 2) kq_moe_kerne
 
 template <int TYPE>
 cudaError_t launch_kq_rows_prep_t(const void* in, int in_dtype, const int* row_src, int n, const int* n_dev, int K,
-                                  uint16_t* out, int n_sm, cudaStream_t st) {
+                                  uint16_t* out, float* xs, int n_sm, cudaStream_t st) {
   const long long total = (long long)n * K;
   if (total == 0) return cudaSuccess;
   const int grid = (int)std::min<long long>((total + 255) / 256, (long long)n_sm * 16);
-  return launch_pdl(kq_rows_prep_kernel<TYPE>, grid, 256, 0, st, in, in_dtype, row_src, n, n_dev, K, out);
+  return launch_pdl(kq_rows_prep_kernel<TYPE>, grid, 256, 0, st, in, in_dtype, row_src, n, n_dev, K, out, xs);
 }
 
 cudaError_t launch_kq_rows_prep(int type, const void* in, int in_dtype, const int* row_src, int n, const int* n_dev,
-                                int K, uint16_t* out, int n_sm, cudaStream_t st) {
-  if (type == kKqQ2) return launch_kq_rows_prep_t<kKqQ2>(in, in_dtype, row_src, n, n_dev, K, out, n_sm, st);
-  if (type == kKqQ3) return launch_kq_rows_prep_t<kKqQ3>(in, in_dtype, row_src, n, n_dev, K, out, n_sm, st);
-  return launch_kq_rows_prep_t<kKqQ4>(in, in_dtype, row_src, n, n_dev, K, out, n_sm, st);
+                                int K, uint16_t* out, float* xs, int n_sm, cudaStream_t st) {
+  if (type == kKqQ2) return launch_kq_rows_prep_t<kKqQ2>(in, in_dtype, row_src, n, n_dev, K, out, xs, n_sm, st);
+  if (type == kKqQ3) return launch_kq_rows_prep_t<kKqQ3>(in, in_dtype, row_src, n, n_dev, K, out, xs, n_sm, st);
+  return launch_kq_rows_prep_t<kKqQ4>(in, in_dtype, row_src, n, n_dev, K, out, xs, n_sm, st);
 }
 
 // Grid: enough CTAs for the item count of the worst case (rows / 8 segments
@@ -166,8 +196,10 @@ struct KqWs {
   float* wts;
   PermBufs pb;
   uint16_t* xp;   // routed rows, permuted for the gate / up type [n_rows][H]
+  float* xs;      // Q4_K gate / up: their sub-block sums [n_rows][H / 32]
   float* h;       // [n_rows][I]
   uint16_t* hp;   // h permuted for the down type [n_rows][I]
+  float* hs;      // Q4_K down: its sub-block sums [n_rows][I / 32]
   float* yrows;   // [n_rows][H]
 };
 
@@ -187,8 +219,10 @@ size_t kq_ws(const ef_moe_cfg* cfg, int T, Carver& c, KqWs& w) {
   w.pb.seg_nrows = c.take<int>(max_segs);
   w.pb.n_seg = c.take<int>(1);
   w.xp = c.take<uint16_t>((size_t)n_rows * H);
+  w.xs = c.take<float>((size_t)n_rows * (H / 32));
   w.h = c.take<float>((size_t)n_rows * I);
   w.hp = c.take<uint16_t>((size_t)n_rows * I);
+  w.hs = c.take<float>((size_t)n_rows * (I / 32));
   w.yrows = c.take<float>((size_t)n_rows * H);
   return c.off;
 }
@@ -270,7 +304,7 @@ ef_status ef_kquant_moe_forward(const ef_moe_cfg* cfg, const void* x, int T, con
                                                   inds, wts, st));
   EF_LAUNCH("permute", launch_permute(inds, T * k, k, E, n_sh, kTokChunk, w.pb, st));
   EF_LAUNCH("kq_prep_x", launch_kq_rows_prep(gate.type, x, bf ? EF_DT_BF16 : EF_DT_F16, w.pb.row_src, n_rows,
-                                             nullptr, H, w.xp, nsm, st));
+                                             nullptr, H, w.xp, w.xs, nsm, st));
   const int max_items_gu = ((n_rows + kTokChunk - 1) / kTokChunk + E + 1) * (I / 16);
   KqMoeParams p0;
   memset(&p0, 0, sizeof(p0));
@@ -281,10 +315,11 @@ ef_status ef_kquant_moe_forward(const ef_moe_cfg* cfg, const void* x, int T, con
   p0.sw0 = sg ? static_cast<const uint8_t*>(sg->blocks) : p0.w0;
   p0.sw1 = su ? static_cast<const uint8_t*>(su->blocks) : p0.w1;
   p0.xp = w.xp;
+  p0.xs = w.xs;
   p0.seg_expert = w.pb.seg_expert; p0.seg_row0 = w.pb.seg_row0; p0.seg_nrows = w.pb.seg_nrows; p0.n_seg = w.pb.n_seg;
   p0.K = H; p0.R = I; p0.n_experts = E; p0.out = w.h;
   EF_LAUNCH("kq_gate_up", launch_kq_moe(gate.type, 0, p0, max_items_gu, nsm, st));
-  EF_LAUNCH("kq_prep_h", launch_kq_rows_prep(down.type, w.h, EF_DT_F32, nullptr, n_rows, nullptr, I, w.hp, nsm, st));
+  EF_LAUNCH("kq_prep_h", launch_kq_rows_prep(down.type, w.h, EF_DT_F32, nullptr, n_rows, nullptr, I, w.hp, w.hs, nsm, st));
   KqMoeParams p1 = p0;
   p1.w0 = static_cast<const uint8_t*>(down.blocks);
   p1.w1 = nullptr;
@@ -293,6 +328,7 @@ ef_status ef_kquant_moe_forward(const ef_moe_cfg* cfg, const void* x, int T, con
   p1.sw0 = sd ? static_cast<const uint8_t*>(sd->blocks) : p1.w0;
   p1.sw1 = nullptr;
   p1.xp = w.hp;
+  p1.xs = w.hs;
   p1.K = I; p1.R = H; p1.out = w.yrows;
   const int max_items_d = ((n_rows + kTokChunk - 1) / kTokChunk + E + 1) * (H / 16);
   EF_LAUNCH("kq_down", launch_kq_moe(down.type, 1, p1, max_items_d, nsm, st));

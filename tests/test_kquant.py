@@ -11,7 +11,8 @@ reader's error behaviour follows the reference's parser tests
 (tests/test_gguf_loader.py:94-136).
 GPU: ef_kquant_dequantize is bit-exact with the reference; ef_kquant_matmul
 is within the fp tolerance of the oracle over every format, token count and
-both activation dtypes.
+both activation dtypes (Q4_K within the bound of the reference's fp16 rounding
+of each weight, since its GEMV contracts the exact weights).
 """
 import hashlib
 import importlib.util
@@ -185,11 +186,26 @@ def test_gpu_dequantize_model_experts(K, Z, tmp_path):
         assert hashlib.sha256(got.tobytes()).hexdigest() == deq_sha, (layer, e, proj)
 
 
-def _check_close(y, ref):
+def _check_close(y, ref, bound=None):
+    """Within 2e-2 absolute (or, with `bound`, within it elementwise) and 1e-3
+    relative L2 of the oracle."""
     y = np.asarray(y, np.float64)
     err = np.abs(y - ref)
     rel_l2 = np.linalg.norm(y - ref) / max(np.linalg.norm(ref), 1e-30)
-    assert err.max() <= 2e-2 and rel_l2 <= 1e-3, (float(err.max()), float(rel_l2))
+    ok = (err <= bound).all() if bound is not None else err.max() <= 2e-2
+    assert ok and rel_l2 <= 1e-3, (float(err.max()), float(rel_l2))
+
+
+def _q4_bound(x, raw, dtype, N, K):
+    """Q4_K: the kernel contracts the exact weights A q - B (codes on the tensor
+    cores, scale and min folded in fp32), the oracle the reference's fp16
+    weights RN16(A q - B); they differ by at most half an fp16 ulp per weight,
+    2^-11 |w|, so |y - ref| <= 2^-10 sum |x| |w| (twice that, for the fp32
+    accumulation) + 1e-5.  Other formats: None (the 2e-2 bar)."""
+    if dtype != G.GGML_TYPE_Q4_K:
+        return None
+    w = np.abs(O.np_dequant_kquant(raw, dtype).astype(np.float64).reshape(N, K))
+    return 2.0 ** -10 * (np.abs(np.asarray(x, np.float64)) @ w.T) + 1e-5
 
 
 @pytest.mark.gpu
@@ -204,9 +220,10 @@ def test_gpu_matmul_matches_oracle(K, dtype, T):
         x = rng.standard_normal((T, Kd)).astype(np.float32)
         for act in (torch.bfloat16, torch.float16):
             xt = torch.from_numpy(x).to(act).cuda()
-            ref = O.np_kquant_matmul(xt.float().cpu().numpy(), raw, dtype, N, Kd)
+            xf = xt.float().cpu().numpy()
+            ref = O.np_kquant_matmul(xf, raw, dtype, N, Kd)
             y = K.matmul(xt, torch.from_numpy(np.frombuffer(raw, np.uint8).copy()).cuda(), dtype, N, Kd)
-            _check_close(y.cpu().numpy(), ref)
+            _check_close(y.cpu().numpy(), ref, _q4_bound(xf, raw, dtype, N, Kd))
     from expertflow_b200.moe import device_error
     assert device_error() == 0
 
@@ -223,7 +240,8 @@ def test_gpu_matmul_large_and_deterministic(K):
     x = torch.from_numpy(rng.standard_normal((4, Kd)).astype(np.float32)).to(torch.bfloat16).cuda()
     y1, y2 = K.matmul(x, w, dtype, N, Kd), K.matmul(x, w, dtype, N, Kd)
     assert torch.equal(y1, y2)
-    _check_close(y1.cpu().numpy(), O.np_kquant_matmul(x.float().cpu().numpy(), raw, dtype, N, Kd))
+    xf = x.float().cpu().numpy()
+    _check_close(y1.cpu().numpy(), O.np_kquant_matmul(xf, raw, dtype, N, Kd), _q4_bound(xf, raw, dtype, N, Kd))
 
 
 @pytest.mark.gpu
