@@ -439,6 +439,125 @@ __global__ void __launch_bounds__(kKqWarps * 32, (NT == 1 && TYPE == kKqQ2) ? 3 
     }
 }
 
+// Q4_K GEMV fed through shared memory: each warp streams its tile's 16 rows
+// through a private ring of kKq4Stages stages of kKq4SB blocks per row (one
+// bulk copy per row per stage, completion on the stage's mbarrier), so a warp
+// has up to kKq4Stages * 16 * kKq4SB * 144 bytes in flight and its lanes read
+// the staged words from shared memory (two CTAs per SM).  Same tiles, split
+// and reduction as kquant_gemv_kernel; every wait is bounded and after a
+// failed one the warp waits (bounded) for the copies it has issued.
+constexpr int kKq4Stages = 2;
+constexpr int kKq4SB = 2;
+constexpr int kKq4RowBytes = kKq4SB * 144;               // one row's share of a stage
+constexpr int kKq4StageBytes = 16 * kKq4RowBytes;         // a stage of the warp's 16 rows
+constexpr int kKq4WarpBytes = kKq4Stages * kKq4StageBytes;
+
+template <int NT>
+__global__ void __launch_bounds__(kKqWarps * 32, 2) kq4_bulk_gemv_kernel(const uint8_t* __restrict__ w,
+                                                                         const uint16_t* __restrict__ xp,
+                                                                         const float* __restrict__ xs, int T, int N,
+                                                                         int K, int split, float* __restrict__ y) {
+  extern __shared__ __align__(128) uint8_t kq4_smem[];
+  __shared__ __align__(8) uint64_t bars[kKqWarps][kKq4Stages];
+  __shared__ float red[kKqWarps][32][NT * 4];
+  constexpr int BB = 144;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int tiles_per_cta = kKqWarps / split;
+  const int tile = blockIdx.x * tiles_per_cta + warp / split;
+  const int part = warp % split;
+  const int nb = K >> 8;
+  const int n_tiles = N >> 4;
+  float acc[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+  if (tile < n_tiles) {
+    const int kb0 = (int)((long long)nb * part / split), kb1 = (int)((long long)nb * (part + 1) / split);
+    const size_t row_bytes = (size_t)nb * BB;
+    const uint8_t* rows = w + (size_t)(16 * tile) * row_bytes;  // the tile's first row
+    uint8_t* ring = kq4_smem + (size_t)warp * kKq4WarpBytes;
+    uint64_t* bar = bars[warp];
+    if (lane == 0) {
+      for (int i = 0; i < kKq4Stages; ++i) mbar_init(&bar[i], 1);
+      mbar_fence_init();
+    }
+    __syncwarp();
+    // stage st covers blocks [kb0 + st * SB, + SB) of every row
+    const int n_st = (kb1 - kb0 + kKq4SB - 1) / kKq4SB;
+    auto issue = [&](int st) {
+      const int kb = kb0 + st * kKq4SB, nblk = min(kKq4SB, kb1 - kb);
+      uint64_t* b = &bar[st % kKq4Stages];
+      uint8_t* dst = ring + (size_t)(st % kKq4Stages) * kKq4StageBytes;
+      mbar_arrive_expect_tx(b, (uint32_t)(16 * nblk * BB));
+      for (int r = 0; r < 16; ++r)
+        bulk_load(dst + r * kKq4RowBytes, rows + (size_t)r * row_bytes + (size_t)kb * BB, (uint32_t)(nblk * BB), b);
+    };
+    if (lane == 0)
+      for (int st = 0; st < min(kKq4Stages, n_st); ++st) issue(st);
+    const uint16_t* xl = xp + 8 * c;
+    size_t tok_off[NT];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) tok_off[n] = (size_t)(8 * n + g < T ? 8 * n + g : T) * (size_t)K;
+    size_t xs_off[NT][2];
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) xs_off[n][i] = (size_t)(8 * n + 2 * c + i) * (size_t)(K >> 5);
+    int st = 0;
+    bool ok = true;
+    for (; st < n_st; ++st) {
+      if (!mbar_wait(&bar[st % kKq4Stages], (uint32_t)(st / kKq4Stages) & 1u, kDevErrTimeoutFull)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* stage = ring + (size_t)(st % kKq4Stages) * kKq4StageBytes;
+      const int kb = kb0 + st * kKq4SB, nblk = min(kKq4SB, kb1 - kb);
+#pragma unroll
+      for (int i = 0; i < kKq4SB; ++i) {
+        if (i < nblk) {
+          KqRow<kKqQ4> r0, r1;
+          r0.load_shared(stage + g * kKq4RowBytes + i * BB, c);
+          r1.load_shared(stage + (g + 8) * kKq4RowBytes + i * BB, c);
+          kq_block_q4<NT>(r0, r1, c, xl + (size_t)(kb + i) * 256, tok_off, xs + (size_t)(kb + i) * 8, xs_off, acc);
+        }
+      }
+      __syncwarp();
+      if (lane == 0 && st + kKq4Stages < n_st) {
+        fence_proxy_async();  // this stage's shared-memory reads before the copy that overwrites it
+        issue(st + kKq4Stages);
+      }
+    }
+    if (!ok && lane == 0)  // stages issued but not consumed: wait (bounded) for their copies before leaving
+      for (int d = st; d < min(n_st, st + kKq4Stages); ++d)
+        mbar_wait(&bar[d % kKq4Stages], (uint32_t)(d / kKq4Stages) & 1u, kDevErrTimeoutFull);
+  }
+  if (split > 1) {
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) red[warp][lane][4 * n + i] = acc[n][i];
+    __syncthreads();
+    if (part != 0) return;
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float sum = 0.0f;
+        for (int q = 0; q < split; ++q) sum += red[warp + q][lane][4 * n + i];
+        acc[n][i] = sum;
+      }
+  }
+  if (tile >= n_tiles) return;
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int tok = 8 * n + 2 * c + (i & 1);
+      const int row = 16 * tile + g + ((i & 2) ? 8 : 0);
+      if (tok < T) y[(size_t)tok * N + row] = acc[n][i];
+    }
+}
+
 // fp16 out[n_blocks * 256]: the reference's decode, one thread per 16 elements.
 template <int TYPE>
 __global__ void kquant_dequant_kernel(const uint8_t* __restrict__ blocks, long long n_blocks,
@@ -491,6 +610,23 @@ cudaError_t launch_kquant_gemv_t(const uint8_t* w, const uint16_t* xp, const flo
   const int n_tiles = N >> 4, tiles_per_cta = kKqWarps / split;
   const int grid = (n_tiles + tiles_per_cta - 1) / tiles_per_cta;
   const int nt = (T + 7) / 8;
+  if constexpr (TYPE == kKqQ4) {
+    // up to 16 tokens through shared memory; 17..32 (four token groups) in
+    // registers (the shared-memory kernel spills there and measured slower)
+    if (nt <= 2) {
+      constexpr int smem = kKqWarps * kKq4WarpBytes;
+      static std::atomic<bool> a1[64], a2[64];
+      cudaError_t e;
+      if (nt == 1) {
+        if ((e = set_max_smem_once(kq4_bulk_gemv_kernel<1>, smem, a1))) return e;
+        kq4_bulk_gemv_kernel<1><<<grid, kKqWarps * 32, smem, st>>>(w, xp, xs, T, N, K, split, y);
+      } else {
+        if ((e = set_max_smem_once(kq4_bulk_gemv_kernel<2>, smem, a2))) return e;
+        kq4_bulk_gemv_kernel<2><<<grid, kKqWarps * 32, smem, st>>>(w, xp, xs, T, N, K, split, y);
+      }
+      return cudaGetLastError();
+    }
+  }
   if (nt == 1) kquant_gemv_kernel<TYPE, 1><<<grid, kKqWarps * 32, 0, st>>>(w, xp, xs, T, N, K, split, y);
   else if (nt == 2) kquant_gemv_kernel<TYPE, 2><<<grid, kKqWarps * 32, 0, st>>>(w, xp, xs, T, N, K, split, y);
   else kquant_gemv_kernel<TYPE, 4><<<grid, kKqWarps * 32, 0, st>>>(w, xp, xs, T, N, K, split, y);
@@ -507,6 +643,16 @@ int kq_split(int N, int K, int n_sm) {
   const int n_tiles = N >> 4, nb = K >> 8;
   int split = 1;
   while (split < ef::kKqWarps && (long long)n_tiles * split < 96LL * n_sm && split * 2 <= nb) split *= 2;
+  return split;
+}
+
+// Q4_K up to 16 tokens (shared-memory kernel, two CTAs of kKqWarps warps per
+// SM): warps share a tile only while the tiles give fewer than one wave of
+// resident warps, so each warp streams long row ranges through its ring.
+int kq4_split(int N, int K, int n_sm) {
+  const int n_tiles = N >> 4, nb = K >> 8;
+  int split = 1;
+  while (split < ef::kKqWarps && (long long)n_tiles * split < 2LL * ef::kKqWarps * n_sm && split * 2 <= nb) split *= 2;
   return split;
 }
 
@@ -577,7 +723,7 @@ ef_status ef_kquant_matmul(const void* x, int act_dtype, int T, const void* bloc
   else ef::kquant_prep_kernel<ef::kKqQ4><<<pgrid, 256, 0, st>>>(xs, bf, T, K, n_tok_k, xp, xsum);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(EF_ERR_CUDA, "kquant_prep: %s", cudaGetErrorString(e));
-  const int split = kq_split(N, K, n_sm);
+  const int split = type == ef::kKqQ4 && T <= 16 ? kq4_split(N, K, n_sm) : kq_split(N, K, n_sm);
   const uint8_t* w = static_cast<const uint8_t*>(blocks);
   if (type == ef::kKqQ2) e = ef::launch_kquant_gemv_t<ef::kKqQ2>(w, xp, xsum, T, N, K, split, y, st);
   else if (type == ef::kKqQ3) e = ef::launch_kquant_gemv_t<ef::kKqQ3>(w, xp, xsum, T, N, K, split, y, st);
