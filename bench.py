@@ -522,10 +522,10 @@ def stream_from_files(spec, host, gates, run, steps, budget, ms_res, args):
             store = P.ExpertStore.from_safetensors(root, spec=spec)
         host_blobs = max(2 * spec.top_k, int(args.stream_host_frac * NL * E))
         pl = P.ExpertSlotPool.from_store(store, budget=budget, host_blobs=host_blobs, headroom=spec.top_k)
-        run(pl, True, min(16, steps))
+        run(pl, 2, min(16, steps))  # file reads and copies two layers ahead
         pl.reset_stats()
         f0 = store.info()["file_bytes"]
-        ms = run(pl, True, steps)
+        ms = run(pl, 2, steps)
         st = pl.stats()
         fb = store.info()["file_bytes"] - f0
         info = store.info()
@@ -533,7 +533,7 @@ def stream_from_files(spec, host, gates, run, steps, budget, ms_res, args):
         store.close()
         asked = st["host_hits"] + st["host_reads"]
         return {"tokens_per_s": round(steps / (ms * 1e-3), 2), "ms_per_token": round(ms / steps, 4),
-                "direct_io": bool(info["direct"]), "readers": info["n_readers"],
+                "lookahead_layers": 2, "direct_io": bool(info["direct"]), "readers": info["n_readers"],
                 "host_blobs": host_blobs, "host_frac": args.stream_host_frac,
                 "model_bytes_on_disk": int(sum(os.path.getsize(os.path.join(root, n)) for n in os.listdir(root))),
                 "write_s": round(write_s, 1),
