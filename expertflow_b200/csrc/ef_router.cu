@@ -184,6 +184,8 @@ constexpr int kSelWarps = 4;
 // One warp per token.  Scores live in shared memory (E <= 512).  blockIdx.y = 1
 // and 2 select the second and third gate's logits / bias / outputs (see
 // router_logits_kernel).
+// PER: score keys per lane (E <= 32 PER); the picks do not depend on it.
+template <int PER>
 __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const float* __restrict__ logits,
                                                                        const float* __restrict__ e_bias, int T,
                                                                        SelCfg cfg, int* __restrict__ inds,
@@ -238,6 +240,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const flo
     const int G = cfg.n_group, gsz = E / G;
     if (lane < G) {
       float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll 8
       for (int e = lane * gsz; e < (lane + 1) * gsz; ++e) {
         float v = sc[e];
         if (v > m1) { m2 = m1; m1 = v; }
@@ -264,7 +267,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) router_select_kernel(const flo
   // elements e = lane + 32 r, a taken element's key drops to 0.  Lane j < k
   // keeps the j-th pick (no per-thread arrays indexed by j: they would live
   // in local memory).
-  constexpr int kPerLane = kMaxE / 32;
+  constexpr int kPerLane = PER;
   uint32_t keys[kPerLane];
 #pragma unroll
   for (int r = 0; r < kPerLane; ++r) keys[r] = lane + 32 * r < E ? order_key(sc[lane + 32 * r]) : 0u;
@@ -350,7 +353,13 @@ cudaError_t launch_router_select(const float* logits, const float* e_bias, int T
                                  float* wts2, const float* logits3, const float* e_bias3, int* inds3, float* wts3) {
   SelCfg c{E, k, mode, norm_topk, n_group, topk_group, scaling};
   dim3 grid((T + kSelWarps - 1) / kSelWarps, logits2 ? (logits3 ? 3 : 2) : 1);
-  return launch_pdl(router_select_kernel, grid, kSelWarps * 32, 0, st, logits, e_bias, T, c, inds, wts, logits2, e_bias2,
+  if (E <= 128)
+    return launch_pdl(router_select_kernel<4>, grid, kSelWarps * 32, 0, st, logits, e_bias, T, c, inds, wts, logits2,
+                      e_bias2, inds2, wts2, logits3, e_bias3, inds3, wts3);
+  if (E <= 256)
+    return launch_pdl(router_select_kernel<8>, grid, kSelWarps * 32, 0, st, logits, e_bias, T, c, inds, wts, logits2,
+                      e_bias2, inds2, wts2, logits3, e_bias3, inds3, wts3);
+  return launch_pdl(router_select_kernel<kMaxE / 32>, grid, kSelWarps * 32, 0, st, logits, e_bias, T, c, inds, wts, logits2, e_bias2,
                     inds2, wts2, logits3, e_bias3, inds3, wts3);
 }
 
