@@ -32,7 +32,7 @@ class MoESpec:
     n_shared: int = 0
     act_dtype: str = "bfloat16"      # activations x / y: "bfloat16" | "float16"
     gate_dtype: str = "float16"      # router weight
-    # synthetic-data distribution (BASELINE workloads)
+    # synthetic-data distribution of the benchmark workloads
     gate_std: float = 0.02
     e_bias_std: float = 0.0
     scale_std: float = 0.02
